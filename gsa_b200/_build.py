@@ -1,0 +1,87 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Compile the native libraries in-tree for B200 (sm_100a).
+
+``python -m gsa_b200._build`` writes ``gsa_b200/_native/gsa_bvh.so`` and
+``gsa_b200/_native/reference_queries.so`` (the two library names GSA's
+``gsa/_library.py`` loads), plus ``gsa_bvh_stack4.so``, a test variant whose
+traversal stack holds 4 entries so that the exact full-scan fallback path is
+exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
+intrinsics for every distance operation.
+"""
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+NATIVE = PKG / "_native"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = [
+    "-O3",
+    "--fmad=false",
+    "--ftz=false",
+    "-std=c++17",
+    "-lineinfo",
+    "-Xcompiler",
+    "-fPIC,-fvisibility=hidden",
+    "-shared",
+    "-I" + str(ROOT / "include"),
+]
+
+LIBS = {
+    "gsa_bvh": (["pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"], []),
+    "reference_queries": (["reference_queries.cu"], []),
+    "gsa_bvh_stack4": (
+        ["pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"],
+        ["-DGSA_STACK=4"],
+    ),
+}
+
+
+def nvcc():
+    path = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(path).exists():
+        raise RuntimeError("nvcc not found; the CUDA toolkit is required to build gsa_b200")
+    return path
+
+
+def _stale(out, sources):
+    if not out.exists():
+        return True
+    t = out.stat().st_mtime
+    deps = list(sources) + list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h"))
+    return any(p.stat().st_mtime > t for p in deps) or Path(__file__).stat().st_mtime > t
+
+
+def build(names=None, force=False, verbose=False, extra=()):
+    """Build the named libraries (default: all); returns their paths."""
+    NATIVE.mkdir(exist_ok=True)
+    out_paths = []
+    for name, (files, defs) in LIBS.items():
+        if names and name not in names:
+            continue
+        sources = [CSRC / f for f in files]
+        out = NATIVE / (name + ".so")
+        out_paths.append(out)
+        if not force and not _stale(out, sources):
+            continue
+        tmp = out.with_suffix(".so.tmp%d" % os.getpid())
+        cmd = [nvcc()] + ARCH + FLAGS + list(defs) + list(extra) + [str(s) for s in sources] + ["-o", str(tmp)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        os.replace(tmp, out)
+    return out_paths
+
+
+if __name__ == "__main__":
+    force = "--force" in sys.argv
+    extra = [a for a in sys.argv[1:] if a.startswith("-X") or a.startswith("--resource-usage")]
+    for p in build(force=force, verbose=True, extra=extra):
+        print("built", p)

@@ -1,0 +1,642 @@
+// SPDX-License-Identifier: Apache-2.0
+// Morton/LBVH forest builder with four prefix levels on one topology.
+//
+// Replaces the cuBQL spatial-median build + refit + prefix refit of GSA
+// (csrc/gsa_bvh.cu:217-248, 60-120).  Query results never depend on the tree
+// topology (ordered first-K radius and (d2, id) 3NN with conservative bounds),
+// so any valid hierarchy gives bit-identical answers; this one is built with
+// no host synchronisation:
+//   1. per-tree bounds of the finite points          (bounds_kernel)
+//   2. 63-bit Morton keys, local point index values  (morton_kernel)
+//   3. stable LSD radix sort, 8 passes of 8 bits, per tree
+//      (sort_upsweep / seg_scan / sort_scatter; all trees in one launch)
+//   4. Karras radix-tree topology on (key, index)    (karras_kernel)
+//   5. bottom-up refit: leaves = maximal subtrees of <= `leaf` points; points
+//      written to `pts` in leaf order and ascending ID inside a leaf; per
+//      level child entries (box of the finite members with ID < n/4^l, the
+//      subtree's minimum ID, child/leaf reference); children stored in
+//      ascending minimum-ID order                    (refit_kernel)
+//   6. per level, the IDs < n/4^l in leaf order, used as a spatially coherent
+//      query order for prefix queries               (qorder_* kernels)
+#include <algorithm>
+#include <new>
+#include "forest.cuh"
+#include "pool.cuh"
+
+namespace gsa {
+namespace {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortItems = 8;
+constexpr int kSortTile = kSortThreads * kSortItems;  // 2048 keys per block
+constexpr int kScanThreads = 1024;
+
+__device__ __forceinline__ unsigned float_key(float f) {
+  unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(unsigned k) {
+  unsigned u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+struct DescChunk {
+  TreeDesc d[256];
+  int first, count;
+};
+
+__global__ void upload_desc(TreeDesc* dst, DescChunk c, unsigned* bounds) {
+  int i = threadIdx.x;
+  if (i < c.count) {
+    dst[c.first + i] = c.d[i];
+    unsigned* b = bounds + 6 * (c.first + i);
+    b[0] = b[1] = b[2] = 0xffffffffu;  // min keys
+    b[3] = b[4] = b[5] = 0u;           // max keys
+  }
+}
+
+// Bounds over points whose three coordinates are finite (non-finite points
+// can never qualify: their squared distance is inf or NaN).
+__global__ void bounds_kernel(const TreeDesc* desc, const float* x,
+                              unsigned* bounds) {
+  TreeDesc d = desc[blockIdx.y];
+  float lo[3] = {INFINITY, INFINITY, INFINITY};
+  float hi[3] = {-INFINITY, -INFINITY, -INFINITY};
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
+       i += gridDim.x * blockDim.x) {
+    const float* p = x + 3ll * (d.p0 + i);
+    float a = p[0], b = p[1], c = p[2];
+    if (finite3(a, b, c)) {
+      lo[0] = fminf(lo[0], a); lo[1] = fminf(lo[1], b); lo[2] = fminf(lo[2], c);
+      hi[0] = fmaxf(hi[0], a); hi[1] = fmaxf(hi[1], b); hi[2] = fmaxf(hi[2], c);
+    }
+  }
+  for (int k = 0; k < 3; ++k) {
+    for (int o = 16; o; o >>= 1) {
+      lo[k] = fminf(lo[k], __shfl_xor_sync(kFull, lo[k], o));
+      hi[k] = fmaxf(hi[k], __shfl_xor_sync(kFull, hi[k], o));
+    }
+  }
+  if ((threadIdx.x & 31) == 0 && lo[0] <= hi[0]) {
+    unsigned* b = bounds + 6 * blockIdx.y;
+    for (int k = 0; k < 3; ++k) {
+      atomicMin(b + k, float_key(lo[k]));
+      atomicMax(b + 3 + k, float_key(hi[k]));
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t spread3(unsigned v) {
+  uint64_t x = v & 0x1fffffu;
+  x = (x | x << 32) & 0x1f00000000ffffull;
+  x = (x | x << 16) & 0x1f0000ff0000ffull;
+  x = (x | x << 8) & 0x100f00f00f00f00full;
+  x = (x | x << 4) & 0x10c30c30c30c30c3ull;
+  x = (x | x << 2) & 0x1249249249249249ull;
+  return x;
+}
+
+__device__ __forceinline__ unsigned quantize(float v, float lo, float scale) {
+  float t = (v - lo) * scale;
+  if (!(t >= 0.f)) return 0u;  // also NaN
+  if (t >= 2097151.f) return 2097151u;
+  return (unsigned)t;
+}
+
+__global__ void morton_kernel(const TreeDesc* desc, const float* x,
+                              const unsigned* bounds, uint64_t* keys,
+                              int* vals) {
+  TreeDesc d = desc[blockIdx.y];
+  const unsigned* b = bounds + 6 * blockIdx.y;
+  float lo[3], ext = 0.f;
+  bool any = b[0] != 0xffffffffu;
+  for (int k = 0; k < 3; ++k) {
+    lo[k] = any ? key_float(b[k]) : 0.f;
+    float h = any ? key_float(b[3 + k]) : 0.f;
+    ext = fmaxf(ext, h - lo[k]);
+  }
+  float scale = (ext > 0.f && isfinite(ext)) ? 2097151.f / ext : 0.f;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
+       i += gridDim.x * blockDim.x) {
+    const float* p = x + 3ll * (d.p0 + i);
+    uint64_t key = (spread3(quantize(p[0], lo[0], scale)) << 2) |
+                   (spread3(quantize(p[1], lo[1], scale)) << 1) |
+                   spread3(quantize(p[2], lo[2], scale));
+    keys[d.p0 + i] = key;
+    vals[d.p0 + i] = i;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Stable per-tree LSD radix sort of (64-bit key, int value) pairs.
+// Histogram layout per tree: hist[(tree*D + digit)*max_tiles + tile].
+__global__ void __launch_bounds__(kSortThreads)
+    sort_upsweep(const TreeDesc* desc, const uint64_t* keys, int shift,
+                 int* hist, int max_tiles) {
+  __shared__ int h[256];
+  TreeDesc d = desc[blockIdx.y];
+  int tile = blockIdx.x;
+  int base = tile * kSortTile;
+  if (base >= d.n) return;
+  h[threadIdx.x] = 0;
+  __syncthreads();
+  const uint64_t* k = keys + d.p0;
+#pragma unroll
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + threadIdx.x;
+    if (idx < d.n) atomicAdd(&h[(k[idx] >> shift) & 255], 1);
+  }
+  __syncthreads();
+  hist[((size_t)blockIdx.y * 256 + threadIdx.x) * max_tiles + tile] =
+      h[threadIdx.x];
+}
+
+// Exclusive scan, per tree, of `digits` x tiles(tree) counters in digit-major
+// order (one block per tree).  tiles(tree) = ceil(n / tile_size).
+__global__ void __launch_bounds__(kScanThreads)
+    seg_scan(const TreeDesc* desc, int* hist, int digits, int max_tiles,
+             int tile_size) {
+  __shared__ int warp_sums[32];
+  int b = blockIdx.x;
+  int n = desc[b].n;
+  int tiles = (n + tile_size - 1) / tile_size;
+  int total = digits * tiles;
+  int per = (total + kScanThreads - 1) / kScanThreads;
+  int start = threadIdx.x * per;
+  int end = min(start + per, total);
+  int* base = hist + (size_t)b * digits * max_tiles;
+  auto at = [&](int e) -> int& {
+    return base[(size_t)(e / tiles) * max_tiles + (e % tiles)];
+  };
+  int sum = 0;
+  for (int e = start; e < end; ++e) sum += at(e);
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = sum;
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_sums[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(kFull, v, o);
+      if (lane >= o) v += u;
+    }
+    warp_sums[lane] = v;  // inclusive
+  }
+  __syncthreads();
+  int run = incl - sum + (warp ? warp_sums[warp - 1] : 0);
+  for (int e = start; e < end; ++e) {
+    int c = at(e);
+    at(e) = run;
+    run += c;
+  }
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+    sort_scatter(const TreeDesc* desc, const uint64_t* kin, const int* vin,
+                 uint64_t* kout, int* vout, const int* hist, int shift,
+                 int max_tiles) {
+  __shared__ int cnt[256];
+  __shared__ int goff[256];
+  __shared__ int wcnt[kSortThreads / 32][256];
+  TreeDesc d = desc[blockIdx.y];
+  int tile = blockIdx.x;
+  int base = tile * kSortTile;
+  if (base >= d.n) return;
+  int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  cnt[tid] = 0;
+  goff[tid] = hist[((size_t)blockIdx.y * 256 + tid) * max_tiles + tile];
+#pragma unroll
+  for (int w = 0; w < kSortThreads / 32; ++w) wcnt[w][tid] = 0;
+  __syncthreads();
+  const uint64_t* k = kin + d.p0;
+  const int* v = vin + d.p0;
+  uint64_t* ko = kout + d.p0;
+  int* vo = vout + d.p0;
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + tid;
+    bool valid = idx < d.n;
+    uint64_t key = valid ? k[idx] : 0;
+    int val = valid ? v[idx] : 0;
+    int digit = valid ? (int)((key >> shift) & 255) : 256 + lane;
+    unsigned peers = __match_any_sync(kFull, digit);
+    int lower = __popc(peers & ((1u << lane) - 1u));
+    if (valid && lower == 0) wcnt[warp][digit] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int r = goff[digit] + cnt[digit] + lower;
+      for (int w = 0; w < warp; ++w) r += wcnt[w][digit];
+      ko[r] = key;
+      vo[r] = val;
+    }
+    __syncthreads();
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < kSortThreads / 32; ++w) {
+      s += wcnt[w][tid];
+      wcnt[w][tid] = 0;
+    }
+    cnt[tid] += s;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Karras (2012) binary radix tree over sorted keys made unique by their
+// position.  Internal node i covers sorted positions [first, last]; its
+// children are gamma and gamma+1 (a single position is a point).
+__device__ __forceinline__ int common_prefix(const uint64_t* k, int n, int i,
+                                             int j) {
+  if (j < 0 || j >= n) return -1;
+  uint64_t a = k[i], c = k[j];
+  if (a != c) return __clzll(a ^ c);
+  return 64 + __clz(i ^ j);
+}
+
+__global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
+                              int4* range, int* parent) {
+  int b = blockIdx.y;
+  TreeDesc d = desc[b];
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= d.n - 1) return;
+  const uint64_t* k = keys + d.p0;
+  int n = d.n;
+  int4* rg = range + (d.p0 - b);
+  int* par = parent + (d.p0 - b);
+  int dir = common_prefix(k, n, i, i + 1) > common_prefix(k, n, i, i - 1) ? 1 : -1;
+  int dmin = common_prefix(k, n, i, i - dir);
+  int lmax = 2;
+  while (common_prefix(k, n, i, i + lmax * dir) > dmin) lmax <<= 1;
+  int l = 0;
+  for (int t = lmax >> 1; t >= 1; t >>= 1)
+    if (common_prefix(k, n, i, i + (l + t) * dir) > dmin) l += t;
+  int j = i + l * dir;
+  int dnode = common_prefix(k, n, i, j);
+  int s = 0, t = l;
+  do {
+    t = (t + 1) >> 1;
+    if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
+  } while (t > 1);
+  int gamma = i + s * dir + min(dir, 0);
+  int first = min(i, j), last = max(i, j);
+  rg[i] = make_int4(first, last, gamma, 0);
+  if (first != gamma) par[gamma] = (i << 1) | 0;
+  if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
+}
+
+// ---------------------------------------------------------------------------
+struct RefitArgs {
+  const TreeDesc* desc;
+  const float* x;
+  const int* perm;     // sorted local point indices
+  const int4* range;
+  const int* parent;
+  int* counter;
+  float4* pts;
+  Entry* nodes;
+  Entry* root;
+  int levels;
+  int leaf;
+};
+
+__device__ __forceinline__ Entry* node_entry(Entry* nodes, const TreeDesc& d,
+                                             int level, int node, int slot) {
+  return nodes + d.node0 + ((size_t)level * (d.n - 1) + node) * 2 + slot;
+}
+
+// Leaf over sorted positions [cf, cl]: points re-ordered by ascending ID and
+// written to pts; one entry per level.
+__device__ void make_leaf(const RefitArgs& a, const TreeDesc& d, int cf, int cl,
+                          Entry* e) {
+  int ids[kMaxLeaf];
+  int c = cl - cf + 1;
+  for (int k = 0; k < c; ++k) {
+    int id = a.perm[d.p0 + cf + k];
+    int pos = k;
+    while (pos > 0 && ids[pos - 1] > id) {
+      ids[pos] = ids[pos - 1];
+      --pos;
+    }
+    ids[pos] = id;
+  }
+  for (int l = 0; l < a.levels; ++l) {
+    e[l].lox = e[l].loy = e[l].loz = INFINITY;
+    e[l].hix = e[l].hiy = e[l].hiz = -INFINITY;
+    e[l].minid = ids[0];
+    e[l].ref = leaf_ref(cf, 1);
+  }
+  for (int k = 0; k < c; ++k) {
+    int id = ids[k];
+    const float* p = a.x + 3ll * (d.p0 + id);
+    float px = p[0], py = p[1], pz = p[2];
+    a.pts[d.p0 + cf + k] = make_float4(px, py, pz, __int_as_float(id));
+    bool fin = finite3(px, py, pz);
+    for (int l = 0; l < a.levels; ++l) {
+      if (id < level_size(d.n, l)) {
+        e[l].ref = leaf_ref(cf, k + 1);
+        if (fin) {
+          e[l].lox = fminf(e[l].lox, px); e[l].loy = fminf(e[l].loy, py);
+          e[l].loz = fminf(e[l].loz, pz); e[l].hix = fmaxf(e[l].hix, px);
+          e[l].hiy = fmaxf(e[l].hiy, py); e[l].hiz = fmaxf(e[l].hiz, pz);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ Entry load_entry_cg(const Entry* e) {
+  const float4* p = reinterpret_cast<const float4*>(e);
+  float4 a = __ldcg(p), b = __ldcg(p + 1);
+  Entry r;
+  r.lox = a.x; r.loy = a.y; r.loz = a.z; r.minid = __float_as_int(a.w);
+  r.hix = b.x; r.hiy = b.y; r.hiz = b.z; r.ref = __float_as_int(b.w);
+  return r;
+}
+
+__global__ void refit_kernel(RefitArgs a) {
+  int b = blockIdx.y;
+  TreeDesc d = a.desc[b];
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  Entry e[kMaxLevels];
+  if (d.n <= a.leaf) {
+    if (i == 0) {
+      make_leaf(a, d, 0, d.n - 1, e);
+      for (int l = 0; l < a.levels; ++l) a.root[b * a.levels + l] = e[l];
+    }
+    return;
+  }
+  if (i >= d.n - 1) return;
+  const int4* rg = a.range + (d.p0 - b);
+  const int* par = a.parent + (d.p0 - b);
+  int* cnt = a.counter + (d.p0 - b);
+  int4 r = rg[i];
+  if (r.y - r.x + 1 <= a.leaf) return;  // inside a leaf
+  int leaves = 0;
+  for (int side = 0; side < 2; ++side) {
+    int cf = side ? r.z + 1 : r.x;
+    int cl = side ? r.y : r.z;
+    if (cl - cf + 1 <= a.leaf) {
+      make_leaf(a, d, cf, cl, e);
+      for (int l = 0; l < a.levels; ++l)
+        store_entry(node_entry(a.nodes, d, l, i, side), e[l]);
+      ++leaves;
+    }
+  }
+  if (!leaves) return;
+  __threadfence();
+  int old = atomicAdd(cnt + i, leaves);
+  if (old + leaves < 2) return;
+  // Karras depth is below 97 (64 key bits + 32 index bits); the bound only
+  // guards against a corrupted topology.
+  for (int climb = 0; climb < 128; ++climb) {
+    __threadfence();
+    Entry c0 = load_entry_cg(node_entry(a.nodes, d, 0, i, 0));
+    Entry c1 = load_entry_cg(node_entry(a.nodes, d, 0, i, 1));
+    bool swap = c1.minid < c0.minid;
+    for (int l = 0; l < a.levels; ++l) {
+      Entry u0 = l ? load_entry_cg(node_entry(a.nodes, d, l, i, 0)) : c0;
+      Entry u1 = l ? load_entry_cg(node_entry(a.nodes, d, l, i, 1)) : c1;
+      if (swap) {
+        store_entry(node_entry(a.nodes, d, l, i, 0), u1);
+        store_entry(node_entry(a.nodes, d, l, i, 1), u0);
+      }
+      Entry u;
+      u.lox = fminf(u0.lox, u1.lox); u.loy = fminf(u0.loy, u1.loy);
+      u.loz = fminf(u0.loz, u1.loz); u.hix = fmaxf(u0.hix, u1.hix);
+      u.hiy = fmaxf(u0.hiy, u1.hiy); u.hiz = fmaxf(u0.hiz, u1.hiz);
+      u.minid = min(u0.minid, u1.minid);
+      u.ref = i;
+      e[l] = u;
+    }
+    if (i == 0) {
+      for (int l = 0; l < a.levels; ++l) a.root[b * a.levels + l] = e[l];
+      break;
+    }
+    int pc = par[i];
+    int p = pc >> 1, side = pc & 1;
+    for (int l = 0; l < a.levels; ++l)
+      store_entry(node_entry(a.nodes, d, l, p, side), e[l]);
+    __threadfence();
+    if (atomicAdd(cnt + p, 1) == 0) break;
+    i = p;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per level l, the original IDs < n/4^l in leaf order (stable compaction).
+// Counter layout per tree: cnt[(tree*levels + level)*max_tiles + tile].
+__global__ void __launch_bounds__(kSortThreads)
+    qorder_count(const TreeDesc* desc, const float4* pts, int levels, int* cnt,
+                 int max_tiles) {
+  __shared__ int h[kMaxLevels];
+  TreeDesc d = desc[blockIdx.y];
+  int base = blockIdx.x * kSortTile;
+  if (base >= d.n) return;
+  if (threadIdx.x < kMaxLevels) h[threadIdx.x] = 0;
+  __syncthreads();
+  int c[kMaxLevels] = {0, 0, 0, 0};
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + threadIdx.x;
+    if (idx < d.n) {
+      int id = __float_as_int(pts[d.p0 + idx].w);
+      for (int l = 0; l < levels; ++l) c[l] += id < level_size(d.n, l);
+    }
+  }
+  for (int l = 0; l < levels; ++l) {
+    int v = c[l];
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&h[l], v);
+  }
+  __syncthreads();
+  if (threadIdx.x < levels)
+    cnt[((size_t)blockIdx.y * levels + threadIdx.x) * max_tiles + blockIdx.x] =
+        h[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+    qorder_scatter(const TreeDesc* desc, const float4* pts, int levels,
+                   const int* cnt, int max_tiles, int* qorder) {
+  __shared__ int run[kMaxLevels];
+  __shared__ int wsum[kSortThreads / 32][kMaxLevels];
+  TreeDesc d = desc[blockIdx.y];
+  int base = blockIdx.x * kSortTile;
+  if (base >= d.n) return;
+  int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid < levels)
+    run[tid] =
+        cnt[((size_t)blockIdx.y * levels + tid) * max_tiles + blockIdx.x];
+  __syncthreads();
+  int* out = qorder + d.q0;
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + tid;
+    int id = idx < d.n ? __float_as_int(pts[d.p0 + idx].w) : INT_MAX;
+    unsigned bal[kMaxLevels];
+    for (int l = 0; l < levels; ++l) {
+      bal[l] = __ballot_sync(kFull, id < level_size(d.n, l));
+      if (lane == 0) wsum[warp][l] = __popc(bal[l]);
+    }
+    __syncthreads();
+    for (int l = 0; l < levels; ++l) {
+      if (id < level_size(d.n, l)) {
+        int r = run[l] + __popc(bal[l] & ((1u << lane) - 1u));
+        for (int w = 0; w < warp; ++w) r += wsum[w][l];
+        out[r] = id;
+      }
+    }
+    __syncthreads();
+    if (tid < levels) {
+      int s = 0;
+      for (int w = 0; w < kSortThreads / 32; ++w) s += wsum[w][tid];
+      run[tid] += s;
+    }
+    __syncthreads();
+  }
+}
+
+inline int blocks_for(long long n, int per) {
+  return (int)std::max<long long>(1, (n + per - 1) / per);
+}
+
+}  // namespace
+
+cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
+                         int leaf, cudaStream_t s, Forest** out) {
+  *out = nullptr;
+  if (B < 1 || B > 65535 || !x || leaf < 1) return cudaErrorInvalidValue;
+  Forest* f = new (std::nothrow) Forest();
+  if (!f) return cudaErrorMemoryAllocation;
+  f->B = B;
+  f->levels = prefix ? kMaxLevels : 1;
+  f->leaf = std::min(leaf, kMaxLeaf);
+  f->x = x;
+  f->hdesc.resize(B);
+  long long node_entries = 0, q_total = 0, N = 0;
+  int max_n = 0;
+  for (int b = 0; b < B; ++b) {
+    int n = seg[b + 1] - seg[b];
+    if (n < 1 || seg[b] != N) {
+      delete f;
+      return cudaErrorInvalidValue;
+    }
+    TreeDesc& d = f->hdesc[b];
+    d.p0 = (int)N;
+    d.n = n;
+    d.node0 = (int)node_entries;
+    d.q0 = (int)q_total;
+    node_entries += 2ll * f->levels * (n - 1);
+    for (int l = 0; l < f->levels; ++l) q_total += level_size(n, l);
+    N += n;
+    max_n = std::max(max_n, n);
+  }
+  if (N > kMaxPoints || node_entries > INT_MAX || q_total > INT_MAX) {
+    delete f;
+    return cudaErrorInvalidValue;
+  }
+  f->N = (int)N;
+  f->max_n = max_n;
+  f->q_total = q_total;
+
+  cudaError_t e = cudaSuccess;
+  auto alloc = [&](void** p, size_t bytes) {
+    if (!e) e = pool_alloc(p, bytes, s);
+  };
+  alloc((void**)&f->desc, sizeof(TreeDesc) * B);
+  alloc((void**)&f->pts, sizeof(float4) * N);
+  alloc((void**)&f->nodes, sizeof(Entry) * std::max<long long>(1, node_entries));
+  alloc((void**)&f->root, sizeof(Entry) * B * f->levels);
+  alloc((void**)&f->qorder, sizeof(int) * std::max<long long>(1, q_total));
+  int max_tiles = blocks_for(max_n, kSortTile);
+  uint64_t *keys = nullptr, *keys2 = nullptr;
+  int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
+      *counter = nullptr;
+  unsigned* bounds = nullptr;
+  int4* range = nullptr;
+  long long inner = std::max<long long>(1, N - B);
+  alloc((void**)&keys, sizeof(uint64_t) * N);
+  alloc((void**)&keys2, sizeof(uint64_t) * N);
+  alloc((void**)&vals, sizeof(int) * N);
+  alloc((void**)&vals2, sizeof(int) * N);
+  alloc((void**)&hist, sizeof(int) * 256ll * B * max_tiles);
+  alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
+  alloc((void**)&range, sizeof(int4) * inner);
+  alloc((void**)&parent, sizeof(int) * inner);
+  alloc((void**)&counter, sizeof(int) * inner);
+  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * inner, s);
+
+  for (int b0 = 0; !e && b0 < B; b0 += 256) {
+    DescChunk c;
+    c.first = b0;
+    c.count = std::min(256, B - b0);
+    for (int i = 0; i < c.count; ++i) c.d[i] = f->hdesc[b0 + i];
+    upload_desc<<<1, 256, 0, s>>>(f->desc, c, bounds);
+  }
+  if (!e) {
+    dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
+    bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
+    dim3 gm(std::min(blocks_for(max_n, 256), 1024), B);
+    morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, keys, vals);
+    dim3 gs(max_tiles, B);
+    for (int pass = 0; pass < 8; ++pass) {
+      int shift = 8 * pass;
+      sort_upsweep<<<gs, kSortThreads, 0, s>>>(f->desc, keys, shift, hist,
+                                               max_tiles);
+      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, 256, max_tiles,
+                                          kSortTile);
+      sort_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, keys, vals, keys2,
+                                               vals2, hist, shift, max_tiles);
+      std::swap(keys, keys2);
+      std::swap(vals, vals2);
+    }
+    dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
+    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, range, parent);
+    RefitArgs ra;
+    ra.desc = f->desc;
+    ra.x = x;
+    ra.perm = vals;
+    ra.range = range;
+    ra.parent = parent;
+    ra.counter = counter;
+    ra.pts = f->pts;
+    ra.nodes = f->nodes;
+    ra.root = f->root;
+    ra.levels = f->levels;
+    ra.leaf = f->leaf;
+    refit_kernel<<<gk, 256, 0, s>>>(ra);
+    qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels, hist,
+                                             max_tiles);
+    seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
+                                        kSortTile);
+    qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
+                                               hist, max_tiles, f->qorder);
+    e = cudaGetLastError();
+  }
+  void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, range, parent,
+                     counter};
+  for (void* p : scratch) {
+    cudaError_t fe = pool_free(p, s);
+    if (!e) e = fe;
+  }
+  if (e) {
+    free_forest(f, s);
+    return e;
+  }
+  *out = f;
+  return cudaSuccess;
+}
+
+cudaError_t free_forest(Forest* f, cudaStream_t s) {
+  if (!f) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  void* bufs[] = {f->desc, f->pts, f->nodes, f->root, f->qorder};
+  for (void* p : bufs) {
+    cudaError_t fe = pool_free(p, s);
+    if (!e) e = fe;
+  }
+  delete f;
+  return e;
+}
+
+}  // namespace gsa

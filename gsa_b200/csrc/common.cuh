@@ -1,0 +1,104 @@
+// SPDX-License-Identifier: Apache-2.0
+// Shared device-side definitions of the B200 query engine: the forest layout
+// in HBM, the exact FP32 distance and the round-down box lower bound.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <limits.h>
+
+#define GSA_API extern "C" __attribute__((visibility("default")))
+
+namespace gsa {
+
+constexpr int kMaxLevels = 4;   // prefixes n, n/4, n/16, n/64
+constexpr int kMaxLeaf = 32;    // leaf point count fits 5 bits
+constexpr int kMaxPoints = 1 << 26;  // leaf start fits 26 bits
+constexpr unsigned kFull = 0xffffffffu;
+
+// One child entry of a binary node, per prefix level: 32 bytes, loaded as two
+// float4.  `minid` is the smallest original support ID in the subtree (all
+// levels); `ref` >= 0 names an internal node, ref < 0 encodes a leaf
+// ~((start << 5) | (count - 1)) whose `count` points are this level's members.
+struct Entry {
+  float lox, loy, loz;
+  int minid;
+  float hix, hiy, hiz;
+  int ref;
+};
+static_assert(sizeof(Entry) == 32, "entry is 32 bytes");
+
+// Per-tree descriptor of a forest (a batch of independent trees, one per
+// scene).  Offsets are in elements of the forest-wide arrays.
+struct TreeDesc {
+  int p0;     // first point of this tree in pts / x (and first row of seg)
+  int n;      // number of support points
+  int node0;  // first Entry of this tree in `nodes` (levels*(n-1)*2 entries)
+  int q0;     // first slot of this tree in `qorder` (sum of level sizes)
+};
+
+struct ForestView {
+  const TreeDesc* desc;
+  const float4* pts;    // leaf order; within a leaf ascending ID; w = ID bits
+  const Entry* nodes;   // [tree][level][node][2]
+  const Entry* root;    // [tree][level]
+  const int* qorder;    // [tree][level][m_l] original IDs < m_l in leaf order
+  const float* x;       // borrowed original coordinates (AoS, 3 floats)
+  int levels;           // 4 for prefix trees, 1 otherwise
+};
+
+__host__ __device__ inline int level_size(int n, int level) {
+  return level <= 0 ? n : (n >> (2 * level));
+}
+
+__device__ inline int leaf_ref(int start, int count) {
+  return ~((start << 5) | (count - 1));
+}
+__device__ inline void leaf_decode(int ref, int& start, int& count) {
+  int v = ~ref;
+  start = v >> 5;
+  count = (v & 31) + 1;
+}
+
+__device__ inline Entry load_entry(const Entry* e) {
+  const float4* p = reinterpret_cast<const float4*>(e);
+  float4 a = __ldg(p), b = __ldg(p + 1);
+  Entry r;
+  r.lox = a.x; r.loy = a.y; r.loz = a.z; r.minid = __float_as_int(a.w);
+  r.hix = b.x; r.hiy = b.y; r.hiz = b.z; r.ref = __float_as_int(b.w);
+  return r;
+}
+
+__device__ inline void store_entry(Entry* e, const Entry& r) {
+  float4* p = reinterpret_cast<float4*>(e);
+  p[0] = make_float4(r.lox, r.loy, r.loz, __int_as_float(r.minid));
+  p[1] = make_float4(r.hix, r.hiy, r.hiz, __int_as_float(r.ref));
+}
+
+// Exact squared distance ((dx*dx + dy*dy) + dz*dz), every operation rounded
+// to nearest, never contracted into FMA, subnormals kept (GSA
+// csrc/gsa_bvh.cu:278-281, csrc/reference_queries.cu:34-35, docs/api.md).
+__device__ __forceinline__ float exact_d2(float qx, float qy, float qz,
+                                          float px, float py, float pz) {
+  float dx = __fsub_rn(qx, px), dy = __fsub_rn(qy, py), dz = __fsub_rn(qz, pz);
+  return __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)),
+                   __fmul_rn(dz, dz));
+}
+
+// Squared point-to-box distance rounded toward -inf at every step, so it never
+// exceeds exact_d2 of any point inside the box (GSA csrc/gsa_bvh.cu:121-132).
+// An empty box (lo > hi) is reported as +inf.
+__device__ __forceinline__ float lower_d2(float qx, float qy, float qz,
+                                         const Entry& b) {
+  if (b.lox > b.hix) return __int_as_float(0x7f800000);
+  float dx = fmaxf(0.f, fmaxf(__fsub_rd(b.lox, qx), __fsub_rd(qx, b.hix)));
+  float dy = fmaxf(0.f, fmaxf(__fsub_rd(b.loy, qy), __fsub_rd(qy, b.hiy)));
+  float dz = fmaxf(0.f, fmaxf(__fsub_rd(b.loz, qz), __fsub_rd(qz, b.hiz)));
+  return __fadd_rd(__fadd_rd(__fmul_rd(dx, dx), __fmul_rd(dy, dy)),
+                   __fmul_rd(dz, dz));
+}
+
+__device__ __forceinline__ bool finite3(float a, float b, float c) {
+  return isfinite(a) && isfinite(b) && isfinite(c);
+}
+
+}  // namespace gsa

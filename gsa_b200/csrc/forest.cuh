@@ -1,0 +1,57 @@
+// SPDX-License-Identifier: Apache-2.0
+// Host-side forest object: a batch of independent prefix BVHs (one per scene)
+// built and queried together.  A single-scene tree is a forest of one.
+#pragma once
+#include <vector>
+#include "common.cuh"
+
+namespace gsa {
+
+struct Forest {
+  int B = 0;        // trees
+  int N = 0;        // total support points
+  int levels = 1;   // 4 for prefix trees
+  int leaf = 16;    // maximum leaf size used by the builder
+  int max_n = 0;
+  long long q_total = 0;
+  std::vector<TreeDesc> hdesc;
+  TreeDesc* desc = nullptr;
+  float4* pts = nullptr;
+  Entry* nodes = nullptr;
+  Entry* root = nullptr;
+  int* qorder = nullptr;
+  const float* x = nullptr;  // borrowed
+
+  ForestView view() const {
+    ForestView v;
+    v.desc = desc;
+    v.pts = pts;
+    v.nodes = nodes;
+    v.root = root;
+    v.qorder = qorder;
+    v.x = x;
+    v.levels = levels;
+    return v;
+  }
+};
+
+// Builds a forest over `B` trees whose points are x[seg[b]*3 .. seg[b+1]*3)
+// (seg on the host, B+1 entries, every tree non-empty).  Stream-ordered; no
+// host synchronisation.  Returns cudaSuccess or an error.
+cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
+                         int leaf, cudaStream_t s, Forest** out);
+cudaError_t free_forest(Forest* f, cudaStream_t s);
+
+// Query launchers (query.cu).  For a forest, `qseg` (device) and
+// `qseg_host` (host) hold B+1 query offsets and each tree uses its own level
+// size as support prefix; for a single tree both are null and `nq` queries
+// with the explicit support prefix `m` are used.
+cudaError_t launch_radius(const Forest& f, const float* q, const int* qseg,
+                          const int* qseg_host, int nq, int m, int level,
+                          float radius, int ns, int* out, int* fallback,
+                          cudaStream_t s);
+cudaError_t launch_knn3(const Forest& f, const float* q, const int* qseg,
+                        const int* qseg_host, int nq, int m, int level,
+                        float* d, int* ix, int* fallback, cudaStream_t s);
+
+}  // namespace gsa

@@ -1,0 +1,405 @@
+// SPDX-License-Identifier: Apache-2.0
+// Exact ordered radius query and exact 3NN query over a prefix-bounds forest.
+//
+// Semantics follow GSA csrc/gsa_bvh.cu:282-343 (radius_ordered) and
+// csrc/gsa_bvh.cu:149-211 (query3): the first `ns` qualifying support IDs
+// < m in ascending ID order with d2 < r*r (pad with the first, zero row when
+// none); the three smallest finite squared distances in (d2, id) order,
+// missing entries (inf, 0).  Results do not depend on traversal order.
+//
+// Execution model (B200): one warp traverses the tree for 32 queries at once
+// ("packet" traversal).  Queries are visited in the tree's leaf order (for a
+// query array that is a prefix of the support, neighbouring lanes hold
+// neighbouring points), so the 32 lanes need nearly the same nodes; a node is
+// entered when any lane needs it, node entries and leaf points are loaded
+// once per warp as 16-byte broadcast loads, and each lane tests its own query.
+// The radius descent order is ascending subtree minimum ID (stored order of
+// the children), which makes the "K found and minid >= K-th ID" early exit of
+// the reference effective.  The warp stack lives in shared memory; a stack
+// overflow (impossible for STACK >= 97 on a Karras tree of 64-bit keys) falls
+// back to the exact original-order scan and is counted, as in the reference.
+#include <algorithm>
+#include "forest.cuh"
+
+#ifndef GSA_STACK
+#define GSA_STACK 128
+#endif
+
+namespace gsa {
+namespace {
+
+constexpr int kQThreads = 256;
+constexpr int kQWarps = kQThreads / 32;
+
+struct QArgs {
+  ForestView f;
+  const float* q;
+  const int* qseg;  // per-tree query offsets (device) or null
+  int nq;           // single tree: number of queries
+  int m;            // single tree: support prefix; 0 = level size
+  int level;        // bounds level, -1 = all points (level 0 data)
+  float radius;
+  int ns;
+  int* out;
+  float* dout;
+  int* fallback;
+};
+
+__device__ __forceinline__ bool nonempty(const Entry& e) {
+  return e.lox <= e.hix;
+}
+
+// Largest stored level whose prefix still holds all Q queries.
+__device__ __forceinline__ int query_level(int n, int levels, int Q) {
+  int l = 0;
+  while (l + 1 < levels && level_size(n, l + 1) >= Q) ++l;
+  return l;
+}
+
+__device__ __forceinline__ int level_offset(int n, int l) {
+  int o = 0;
+  for (int k = 0; k < l; ++k) o += level_size(n, k);
+  return o;
+}
+
+struct Slot {
+  int qbase, Q, m, slots, lev;
+  const int* order;
+};
+
+__device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
+                                           int b) {
+  Slot s;
+  s.qbase = a.qseg ? a.qseg[b] : 0;
+  s.Q = a.qseg ? a.qseg[b + 1] - s.qbase : a.nq;
+  s.m = a.m > 0 ? a.m : level_size(d.n, a.level);
+  s.lev = a.level < 0 ? 0 : a.level;
+  int ql = s.Q <= d.n ? query_level(d.n, a.f.levels, s.Q) : 0;
+  s.slots = s.Q <= d.n ? level_size(d.n, ql) : s.Q;
+  s.order = a.f.qorder + d.q0 + level_offset(d.n, ql);
+  return s;
+}
+
+__device__ __forceinline__ int slot_query(const Slot& s, const TreeDesc& d,
+                                          int t) {
+  if (t >= s.slots) return -1;
+  int qi = t < d.n ? __ldg(s.order + t) : t;
+  return qi < s.Q ? qi : -1;
+}
+
+__device__ __forceinline__ bool radius_test(const Entry& e, float px, float py,
+                                            float pz, int m, int bound,
+                                            float r2) {
+  return e.minid < m && e.minid < bound && nonempty(e) &&
+         lower_d2(px, py, pz, e) < r2;
+}
+
+template <int STACK>
+__global__ void __launch_bounds__(kQThreads)
+    radius_kernel(QArgs a) {
+  __shared__ int lists[kQWarps][32][33];
+  __shared__ int stack[kQWarps][STACK];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
+  if (t0 >= s.slots) return;  // warp-uniform
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qbase + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  const int K = a.ns;
+  const int m = s.m;
+  const float r2 = __fmul_rn(a.radius, a.radius);
+  int* L = lists[warp][lane];
+  int* stk = stack[warp];
+  int count = 0, bound = INT_MAX;
+  const Entry* nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  const float4* pts = a.f.pts + d.p0;
+  Entry cur = load_entry(a.f.root + b * a.f.levels + s.lev);
+  bool need = active && radius_test(cur, px, py, pz, m, bound, r2);
+  int top = 0;
+  bool overflow = false;
+  // A valid tree is visited at most once per node; the cap only guards
+  // against a corrupted handle (then the exact scan answers).
+  long long steps = 0, max_steps = 4ll * d.n + 64;
+  while (true) {
+    if (++steps > max_steps) {
+      overflow = true;
+      break;
+    }
+    if (!__any_sync(kFull, need)) {
+      if (top == 0) break;
+      int ei = stk[--top];
+      cur = load_entry(nodes + ei);
+      need = active && radius_test(cur, px, py, pz, m, bound, r2);
+      continue;
+    }
+    if (cur.ref >= 0) {
+      const Entry* ch = nodes + (size_t)cur.ref * 2;
+      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
+      bool n0 = need && radius_test(c0, px, py, pz, m, bound, r2);
+      bool n1 = need && radius_test(c1, px, py, pz, m, bound, r2);
+      bool a0 = __any_sync(kFull, n0), a1 = __any_sync(kFull, n1);
+      if (a0) {
+        if (a1) {
+          if (top == STACK) {
+            overflow = true;
+            break;
+          }
+          stk[top++] = cur.ref * 2 + 1;
+        }
+        cur = c0;
+        need = n0;
+      } else {
+        cur = c1;
+        need = n1;
+      }
+    } else {
+      int start, cnt;
+      leaf_decode(cur.ref, start, cnt);
+      for (int j = 0; j < cnt; ++j) {
+        float4 pt = __ldg(pts + start + j);
+        int id = __float_as_int(pt.w);
+        if (id >= m) break;  // leaf points ascend by ID
+        bool cand = need && id < bound;
+        if (!__any_sync(kFull, cand)) break;
+        if (cand && exact_d2(px, py, pz, pt.x, pt.y, pt.z) < r2) {
+          int pos = count < K ? count : K - 1;
+          while (pos > 0 && L[pos - 1] > id) {
+            L[pos] = L[pos - 1];
+            --pos;
+          }
+          L[pos] = id;
+          if (count < K) ++count;
+          if (count == K) bound = L[K - 1];
+        }
+      }
+      need = false;
+    }
+  }
+  if (overflow && active) {
+    atomicAdd(a.fallback, 1);
+    count = 0;
+    const float* xs = a.f.x + 3ll * d.p0;
+    for (int id = 0; id < m && count < K; ++id) {
+      const float* p = xs + 3ll * id;
+      if (exact_d2(px, py, pz, p[0], p[1], p[2]) < r2) L[count++] = id;
+    }
+  }
+  __syncwarp();
+  for (int j = 0; j < 32; ++j) {
+    int qj = __shfl_sync(kFull, qi, j);
+    int cj = __shfl_sync(kFull, count, j);
+    if (qj < 0) continue;
+    if (lane < K) {
+      int v = cj ? lists[warp][j][lane < cj ? lane : 0] : 0;
+      a.out[(size_t)(s.qbase + qj) * K + lane] = v;
+    }
+  }
+}
+
+__device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
+                                        float& d2, int& i0, int& i1, int& i2) {
+  if (!isfinite(v)) return;
+  if (v < d2 || (v == d2 && id < i2)) {
+    if (v < d1 || (v == d1 && id < i1)) {
+      d2 = d1;
+      i2 = i1;
+      if (v < d0 || (v == d0 && id < i0)) {
+        d1 = d0;
+        i1 = i0;
+        d0 = v;
+        i0 = id;
+      } else {
+        d1 = v;
+        i1 = id;
+      }
+    } else {
+      d2 = v;
+      i2 = id;
+    }
+  }
+}
+
+template <int STACK>
+__global__ void __launch_bounds__(kQThreads)
+    knn3_kernel(QArgs a) {
+  __shared__ int stack[kQWarps][STACK];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
+  if (t0 >= s.slots) return;
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qbase + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  const int m = s.m;
+  const float inf = __int_as_float(0x7f800000);
+  float d0 = inf, d1 = inf, d2 = inf;
+  int i0 = INT_MAX, i1 = INT_MAX, i2 = INT_MAX;
+  int* stk = stack[warp];
+  const Entry* nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  const float4* pts = a.f.pts + d.p0;
+  Entry cur = load_entry(a.f.root + b * a.f.levels + s.lev);
+  bool need = active && cur.minid < m && nonempty(cur) &&
+              lower_d2(px, py, pz, cur) <= d2;
+  int top = 0;
+  bool overflow = false;
+  long long steps = 0, max_steps = 4ll * d.n + 64;
+  while (true) {
+    if (++steps > max_steps) {
+      overflow = true;
+      break;
+    }
+    if (!__any_sync(kFull, need)) {
+      if (top == 0) break;
+      int ei = stk[--top];
+      cur = load_entry(nodes + ei);
+      need = active && cur.minid < m && nonempty(cur) &&
+             lower_d2(px, py, pz, cur) <= d2;
+      continue;
+    }
+    if (cur.ref >= 0) {
+      const Entry* ch = nodes + (size_t)cur.ref * 2;
+      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
+      float l0 = lower_d2(px, py, pz, c0), l1 = lower_d2(px, py, pz, c1);
+      bool n0 = need && c0.minid < m && nonempty(c0) && l0 <= d2;
+      bool n1 = need && c1.minid < m && nonempty(c1) && l1 <= d2;
+      unsigned b0 = __ballot_sync(kFull, n0), b1 = __ballot_sync(kFull, n1);
+      if (b0 && b1) {
+        unsigned both = b0 & b1;
+        unsigned pref1 = __ballot_sync(kFull, n0 && n1 && l1 < l0);
+        bool first1 = 2 * __popc(pref1) > __popc(both);
+        if (top == STACK) {
+          overflow = true;
+          break;
+        }
+        stk[top++] = cur.ref * 2 + (first1 ? 0 : 1);
+        cur = first1 ? c1 : c0;
+        need = first1 ? n1 : n0;
+      } else if (b0) {
+        cur = c0;
+        need = n0;
+      } else {
+        cur = c1;
+        need = n1;
+      }
+    } else {
+      int start, cnt;
+      leaf_decode(cur.ref, start, cnt);
+      for (int j = 0; j < cnt; ++j) {
+        float4 pt = __ldg(pts + start + j);
+        int id = __float_as_int(pt.w);
+        if (id >= m) break;
+        if (need)
+          insert3(exact_d2(px, py, pz, pt.x, pt.y, pt.z), id, d0, d1, d2, i0,
+                  i1, i2);
+      }
+      need = false;
+    }
+  }
+  if (overflow && active) {
+    atomicAdd(a.fallback, 1);
+    d0 = d1 = d2 = inf;
+    i0 = i1 = i2 = INT_MAX;
+    const float* xs = a.f.x + 3ll * d.p0;
+    for (int id = 0; id < m; ++id) {
+      const float* p = xs + 3ll * id;
+      insert3(exact_d2(px, py, pz, p[0], p[1], p[2]), id, d0, d1, d2, i0, i1,
+              i2);
+    }
+  }
+  if (active) {
+    size_t o = (size_t)(s.qbase + qi) * 3;
+    a.dout[o] = d0;
+    a.dout[o + 1] = d1;
+    a.dout[o + 2] = d2;
+    a.out[o] = i0 == INT_MAX ? 0 : i0;
+    a.out[o + 1] = i1 == INT_MAX ? 0 : i1;
+    a.out[o + 2] = i2 == INT_MAX ? 0 : i2;
+  }
+}
+
+// Slots (query positions walked by warps) of one tree, as slot_setup.
+long long tree_slots(int n, int levels, int nq) {
+  if (nq > n) return nq;
+  int l = 0;
+  while (l + 1 < levels && level_size(n, l + 1) >= nq) ++l;
+  return level_size(n, l);
+}
+
+// Largest slot count over the trees, from host-side query offsets.
+long long max_slots(const Forest& f, const int* qseg_host, int nq) {
+  if (!qseg_host) return nq > 0 ? tree_slots(f.hdesc[0].n, f.levels, nq) : 0;
+  long long best = 0;
+  for (int b = 0; b < f.B; ++b) {
+    int q = qseg_host[b + 1] - qseg_host[b];
+    if (q > 0) best = std::max(best, tree_slots(f.hdesc[b].n, f.levels, q));
+  }
+  return best;
+}
+
+QArgs make_args(const Forest& f, const float* q, const int* qseg, int nq,
+                int m, int level) {
+  QArgs a;
+  a.f = f.view();
+  a.q = q;
+  a.qseg = qseg;
+  a.nq = nq;
+  a.m = m;
+  a.level = level;
+  a.radius = 0.f;
+  a.ns = 0;
+  a.out = nullptr;
+  a.dout = nullptr;
+  a.fallback = nullptr;
+  return a;
+}
+
+}  // namespace
+
+cudaError_t launch_radius(const Forest& f, const float* q, const int* qseg,
+                          const int* qseg_host, int nq, int m, int level,
+                          float radius, int ns, int* out, int* fallback,
+                          cudaStream_t s) {
+  QArgs a = make_args(f, q, qseg, nq, m, level);
+  a.radius = radius;
+  a.ns = ns;
+  a.out = out;
+  a.fallback = fallback;
+  long long slots = max_slots(f, qseg_host, nq);
+  if (slots <= 0) return cudaSuccess;
+  dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
+  radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_knn3(const Forest& f, const float* q, const int* qseg,
+                        const int* qseg_host, int nq, int m, int level,
+                        float* d, int* ix, int* fallback, cudaStream_t s) {
+  QArgs a = make_args(f, q, qseg, nq, m, level);
+  a.dout = d;
+  a.out = ix;
+  a.fallback = fallback;
+  long long slots = max_slots(f, qseg_host, nq);
+  if (slots <= 0) return cudaSuccess;
+  dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
+  knn3_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace gsa

@@ -1,0 +1,171 @@
+# SPDX-License-Identifier: Apache-2.0
+"""ctypes binding of the prefix-BVH library (drop-in for GSA ``gsa/runtime.py``).
+
+``Tree(x, prefix=False, leaf=16)`` indexes a borrowed CUDA FP32 ``(N, 3)``
+tensor; ``Tree.query`` is the exact 3NN query and ``Tree.ball`` the exact
+ordered radius query, both on the current CUDA stream.  Contract violations
+raise ``ValueError`` and native error codes raise ``RuntimeError``, under the
+same conditions as ``gsa/runtime.py:44-178``; ``pool_memory`` reports the
+native pool's high-water marks (``gsa/runtime.py:34-41``).
+"""
+
+import ctypes
+import math
+
+import torch
+
+from ._library import load
+
+lib = load("gsa_bvh")
+_ptr, _int = ctypes.c_void_p, ctypes.c_int
+_u64p, _intp = ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int)
+for _name, _args in {
+    "build_bvh": [_ptr, _int, _int, _int, ctypes.POINTER(_ptr), _ptr],
+    "query_bvh": [_ptr, _ptr, _int, _int, _int, _ptr, _ptr, _ptr, _ptr],
+    "query_ball_bvh": [_ptr, _ptr, _int, _int, _int, ctypes.c_float, _int, _ptr, _ptr, _ptr],
+    "free_bvh": [_ptr, _int, _ptr],
+    "pool_memory": [_u64p, _u64p],
+    "pool_reset_peak": [],
+    "set_pool_mode": [_int],
+    "bvh_info": [_ptr, _intp, _intp, _intp, _intp],
+}.items():
+    getattr(lib, _name).argtypes = _args
+    getattr(lib, _name).restype = _int
+
+_FLT_MAX = torch.finfo(torch.float32).max
+_pool_device = None
+
+
+def check(code):
+    if code:
+        raise RuntimeError(f"BVH error {code}")
+
+
+def pool_memory():
+    used, reserved = ctypes.c_uint64(), ctypes.c_uint64()
+    check(lib.pool_memory(ctypes.byref(used), ctypes.byref(reserved)))
+    return {
+        "native_pool_used_peak_bytes": used.value,
+        "native_pool_reserved_peak_bytes": reserved.value,
+    }
+
+
+def pool_reset_peak():
+    check(lib.pool_reset_peak())
+
+
+def set_pool_mode(enabled):
+    check(lib.set_pool_mode(int(bool(enabled))))
+
+
+def prefix_sizes(n):
+    """Supports a prefix index over ``n`` points serves: ``n, n//4, n//16,
+    n//64`` (``docs/api.md`` "Index reuse")."""
+    return [n >> (2 * level) for level in range(4)]
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _is_points(x):
+    return (
+        isinstance(x, torch.Tensor)
+        and x.is_cuda
+        and x.is_contiguous()
+        and x.dtype == torch.float32
+        and x.ndim == 2
+        and x.shape[1] == 3
+    )
+
+
+def _is_rows(t, like, rows, width, dtype):
+    return (
+        t.device == like.device
+        and t.is_contiguous()
+        and t.dtype == dtype
+        and t.shape == (rows, width)
+    )
+
+
+class Tree:
+    """Exact query index over a borrowed support tensor."""
+
+    def __init__(self, x, prefix=False, leaf=16):
+        global _pool_device
+        if not (
+            _is_points(x)
+            and len(x) > 0
+            and x.device.index == torch.cuda.current_device()
+            and isinstance(leaf, int)
+            and leaf >= 1
+        ):
+            raise ValueError(
+                "Tree requires nonempty contiguous CUDA FP32 (N,3) on the current device and a positive leaf size"
+            )
+        if _pool_device not in (None, x.device.index):
+            raise ValueError("The native allocator supports one CUDA device per process")
+        _pool_device = x.device.index
+        self.x = x
+        self.prefix = prefix
+        self.stream = _stream()
+        self.ptr = _ptr()
+        self.fallback = torch.zeros(1, device=x.device, dtype=torch.int32)
+        check(lib.build_bvh(x.data_ptr(), len(x), int(prefix), leaf, ctypes.byref(self.ptr), self.stream))
+
+    def level(self, m):
+        """Bounds level for support prefix ``m`` (-1 for a plain tree)."""
+        return prefix_sizes(len(self.x)).index(m) if self.prefix else -1
+
+    def _usable_here(self):
+        return (
+            bool(self.ptr)
+            and torch.cuda.current_device() == self.x.device.index
+            and _stream() == self.stream
+        )
+
+    def _check_query(self, q, m, idx, width):
+        if not (
+            self._usable_here()
+            and q.device == self.x.device
+            and _is_points(q)
+            and _is_rows(idx, q, len(q), width, torch.int32)
+            and 1 <= m <= len(self.x)
+        ):
+            raise ValueError("Invalid query buffers, support length, or tree lifetime/device/stream")
+
+    def query(self, q, m, d, idx):
+        """Exact 3NN of ``q`` against support IDs ``< m``; ``d``/``idx`` (Q, 3)."""
+        self._check_query(q, m, idx, 3)
+        if m < 3 or not _is_rows(d, q, len(q), 3, torch.float32):
+            raise ValueError("3NN requires at least 3 supports and FP32 (Q,3) distances")
+        if len(q):
+            check(
+                lib.query_bvh(
+                    self.ptr, q.data_ptr(), len(q), m, self.level(m), d.data_ptr(),
+                    idx.data_ptr(), self.fallback.data_ptr(), _stream(),
+                )
+            )
+        return d, idx
+
+    def ball(self, q, m, r, ns, idx):
+        """First ``ns`` support IDs ``< m`` within radius ``r`` per query."""
+        self._check_query(q, m, idx, ns)
+        if not (isinstance(ns, int) and 1 <= ns <= 32 and math.isfinite(r) and 0 <= r <= _FLT_MAX):
+            raise ValueError("Radius query requires K in [1,32] and finite nonnegative FP32 radius")
+        if len(q):
+            check(
+                lib.query_ball_bvh(
+                    self.ptr, q.data_ptr(), len(q), m, self.level(m), r, ns,
+                    idx.data_ptr(), self.fallback.data_ptr(), _stream(),
+                )
+            )
+        return idx
+
+    def close(self):
+        if not self.ptr:
+            return
+        if torch.cuda.current_device() != self.x.device.index or _stream() != self.stream:
+            raise ValueError("Close the tree on its original device and stream")
+        check(lib.free_bvh(self.ptr, 1, _stream()))
+        self.ptr = _ptr()

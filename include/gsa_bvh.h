@@ -1,0 +1,134 @@
+/* SPDX-License-Identifier: Apache-2.0
+ *
+ * gsa_bvh: exact prefix-BVH point queries for B200 (sm_100a).
+ * Shared library: gsa_b200/_native/gsa_bvh.so
+ *
+ * Drop-in for the C ABI of GSA's csrc/gsa_bvh.cu (qmkkk/GSA), as bound by
+ * gsa/runtime.py:13-26.  All pointers named x, q, d, ix, out, fallback, flags
+ * and cached are DEVICE pointers on the current CUDA device; `stream` is a
+ * cudaStream_t.  Every call is stream-ordered and does not synchronise the
+ * host (except free_bvh with async_free == 0).
+ *
+ * Return codes (as in the reference): 0 success; a cudaError_t value for a
+ * CUDA error; -1 build failure / invalid build argument; -2 invalid query
+ * argument (bad m, level or ns); -3 invalid handle on free.
+ *
+ * Coordinates are contiguous float32 (N, 3).  Squared distance is
+ * ((dx*dx + dy*dy) + dz*dz), round-to-nearest, no FMA, subnormals kept.
+ */
+#ifndef GSA_B200_GSA_BVH_H
+#define GSA_B200_GSA_BVH_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Builds a tree over x[0..n).  prefix != 0 stores bounds for the four ordered
+ * prefixes n, n/4, n/16, n/64 (levels 0..3) on one topology.  x is BORROWED:
+ * it must stay alive and unchanged until free_bvh.  leaf >= 1 is the maximum
+ * leaf size (clamped to 32; results never depend on it).
+ * Replaces: int build_bvh(const float*, int, int, int, void**, void*)
+ *           -- GSA csrc/gsa_bvh.cu:217 */
+int build_bvh(const float* x, int n, int prefix, int leaf, void** out,
+              void* stream);
+
+/* Exact 3NN of nq queries against support IDs < m (3 <= m <= n).  level is
+ * -1 (all-point bounds) or the prefix level whose size is >= m.  Writes
+ * d[nq*3] ascending squared distances and ix[nq*3] IDs, ties by lower ID,
+ * missing entries (inf, 0).  *fallback counts stack-overflow full scans.
+ * Replaces: int query_bvh(void*, const float*, int, int, int, float*, int*,
+ *           int*, void*) -- GSA csrc/gsa_bvh.cu:249 */
+int query_bvh(void* h, const float* q, int nq, int m, int level, float* d,
+              int* ix, int* fallback, void* stream);
+
+/* Exact ordered radius query: per query the first ns (1..32) support IDs
+ * < m (1 <= m <= n) with d2 < radius*radius, ascending, padded with the
+ * first; a zero row when none qualifies.  out is int32 [nq*ns].
+ * Replaces: int query_ball_bvh(void*, const float*, int, int, int, float,
+ *           int, int*, int*, void*) -- GSA csrc/gsa_bvh.cu:344 */
+int query_ball_bvh(void* h, const float* q, int nq, int m, int level,
+                   float radius, int ns, int* out, int* fallback,
+                   void* stream);
+
+/* Releases a tree (stream-ordered); async_free == 0 also synchronises the
+ * stream.  Replaces: int free_bvh(void*, int, void*)
+ * -- GSA csrc/gsa_bvh.cu:258 */
+int free_bvh(void* h, int async_free, void* stream);
+
+/* 1: allocate from the library's private memory pool (default); 0: from the
+ * device's default pool.  Replaces: int set_pool_mode(int)
+ * -- GSA csrc/gsa_bvh.cu:356 */
+int set_pool_mode(int enabled);
+
+/* High-water marks of the private pool (0, 0 before first use).
+ * Replaces: int pool_memory(uint64_t*, uint64_t*) -- GSA csrc/gsa_bvh.cu:360 */
+int pool_memory(uint64_t* used_peak, uint64_t* reserved_peak);
+
+/* Resets both high-water marks.
+ * Replaces: int pool_reset_peak(void) -- GSA csrc/gsa_bvh.cu:373 */
+int pool_reset_peak(void);
+
+/* ---- Extensions without a counterpart in the reference ---------------- */
+
+/* Forest of b independent trees (one per scene) over one concatenated point
+ * array: tree i owns x[seg[i]..seg[i+1]) (seg is a HOST array of b+1
+ * ascending offsets starting at 0, every tree non-empty).  All trees are
+ * built by the same kernel launches.  Replaces the per-scene loop of
+ * build_bvh calls (GSA csrc/gsa_bvh.cu:217) for batched inference. */
+int build_bvh_batch(const float* x, const int* seg, int b, int prefix,
+                    int leaf, void** out, void* stream);
+
+/* Radius query on every tree of a forest in one launch.  Queries of tree i
+ * are q[qseg[i]..qseg[i+1]) (qseg on the device, qseg_host the same offsets
+ * on the host); tree i uses support prefix m_i = n_i >> (2*level) (n_i for
+ * level -1).  out rows follow the query rows. */
+int query_ball_bvh_batch(void* h, const float* q, const int* qseg,
+                         const int* qseg_host, int level, float radius,
+                         int ns, int* out, int* fallback, void* stream);
+
+/* 3NN on every tree of a forest in one launch (same layout as above). */
+int query_bvh_batch(void* h, const float* q, const int* qseg,
+                    const int* qseg_host, int level, float* d, int* ix,
+                    int* fallback, void* stream);
+
+/* Trees, points, stored levels and leaf size of a handle (any may be null). */
+int bvh_info(void* h, int* trees, int* points, int* levels, int* leaf);
+
+/* Reuse-cache check: for each pair c < count, flags[c] = 0 when the nfloat[c]
+ * float32 values at a[c] and b[c] are all equal (IEEE ==, the semantics of
+ * torch.equal: NaN never equal, -0 == +0), else 1.  a, b, nfloat are HOST
+ * arrays of device pointers / counts; flags is device int[count].  One
+ * launch for all pairs.  Replaces the per-comparison torch.equal of
+ * GSA gsa/session.py:39-43. */
+int coords_mismatch(int count, const float* const* a, const float* const* b,
+                    const long long* nfloat, int* flags, void* stream);
+
+/* Reuse-cache gather: selects the first candidate c < count (count <= 64)
+ * whose flags[2c] and flags[2c+1] are both 0 and copies
+ * cached[c][i*src_ld + j] to dst[i*cols + j] for i < rows, j < cols; writes c
+ * (or -1 when none matches) to *hit (device int, may be null).  cached is a
+ * HOST array of device pointers.  Replaces `out.copy_(cached[:len(q), :k])`
+ * of GSA gsa/session.py:111. */
+int reuse_rows(int count, const int* const* cached, const int* flags,
+               int src_ld, int rows, int cols, int* dst, int* hit,
+               void* stream);
+
+/* dst[i*cols + j] = src[i*src_ld + j] for i < rows, j < cols.  Replaces
+ * `out.copy_(result[:, :k])` of GSA gsa/session.py:128. */
+int gather_rows(const int* src, int src_ld, int rows, int cols, int* dst,
+                void* stream);
+
+/* Farthest-point order of b scenes of n points each (x is [b][n][3]),
+ * starting at start[b] (device int[b]); order is device int[b][n].  Ties pick
+ * the lowest index; chosen points are never repeated.  Input generator for
+ * FPS-ordered supports (FPS itself lives upstream of GSA, in FlashFPS). */
+int fps_order(int b, int n, const float* x, const int* start, int* order,
+              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,101 @@
+# SPDX-License-Identifier: Apache-2.0
+"""CPU stand-ins for the session's device operations, backed by the oracle.
+
+Used only by CPU tests of the session's host logic (admission, candidate
+ordering, statistics replay).  Every device result comes from
+``oracle.numpy_oracle``; comparisons use ``torch.equal`` one pair at a time,
+exactly like the reference session.
+"""
+
+import numpy as np
+import torch
+
+from gsa_b200.session import QuerySession
+from oracle import numpy_oracle as orc
+
+
+class OracleTree:
+    def __init__(self, root):
+        self.x = root
+        self.fallback = torch.zeros(1, dtype=torch.int32)
+
+    def ball(self, q, m, r, ns, out):
+        out.copy_(torch.from_numpy(orc.ball_oracle(q.numpy(), self.x[:m].numpy(), r, ns)))
+
+    def query(self, q, m, d, ids):
+        ed, ei = orc.nn_oracle(q.numpy(), self.x[:m].numpy())
+        d.copy_(torch.from_numpy(ed))
+        ids.copy_(torch.from_numpy(ei))
+
+    def close(self):
+        pass
+
+
+def _ball_scan(b, n, m, r, k, q, x, out):
+    for i in range(b):
+        res = orc.ball_scan_untouched(q[i].numpy(), x[i].numpy(), r, k, out[i].numpy())
+        out[i].copy_(torch.from_numpy(res))
+
+
+def _nn_scan(b, n, m, q, x, d, ids):
+    for i in range(b):
+        ed, ei = orc.nn_oracle(q[i].numpy(), x[i].numpy())
+        d[i].copy_(torch.from_numpy(ed))
+        ids[i].copy_(torch.from_numpy(ei))
+
+
+class OracleOps:
+    comparisons = 0
+
+    @staticmethod
+    def current():
+        return 0, 0
+
+    @staticmethod
+    def on_device(x, device):
+        return not x.is_cuda
+
+    def mismatch(self, pairs, device):
+        return torch.tensor([0 if torch.equal(a, b) else 1 for a, b in pairs], dtype=torch.int32)
+
+    def reuse(self, cached, flags, rows, cols, out):
+        f = flags.tolist()
+        for c, rows_c in enumerate(cached):
+            if not (f[2 * c] or f[2 * c + 1]):
+                out.copy_(rows_c[:rows, :cols])
+                return
+
+    @staticmethod
+    def fetch(flags):
+        return flags.tolist()
+
+    @staticmethod
+    def copy_cols(out, result, k):
+        out.copy_(result[: out.shape[0], :k])
+
+    @staticmethod
+    def zeros(rows, device):
+        return torch.zeros((rows, 32), dtype=torch.int32)
+
+    @staticmethod
+    def snapshot(x):
+        return x.clone()
+
+    @staticmethod
+    def tree(root):
+        return OracleTree(root)
+
+    @staticmethod
+    def collect(tree):
+        return int(tree.fallback.item())
+
+    default_ball = staticmethod(_ball_scan)
+    default_nn = staticmethod(_nn_scan)
+
+
+class OracleSession(QuerySession):
+    _ops_class = OracleOps
+
+
+def make_oracle_session(threshold):
+    return OracleSession(threshold=threshold)

@@ -1,0 +1,37 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Extract the reference's committed query-session golden records.
+
+Reads ``data/query_session/correctness.json`` of the GSA reference checkout
+(default ``/root/reference``) and writes ``query_session_correctness.json``
+beside this script: for each of the 94 calls of the reference test
+``tests/check_queries.py`` its op, label, sizes, radius, K, the SHA-256 of
+the int32 output rows (radius calls) and the session statistics after the
+call.  The reference checkout is only needed to regenerate the fixture; the
+tests read the committed fixture.
+
+Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
+"""
+
+import json
+import sys
+from pathlib import Path
+
+root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+src = json.loads((root / "data/query_session/correctness.json").read_text())
+keep = ("op", "label", "n", "q", "r", "k", "ids_sha256", "stats")
+records = [{k: r[k] for k in keep if k in r} for r in src["records"]]
+assert len(records) == src["calls"] == 94
+out = Path(__file__).with_name("query_session_correctness.json")
+out.write_text(
+    json.dumps(
+        {
+            "source": "GSA data/query_session/correctness.json (reference run of tests/check_queries.py)",
+            "seed": 20261111,
+            "calls": len(records),
+            "records": records,
+        },
+        indent=1,
+    )
+    + "\n"
+)
+print(f"wrote {out} ({len(records)} records)")
