@@ -1,0 +1,535 @@
+#!/usr/bin/env python
+# SPDX-License-Identifier: Apache-2.0
+"""Exact radius + 3NN query throughput on B200; prints one JSON line.
+
+Workload (weak scaling, scenes sharded by rank, no data-path collective):
+each GPU answers the PointNeXt-shaped query hierarchy of 64 FPS-ordered
+synthetic room scenes of 24,000 points (seeds rank*64 + i): per scene,
+prefixes 24000/6000/1500/375/94, radius r = 0.1/0.2/0.4/0.8 with K = 32
+(31,875 computed rows), the down-sampling rows served by the reuse cache
+after its value checks (7,969 rows) and 3NN on every decoder stage (31,875
+rows).  Unit: answered query rows per second, all GPUs together.
+
+* ``value``: one step = build the prefix forest of the rank's scenes and run
+  every stage (``gsa_b200.hierarchy.Batch``), inputs resident in HBM; device
+  time from CUDA events per step, L2 flushed (256 MiB write) between steps
+  outside the timed events; max over ranks.
+* ``e2e``: the same rows through the drop-in ``QuerySession`` API, one scene
+  at a time, points copied from pinned host memory and every output row
+  copied back to pinned host memory inside the timed region.
+  ``e2e_batched``: the same with the batched ``Forest`` engine.
+* ``roofline``: the query kernel with the largest share of step time,
+  algorithmic bytes (radius 12 + 4K B per query, 3NN 36 B per query) over its
+  measured time, against the measured HBM copy bandwidth.
+* ``cpu_baseline``: the NumPy oracle (a port of the reference's test oracle)
+  on one scene, one core, rank 0 at N=1.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle port) on
+all host cores on the same workload and exits; under torchrun only rank 0
+runs it.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "exact radius+3NN queries/sec at 1/2/4/8 B200; % of HBM roofline"
+UNIT = "queries/s"
+SCENES = 64
+SIZES = (24000, 6000, 1500, 375, 94)
+RADII = (0.1, 0.2, 0.4, 0.8)
+K = 32
+FALLBACK_HBM_GBS = 6650.0
+
+
+def rows_per_scene():
+    return sum(SIZES[:4]), sum(SIZES[1:5]), sum(SIZES[:4])
+
+
+def config(scenes):
+    ball, hit, nn = rows_per_scene()
+    return {
+        "workload": f"room hierarchy, {scenes} FPS-ordered scenes x {SIZES[0]} points per GPU",
+        "scenes_per_gpu": scenes,
+        "scene_seeds": "rank*scenes + i",
+        "points_per_scene": SIZES[0],
+        "prefixes": list(SIZES),
+        "radii": list(RADII),
+        "k": K,
+        "rows_per_scene": {"radius_computed": ball, "reuse_hits": hit, "nn3": nn},
+        "parallelism": "scene-sharded, one process per GPU",
+        "l2": "flushed between timed steps (256 MiB write, outside the step events)",
+    }
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--scenes", type=int, default=SCENES)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------
+# reference arm: the oracle port on all host cores
+
+
+def _ref_worker_init():
+    os.environ["OMP_NUM_THREADS"] = "1"
+
+
+def _ref_scene(seed):
+    from gsa_b200 import scenes
+    from oracle import fps
+
+    p, start = scenes.room(seed, n=SIZES[0])
+    return p[fps.fps_order(p, start)]
+
+
+def _ref_step(args):
+    seed, fraction = args
+    from oracle import numpy_oracle as orc
+
+    P = _ref_scene_cache.get(seed)
+    if P is None:
+        P = _ref_scene_cache[seed] = _ref_scene(seed)
+    t0 = time.perf_counter()
+    _, rows = orc.hierarchy_oracle(P, SIZES, RADII, K, fraction)
+    return rows, time.perf_counter() - t0
+
+
+_ref_scene_cache = {}
+
+
+def run_reference(args, rank, world):
+    import multiprocessing as mp
+
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    workers = max(1, min(cores, args.scenes))
+    fraction = 0.25
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers, initializer=_ref_worker_init) as pool:
+        seeds = list(range(workers))
+        pool.map(_ref_step, [(s, 0.001) for s in seeds])  # build each worker's scene (untimed)
+        for _ in range(args.warmup):
+            pool.map(_ref_step, [(s, fraction) for s in seeds])
+        total_rows, total_t = 0, 0.0
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            res = pool.map(_ref_step, [(s, fraction) for s in seeds])
+            total_t += time.perf_counter() - t0
+            total_rows += sum(r for r, _ in res)
+    value = total_rows / total_t
+    sample = (
+        f"{workers} scenes per step, one per process, each the first {fraction:.0%} of every "
+        f"hierarchy call's queries (NumPy oracle port, spawn pool)"
+    )
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total_t / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": config(args.scenes),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# our arm
+
+
+class Clocks:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons."""
+
+    FIELDS = [
+        "uuid",
+        "clocks.sm",
+        "clocks.max.sm",
+        "power.draw",
+        "clocks_event_reasons.hw_slowdown",
+        "clocks_event_reasons.hw_thermal_slowdown",
+        "clocks_event_reasons.sw_thermal_slowdown",
+        "clocks_event_reasons.sw_power_cap",
+    ]
+
+    def __init__(self, torch, device):
+        self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file,
+                stderr=subprocess.DEVNULL,
+            )
+        except OSError as e:
+            self.proc = None
+            self.error = str(e)
+
+    def stop(self):
+        if self.proc is None:
+            return {"error": getattr(self, "error", "nvidia-smi unavailable")}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) != len(self.FIELDS) or cols[0].replace("GPU-", "") not in self.uuid.replace("GPU-", ""):
+                continue
+            try:
+                sm.append(float(cols[1]))
+                mx.append(float(cols[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, cols[4:]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        if not sm:
+            return {"error": "no samples"}
+        return {
+            "sm_mhz": statistics.median(sm),
+            "sm_max_mhz": max(mx),
+            "samples": len(sm),
+            "reasons": sorted(reasons),
+        }
+
+
+def launch_total():
+    import ctypes
+
+    from gsa_b200 import _library
+
+    tot = 0
+    for name in ("gsa_bvh", "reference_queries"):
+        lib = _library.load(name)
+        v = ctypes.c_ulonglong()
+        lib.launch_counter.argtypes = [ctypes.POINTER(ctypes.c_ulonglong)]
+        lib.launch_counter(ctypes.byref(v))
+        tot += v.value
+    return tot
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dram_bytes_per_query():
+    """Measured DRAM bytes per radius query from the committed ncu summary."""
+    p = ROOT / "profiles" / "radius_kernel_room64.md"
+    try:
+        for line in p.read_text().splitlines():
+            if line.strip().startswith("dram_bytes_per_query:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from gsa_b200 import QuerySession, hierarchy as hz, scenes
+
+    dev = torch.device("cuda", local)
+    S = args.scenes
+    seeds = [rank * S + i for i in range(S)]
+    X = scenes.room_batch(seeds)
+    eng = hz.Batch(SIZES, RADII)
+    out = eng.allocate(S, dev)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    for _ in range(max(3, args.warmup)):
+        eng.run(X, out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    clocks = Clocks(torch, dev)
+    launches0 = launch_total()
+    clocks.start()
+    records = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        flush.zero_()
+        start = torch.cuda.Event(enable_timing=True)
+        marks = []
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            marks.append((name, e))
+
+        start.record()
+        eng.run(X, out, mark)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        records.append((start, marks, end))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop()
+    launches = launch_total() - launches0
+
+    step_ms = [s.elapsed_time(e) for s, _, e in records]
+    phase = {}
+    for s, marks, _ in records:
+        prev = s
+        for name, e in marks:
+            key = name.rstrip("0123456789")
+            phase[key] = phase.get(key, 0.0) + prev.elapsed_time(e)
+            prev = e
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ball_rows, hit_rows, nn_rows = rows_per_scene()
+    rows = ball_rows + hit_rows + nn_rows
+    value = world * S * rows * args.steps / (max_ms / 1000.0)
+
+    # roofline of the dominant query kernel
+    peak, peak_kind = hbm_peak()
+    radius_bytes = args.steps * S * ball_rows * (12 + 4 * K)
+    nn_bytes = args.steps * S * nn_rows * 36
+    cands = {
+        "radius_kernel": (phase.get("ball", 0.0), radius_bytes, 12 + 4 * K),
+        "knn3_kernel": (phase.get("nn", 0.0), nn_bytes, 36),
+    }
+    name = max(cands, key=lambda k: cands[k][0])
+    ms, nbytes, per_query = cands[name]
+    achieved = nbytes / (ms / 1000.0) / 1e9
+    dbq = dram_bytes_per_query() if name == "radius_kernel" else None
+    launches_per_step = 4
+    traffic = None if dbq is None else dbq * S * ball_rows / launches_per_step
+    roofline = {
+        "bound": "hbm",
+        "kernel": name,
+        "achieved": achieved,
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": achieved / peak,
+        "traffic": traffic,
+        "peak_source": f"{peak_kind} HBM copy bandwidth",
+        "algorithmic_bytes_per_query": per_query,
+        "note": "achieved = algorithmic bytes of all launches / their summed CUDA-event time",
+    }
+
+    result_sum = torch.zeros(1, dtype=torch.int64, device=dev)
+    for key, v in out.items():
+        if key.startswith(("ball", "hit", "nni")):
+            result_sum += v.to(torch.int64).sum()
+    gathered = [torch.zeros(2, dtype=torch.int64, device=dev) for _ in range(world)]
+    mine = torch.tensor([S * rows, 0], dtype=torch.int64, device=dev)
+    mine[1] = result_sum[0]
+    if world > 1:
+        dist.all_gather(gathered, mine)
+    else:
+        gathered = [mine]
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": config(S),
+        "roofline": roofline,
+        "phases_ms_per_step": {k: v / args.steps for k, v in phase.items()},
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps,
+        "clocks": clock_info,
+        "rank_rows_checksums": [g.tolist() for g in gathered],
+    }
+
+    if not args.no_e2e:
+        line["e2e"], line["e2e_batched"] = e2e(args, X, eng, out, world, dev)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out, S)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def e2e(args, X, eng, out, world, dev):
+    """End-to-end rows/s through the public APIs with pinned host buffers."""
+    import torch
+    import torch.distributed as dist
+
+    from gsa_b200 import QuerySession, hierarchy as hz
+
+    S = X.shape[0]
+    host_x = X.cpu().pin_memory()
+    ball_rows, hit_rows, nn_rows = rows_per_scene()
+    rows = ball_rows + hit_rows + nn_rows
+    steps = max(1, min(args.steps, 3))
+
+    # drop-in QuerySession, one scene at a time
+    host_out = None
+    ms = 0.0
+    d2h = 0
+    for step in range(steps + 1):  # first pass warms allocator and pinned buffers
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        d2h = 0
+        for i in range(S):
+            x = host_x[i].to(dev, non_blocking=True)
+            with QuerySession() as s:
+                res = hz.run_session(s, x, SIZES, RADII)
+            if host_out is None:
+                host_out = [{k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in res.items()} for _ in range(S)]
+            for k, v in res.items():
+                host_out[i][k].copy_(v, non_blocking=True)
+                d2h += v.numel() * v.element_size()
+        t1.record()
+        torch.cuda.synchronize()
+        if step:
+            ms += t0.elapsed_time(t1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    session = {
+        "value": world * S * rows * steps / (float(t.item()) / 1000.0),
+        "unit": UNIT,
+        "h2d_bytes_per_step": int(host_x.numel() * 4),
+        "d2h_bytes_per_step": int(d2h),
+        "api": "gsa_b200.QuerySession (drop-in for gsa.QuerySession), one scene per session, threshold 1024",
+        "steps": steps,
+    }
+
+    # batched Forest engine
+    keys = [k for k in out if k.startswith(("ball", "hit", "nn"))]
+    host_b = {k: torch.empty(out[k].shape, dtype=out[k].dtype, pin_memory=True) for k in keys}
+    xb = torch.empty_like(X)
+    ms = 0.0
+    for step in range(steps + 1):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        xb.copy_(host_x, non_blocking=True)
+        eng.run(xb, out)
+        for k in keys:
+            host_b[k].copy_(out[k], non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        if step:
+            ms += t0.elapsed_time(t1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    batched = {
+        "value": world * S * rows * steps / (float(t.item()) / 1000.0),
+        "unit": UNIT,
+        "h2d_bytes_per_step": int(host_x.numel() * 4),
+        "d2h_bytes_per_step": int(sum(v.numel() * v.element_size() for v in host_b.values())),
+        "api": "gsa_b200.hierarchy.Batch over gsa_b200.Forest (batched C ABI)",
+        "steps": steps,
+    }
+    return session, batched
+
+
+def cpu_baseline(P, out, S):
+    """The NumPy oracle on scene 0 (one core); also checks scene 0's rows."""
+    from oracle import numpy_oracle as orc
+
+    t0 = time.perf_counter()
+    ref, rows = orc.hierarchy_oracle(P, SIZES, RADII, K)
+    dt = time.perf_counter() - t0
+    ok = True
+    for key, v in ref.items():
+        n = v.shape[0]
+        got = out[key][:n].cpu().numpy()
+        import numpy as np
+
+        ok &= bool(np.array_equal(got, v))
+    return {
+        "value": rows / dt,
+        "unit": UNIT,
+        "cores": 1,
+        "kind": "port",
+        "sample": f"one full scene (seed 0, {rows} rows), NumPy oracle port, single process",
+        "seconds": dt,
+        "gpu_rows_equal_oracle": ok,
+    }
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

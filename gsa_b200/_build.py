@@ -34,13 +34,11 @@ FLAGS = [
     "-I" + str(ROOT / "include"),
 ]
 
+_BVH = ["launches.cu", "pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"]
 LIBS = {
-    "gsa_bvh": (["pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"], []),
-    "reference_queries": (["reference_queries.cu"], []),
-    "gsa_bvh_stack4": (
-        ["pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"],
-        ["-DGSA_STACK=4"],
-    ),
+    "gsa_bvh": (_BVH, []),
+    "reference_queries": (["launches.cu", "reference_queries.cu"], []),
+    "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"]),
 }
 
 

@@ -611,6 +611,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
                                         kSortTile);
     qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
                                                hist, max_tiles, f->qorder);
+    // upload chunks + bounds + morton + 8 x 3 sort + karras + refit + 3 qorder
+    count_launches((B + 255) / 256 + 2 + 24 + 2 + 3);
     e = cudaGetLastError();
   }
   void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, range, parent,

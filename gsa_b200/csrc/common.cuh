@@ -10,6 +10,9 @@
 
 namespace gsa {
 
+// Kernel launches issued by this library (read with launch_counter()).
+void count_launches(int n = 1);
+
 constexpr int kMaxLevels = 4;   // prefixes n, n/4, n/16, n/64
 constexpr int kMaxLeaf = 32;    // leaf point count fits 5 bits
 constexpr int kMaxPoints = 1 << 26;  // leaf start fits 26 bits

@@ -42,16 +42,24 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
                          int leaf, cudaStream_t s, Forest** out);
 cudaError_t free_forest(Forest* f, cudaStream_t s);
 
-// Query launchers (query.cu).  For a forest, `qseg` (device) and
-// `qseg_host` (host) hold B+1 query offsets and each tree uses its own level
-// size as support prefix; for a single tree both are null and `nq` queries
-// with the explicit support prefix `m` are used.
-cudaError_t launch_radius(const Forest& f, const float* q, const int* qseg,
-                          const int* qseg_host, int nq, int m, int level,
-                          float radius, int ns, int* out, int* fallback,
-                          cudaStream_t s);
-cudaError_t launch_knn3(const Forest& f, const float* q, const int* qseg,
-                        const int* qseg_host, int nq, int m, int level,
-                        float* d, int* ix, int* fallback, cudaStream_t s);
+// Queries of one launch.  Single tree: qseg == qseg_host == qstart == null,
+// `nq` queries at q[0..nq).  Forest: tree b answers qseg[b+1]-qseg[b] queries
+// read from rows q[qstart[b]..) (qstart null: from row qseg[b]) and written to
+// output rows qseg[b]..; qseg_host is the host copy of qseg.
+struct QuerySet {
+  const float* q = nullptr;
+  const int* qstart = nullptr;
+  const int* qseg = nullptr;
+  const int* qseg_host = nullptr;
+  int nq = 0;
+  int m = 0;      // support prefix of every tree; 0 = that tree's level size
+  int level = -1; // bounds level; -1 = all points
+};
+
+// Query launchers (query.cu).
+cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
+                          int ns, int* out, int* fallback, cudaStream_t s);
+cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
+                        int* fallback, cudaStream_t s);
 
 }  // namespace gsa

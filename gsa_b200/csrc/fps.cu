@@ -95,6 +95,7 @@ GSA_API int fps_order(int b, int n, const float* x, const int* start,
   cudaError_t e = cudaFuncSetAttribute(
       fps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e) return e;
+  count_launches();
   fps_kernel<<<b, kFpsThreads, smem, (cudaStream_t)stream>>>(n, x, start,
                                                               order);
   return cudaGetLastError();

@@ -43,8 +43,12 @@ GSA_API int query_bvh(void* handle, const float* q, int nq, int m, int level,
     return -2;
   if (!nq) return 0;
   if (!q || !d || !ix || !fallback) return -2;
-  return as_code(launch_knn3(*f, q, nullptr, nullptr, nq, m, level, d, ix,
-                             fallback, (cudaStream_t)stream));
+  QuerySet qs;
+  qs.q = q;
+  qs.nq = nq;
+  qs.m = m;
+  qs.level = level;
+  return as_code(launch_knn3(*f, qs, d, ix, fallback, (cudaStream_t)stream));
 }
 
 GSA_API int query_ball_bvh(void* handle, const float* q, int nq, int m,
@@ -56,8 +60,13 @@ GSA_API int query_ball_bvh(void* handle, const float* q, int nq, int m,
     return -2;
   if (!nq) return 0;
   if (!q || !out || !fallback) return -2;
-  return as_code(launch_radius(*f, q, nullptr, nullptr, nq, m, level, radius,
-                               ns, out, fallback, (cudaStream_t)stream));
+  QuerySet qs;
+  qs.q = q;
+  qs.nq = nq;
+  qs.m = m;
+  qs.level = level;
+  return as_code(
+      launch_radius(*f, qs, radius, ns, out, fallback, (cudaStream_t)stream));
 }
 
 GSA_API int free_bvh(void* handle, int async_free, void* stream) {
@@ -97,44 +106,62 @@ GSA_API int build_bvh_batch(const float* x, const int* seg, int b, int prefix,
 }
 
 namespace {
-int check_batch(const Forest* f, const int* qseg, const int* qseg_host,
+// Every tree with queries must have a support prefix of at least min_m
+// points that its level's bounds cover.
+int check_batch(const Forest* f, const int* qseg, const int* qseg_host, int m,
                 int level, int min_m) {
-  if (!f || !qseg || !qseg_host || level < -1 || level >= f->levels) return -2;
+  if (!f || !qseg || !qseg_host || m < 0 || level < -1 || level >= f->levels)
+    return -2;
   if (qseg_host[0] != 0) return -2;
   for (int b = 0; b < f->B; ++b) {
     if (qseg_host[b + 1] < qseg_host[b]) return -2;
-    if (qseg_host[b + 1] > qseg_host[b] &&
-        level_size(f->hdesc[b].n, level) < min_m)
-      return -2;
+    if (qseg_host[b + 1] == qseg_host[b]) continue;
+    int size = level_size(f->hdesc[b].n, level);
+    int mb = m ? m : size;
+    if (mb < min_m || mb > size) return -2;
   }
   return 0;
 }
+
+QuerySet batch_set(const float* q, const int* qstart, const int* qseg,
+                   const int* qseg_host, int m, int level) {
+  QuerySet qs;
+  qs.q = q;
+  qs.qstart = qstart;
+  qs.qseg = qseg;
+  qs.qseg_host = qseg_host;
+  qs.m = m;
+  qs.level = level;
+  return qs;
+}
 }  // namespace
 
-GSA_API int query_ball_bvh_batch(void* handle, const float* q, const int* qseg,
-                                 const int* qseg_host, int level, float radius,
-                                 int ns, int* out, int* fallback,
+GSA_API int query_ball_bvh_batch(void* handle, const float* q,
+                                 const int* qstart, const int* qseg,
+                                 const int* qseg_host, int m, int level,
+                                 float radius, int ns, int* out, int* fallback,
                                  void* stream) {
   Forest* f = (Forest*)handle;
   if (ns < 1 || ns > 32) return -2;
-  int c = check_batch(f, qseg, qseg_host, level, 1);
+  int c = check_batch(f, qseg, qseg_host, m, level, 1);
   if (c) return c;
   if (qseg_host[f->B] == 0) return 0;
   if (!q || !out || !fallback) return -2;
-  return as_code(launch_radius(*f, q, qseg, qseg_host, 0, 0, level, radius, ns,
-                               out, fallback, (cudaStream_t)stream));
+  return as_code(launch_radius(*f, batch_set(q, qstart, qseg, qseg_host, m, level),
+                               radius, ns, out, fallback, (cudaStream_t)stream));
 }
 
-GSA_API int query_bvh_batch(void* handle, const float* q, const int* qseg,
-                            const int* qseg_host, int level, float* d, int* ix,
-                            int* fallback, void* stream) {
+GSA_API int query_bvh_batch(void* handle, const float* q, const int* qstart,
+                            const int* qseg, const int* qseg_host, int m,
+                            int level, float* d, int* ix, int* fallback,
+                            void* stream) {
   Forest* f = (Forest*)handle;
-  int c = check_batch(f, qseg, qseg_host, level, 3);
+  int c = check_batch(f, qseg, qseg_host, m, level, 3);
   if (c) return c;
   if (qseg_host[f->B] == 0) return 0;
   if (!q || !d || !ix || !fallback) return -2;
-  return as_code(launch_knn3(*f, q, qseg, qseg_host, 0, 0, level, d, ix,
-                             fallback, (cudaStream_t)stream));
+  return as_code(launch_knn3(*f, batch_set(q, qstart, qseg, qseg_host, m, level),
+                             d, ix, fallback, (cudaStream_t)stream));
 }
 
 GSA_API int bvh_info(void* handle, int* trees, int* points, int* levels,

@@ -34,9 +34,10 @@ constexpr int kQWarps = kQThreads / 32;
 struct QArgs {
   ForestView f;
   const float* q;
-  const int* qseg;  // per-tree query offsets (device) or null
-  int nq;           // single tree: number of queries
-  int m;            // single tree: support prefix; 0 = level size
+  const int* qstart;  // per-tree first input query row (device) or null
+  const int* qseg;    // per-tree output row offsets (device) or null
+  int nq;             // single tree: number of queries
+  int m;              // support prefix for every tree; 0 = level size
   int level;        // bounds level, -1 = all points (level 0 data)
   float radius;
   int ns;
@@ -63,7 +64,7 @@ __device__ __forceinline__ int level_offset(int n, int l) {
 }
 
 struct Slot {
-  int qbase, Q, m, slots, lev;
+  int qbase, qin, Q, m, slots, lev;
   const int* order;
 };
 
@@ -71,6 +72,7 @@ __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
                                            int b) {
   Slot s;
   s.qbase = a.qseg ? a.qseg[b] : 0;
+  s.qin = a.qstart ? a.qstart[b] : s.qbase;
   s.Q = a.qseg ? a.qseg[b + 1] - s.qbase : a.nq;
   s.m = a.m > 0 ? a.m : level_size(d.n, a.level);
   s.lev = a.level < 0 ? 0 : a.level;
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(kQThreads)
   bool active = qi >= 0;
   float px = 0.f, py = 0.f, pz = 0.f;
   if (active) {
-    const float* qp = a.q + 3ll * (s.qbase + qi);
+    const float* qp = a.q + 3ll * (s.qin + qi);
     px = qp[0];
     py = qp[1];
     pz = qp[2];
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(kQThreads)
   bool active = qi >= 0;
   float px = 0.f, py = 0.f, pz = 0.f;
   if (active) {
-    const float* qp = a.q + 3ll * (s.qbase + qi);
+    const float* qp = a.q + 3ll * (s.qin + qi);
     px = qp[0];
     py = qp[1];
     pz = qp[2];
@@ -353,15 +355,15 @@ long long max_slots(const Forest& f, const int* qseg_host, int nq) {
   return best;
 }
 
-QArgs make_args(const Forest& f, const float* q, const int* qseg, int nq,
-                int m, int level) {
+QArgs make_args(const Forest& f, const QuerySet& qs) {
   QArgs a;
   a.f = f.view();
-  a.q = q;
-  a.qseg = qseg;
-  a.nq = nq;
-  a.m = m;
-  a.level = level;
+  a.q = qs.q;
+  a.qstart = qs.qstart;
+  a.qseg = qs.qseg;
+  a.nq = qs.nq;
+  a.m = qs.m;
+  a.level = qs.level;
   a.radius = 0.f;
   a.ns = 0;
   a.out = nullptr;
@@ -372,32 +374,31 @@ QArgs make_args(const Forest& f, const float* q, const int* qseg, int nq,
 
 }  // namespace
 
-cudaError_t launch_radius(const Forest& f, const float* q, const int* qseg,
-                          const int* qseg_host, int nq, int m, int level,
-                          float radius, int ns, int* out, int* fallback,
-                          cudaStream_t s) {
-  QArgs a = make_args(f, q, qseg, nq, m, level);
+cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
+                          int ns, int* out, int* fallback, cudaStream_t s) {
+  QArgs a = make_args(f, qs);
   a.radius = radius;
   a.ns = ns;
   a.out = out;
   a.fallback = fallback;
-  long long slots = max_slots(f, qseg_host, nq);
+  long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
   dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
+  count_launches();
   radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_knn3(const Forest& f, const float* q, const int* qseg,
-                        const int* qseg_host, int nq, int m, int level,
-                        float* d, int* ix, int* fallback, cudaStream_t s) {
-  QArgs a = make_args(f, q, qseg, nq, m, level);
+cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
+                        int* fallback, cudaStream_t s) {
+  QArgs a = make_args(f, qs);
   a.dout = d;
   a.out = ix;
   a.fallback = fallback;
-  long long slots = max_slots(f, qseg_host, nq);
+  long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
   dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
+  count_launches();
   knn3_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
   return cudaGetLastError();
 }

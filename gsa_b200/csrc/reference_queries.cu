@@ -164,6 +164,7 @@ GSA_API int ball(int b, int n, int m, float r, int ns, const float* q,
   if (!b || !m) return 0;
   if (!q || !idx || (n && !x)) return -2;
   dim3 grid((m + kThreads - 1) / kThreads, b);
+  count_launches();
   ball_scan_kernel<<<grid, kThreads, 0, (cudaStream_t)s>>>(n, m, r, ns, q, x,
                                                            idx);
   return cudaGetLastError();
@@ -176,6 +177,7 @@ GSA_API int nn3(int b, int n, int m, const float* q, const float* x, float* d,
   if (!b || !n) return 0;
   if (!q || !d || !idx || (m && !x)) return -2;
   dim3 grid((n + kThreads - 1) / kThreads, b);
+  count_launches();
   nn3_scan_kernel<<<grid, kThreads, 0, (cudaStream_t)s>>>(n, m, q, x, d, idx);
   return cudaGetLastError();
 }

@@ -93,6 +93,45 @@ __global__ void __launch_bounds__(256)
   copy_rows(src, src_ld, rows, cols, dst);
 }
 
+// Pair p = (a + p*a_stride, b + p*b_stride), nfloat values each.
+__global__ void __launch_bounds__(256)
+    mismatch_strided_kernel(const float* a, long long a_stride, const float* b,
+                            long long b_stride, long long n, int* flags,
+                            int flag_stride) {
+  long long p = blockIdx.y;
+  const float* u = a + p * a_stride;
+  const float* v = b + p * b_stride;
+  bool diff = false;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (((((uintptr_t)u) | ((uintptr_t)v)) & 15) == 0) {
+    const float4* u4 = reinterpret_cast<const float4*>(u);
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    long long n4 = n >> 2;
+    for (long long i = t; i < n4; i += stride) {
+      float4 x = __ldcs(u4 + i), y = __ldcs(v4 + i);
+      diff |= (x.x != y.x) | (x.y != y.y) | (x.z != y.z) | (x.w != y.w);
+    }
+    for (long long i = (n4 << 2) + t; i < n; i += stride) diff |= u[i] != v[i];
+  } else {
+    for (long long i = t; i < n; i += stride) diff |= u[i] != v[i];
+  }
+  if (__any_sync(kFull, diff) && (threadIdx.x & 31) == 0)
+    flags[p * flag_stride] = 1;
+}
+
+// Scene i copies its rows unless its support or query flag is set.
+__global__ void __launch_bounds__(256)
+    reuse_rows_batch_kernel(const int* src, long long src_stride, int src_ld,
+                            const int* flags, int rows, int cols, int* dst,
+                            long long dst_stride, int* hits) {
+  long long i = blockIdx.y;
+  bool hit = !flags || !(flags[2 * i] | flags[2 * i + 1]);
+  if (hits && blockIdx.x == 0 && threadIdx.x == 0) hits[i] = hit;
+  if (hit)
+    copy_rows(src + i * src_stride, src_ld, rows, cols, dst + i * dst_stride);
+}
+
 inline unsigned copy_blocks(long long work) {
   long long b = (work + 255) / 256;
   return (unsigned)std::max<long long>(1, std::min<long long>(b, 148 * 8));
@@ -125,6 +164,7 @@ GSA_API int coords_mismatch(int count, const float* const* a,
       if (on) longest = std::max(longest, c.n[i]);
     }
     dim3 grid(copy_blocks((longest + 3) / 4), k);
+    count_launches();
     mismatch_kernel<<<grid, 256, 0, s>>>(c, flags + c0);
   }
   return cudaGetLastError();
@@ -140,6 +180,7 @@ GSA_API int reuse_rows(int count, const int* const* cached, const int* flags,
   RowChunk r;
   for (int i = 0; i < kMaxPairs; ++i) r.src[i] = i < count ? cached[i] : nullptr;
   cudaStream_t s = (cudaStream_t)stream;
+  count_launches();
   reuse_rows_kernel<<<copy_blocks(((long long)rows * cols + 3) / 4), 256, 0,
                       s>>>(r, count, flags, src_ld, rows, cols, dst, hit);
   return cudaGetLastError();
@@ -152,7 +193,45 @@ GSA_API int gather_rows(const int* src, int src_ld, int rows, int cols,
     return -2;
   if (!rows) return 0;
   cudaStream_t s = (cudaStream_t)stream;
+  count_launches();
   gather_rows_kernel<<<copy_blocks(((long long)rows * cols + 3) / 4), 256, 0,
                        s>>>(src, src_ld, rows, cols, dst);
+  return cudaGetLastError();
+}
+
+// See include/gsa_bvh.h.
+GSA_API int coords_mismatch_strided(int count, const float* a,
+                                    long long a_stride, const float* b,
+                                    long long b_stride, long long nfloat,
+                                    int* flags, int flag_stride,
+                                    void* stream) {
+  if (count < 0 || nfloat < 0 || flag_stride < 1 || count > 65535) return -2;
+  if (!count) return 0;
+  if (!a || !b || !flags) return -2;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemset2DAsync(flags, sizeof(int) * flag_stride, 0,
+                                    sizeof(int), count, s);
+  if (e) return e;
+  if (!nfloat) return 0;
+  dim3 grid(copy_blocks((nfloat + 3) / 4), count);
+  count_launches();
+  mismatch_strided_kernel<<<grid, 256, 0, s>>>(a, a_stride, b, b_stride, nfloat,
+                                               flags, flag_stride);
+  return cudaGetLastError();
+}
+
+// See include/gsa_bvh.h.
+GSA_API int reuse_rows_batch(int count, const int* src, long long src_stride,
+                             int src_ld, const int* flags, int rows, int cols,
+                             int* dst, long long dst_stride, int* hits,
+                             void* stream) {
+  if (count < 0 || count > 65535 || rows < 0 || cols < 1 || src_ld < cols)
+    return -2;
+  if (!count) return 0;
+  if (!src || !dst) return -2;
+  dim3 grid(copy_blocks(((long long)rows * cols + 3) / 4), count);
+  count_launches();
+  reuse_rows_batch_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      src, src_stride, src_ld, flags, rows, cols, dst, dst_stride, hits);
   return cudaGetLastError();
 }

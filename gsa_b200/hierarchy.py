@@ -1,0 +1,129 @@
+# SPDX-License-Identifier: Apache-2.0
+"""The PointNeXt-shaped query hierarchy, per scene and for scene batches.
+
+A scene's support ``P`` is farthest-point ordered; its sampled levels are the
+prefixes ``P_s = P[:sizes[s]]`` (ratio 4).  Per encoder stage ``s`` the
+hierarchy runs, with K = 32 (``data/summaries`` call structure of GSA):
+
+* ``ball(P_s -> P_s, r_s)``      computed self-query rows;
+* ``ball(P_{s+1} -> P_s, r_s)``  down-sampling rows, answered from the
+  self-query rows after the support / query-prefix value checks (reuse hit);
+
+and per decoder stage ``nn(P_s -> P_{s+1})`` for s = 3..0.
+
+``run_session`` issues exactly these calls through the drop-in
+``QuerySession``.  ``Batch`` runs the same hierarchy for B equally sized
+scenes with one launch per build step / query stage (forest build, radius
+and 3NN traversal of every scene, one batched value check and one batched
+row gather per stage); its outputs equal ``run_session``'s for every scene.
+"""
+
+import ctypes
+
+import torch
+
+from . import runtime as er
+from .forest import Forest
+
+ROOM_SIZES = (24000, 6000, 1500, 375, 94)
+ROOM_RADII = (0.1, 0.2, 0.4, 0.8)
+LARGE_SIZES = (1_000_000, 250_000, 62_500, 15_625, 3_906)
+LARGE_RADII = (0.05, 0.1, 0.2, 0.4)
+K = 32
+
+_P, _I, _LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+er.lib.coords_mismatch_strided.argtypes = [_I, _P, _LL, _P, _LL, _LL, _P, _I, _P]
+er.lib.coords_mismatch_strided.restype = _I
+er.lib.reuse_rows_batch.argtypes = [_I, _P, _LL, _I, _P, _I, _I, _P, _LL, _P, _P]
+er.lib.reuse_rows_batch.restype = _I
+
+
+def unit_counts(sizes):
+    """Rows answered per scene: (computed radius, reuse hits, 3NN)."""
+    return sum(sizes[:4]), sum(sizes[1:5]), sum(sizes[:4])
+
+
+def run_session(session, P, sizes=ROOM_SIZES, radii=ROOM_RADII):
+    """Run the hierarchy on one scene through ``QuerySession``; returns the
+    outputs as a dict of device tensors."""
+    out = {}
+    for s in range(4):
+        ps, pn = P[: sizes[s]], P[: sizes[s + 1]]
+        rows = torch.empty((sizes[s], K), dtype=torch.int32, device=P.device)
+        session.ball_into(ps, ps, radii[s], K, rows)
+        hits = torch.empty((sizes[s + 1], K), dtype=torch.int32, device=P.device)
+        session.ball_into(pn, ps, radii[s], K, hits)
+        out[f"ball{s}"], out[f"hit{s}"] = rows, hits
+    for s in range(3, -1, -1):
+        d = torch.empty((sizes[s], 3), device=P.device)
+        i = torch.empty((sizes[s], 3), dtype=torch.int32, device=P.device)
+        session.nn_into(P[: sizes[s]], P[: sizes[s + 1]], d, i)
+        out[f"nnd{s}"], out[f"nni{s}"] = d, i
+    return out
+
+
+class Batch:
+    """Hierarchy over B scenes of N points each, all on the device."""
+
+    def __init__(self, sizes=ROOM_SIZES, radii=ROOM_RADII, leaf=16):
+        self.sizes = tuple(sizes)
+        self.radii = tuple(radii)
+        self.leaf = leaf
+
+    def _level(self, size, n):
+        for level in range(4):
+            if size <= n >> (2 * level):
+                best = level
+        return best
+
+    def allocate(self, B, device):
+        """Output buffers of one run (reusable across runs)."""
+        z = {}
+        for s in range(4):
+            z[f"ball{s}"] = torch.empty((B * self.sizes[s], K), dtype=torch.int32, device=device)
+            z[f"hit{s}"] = torch.empty((B * self.sizes[s + 1], K), dtype=torch.int32, device=device)
+            z[f"nnd{s}"] = torch.empty((B * self.sizes[s], 3), device=device)
+            z[f"nni{s}"] = torch.empty((B * self.sizes[s], 3), dtype=torch.int32, device=device)
+        z["flags"] = torch.zeros(2 * B, dtype=torch.int32, device=device)
+        z["hits"] = torch.zeros(B, dtype=torch.int32, device=device)
+        z["snapshot"] = torch.empty((B, self.sizes[0], 3), device=device)
+        return z
+
+    def run(self, X, out=None, mark=None):
+        """X: CUDA float32 (B, N, 3), N == sizes[0], each scene FPS-ordered.
+        ``mark(name)``, if given, is called after each phase (e.g. to record
+        a CUDA event): build, ball<s>, reuse<s>, nn<s>."""
+        B, N = X.shape[0], X.shape[1]
+        if not (X.is_cuda and X.is_contiguous() and X.dtype == torch.float32 and N == self.sizes[0]):
+            raise ValueError("Batch.run needs contiguous CUDA FP32 (B, sizes[0], 3)")
+        out = out if out is not None else self.allocate(B, X.device)
+        mark = mark or (lambda name: None)
+        stream = er._stream()
+        snap = out["snapshot"]
+        snap.copy_(X)  # retained snapshot of every support, as the session keeps
+        forest = Forest(X.view(-1, 3), [i * N for i in range(B + 1)], prefix=True, leaf=self.leaf)
+        mark("build")
+        flags, hitflags = out["flags"], out["hits"]
+        for s in range(4):
+            n_s, n_q = self.sizes[s], self.sizes[s + 1]
+            rows = out[f"ball{s}"]
+            forest.ball_prefix(n_s, s, self.radii[s], K, rows)
+            mark(f"ball{s}")
+            # reuse admission: support P_s and query prefix P_{s+1} equal the
+            # retained snapshot, then gather the first n_q rows of each scene
+            er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, flags.data_ptr(), 2, stream))
+            er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, flags.data_ptr() + 4, 2, stream))
+            er.check(
+                er.lib.reuse_rows_batch(
+                    B, rows.data_ptr(), n_s * K, K, flags.data_ptr(), n_q, K,
+                    out[f"hit{s}"].data_ptr(), n_q * K, hitflags.data_ptr(), stream,
+                )
+            )
+            mark(f"reuse{s}")
+        for s in range(3, -1, -1):
+            m = self.sizes[s + 1]
+            level = self._level(m, N)
+            forest.query_prefix(self.sizes[s], level, out[f"nnd{s}"], out[f"nni{s}"], m=m if m != N >> (2 * level) else 0)
+            mark(f"nn{s}")
+        forest.close()
+        return out

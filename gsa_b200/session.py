@@ -29,22 +29,28 @@ from . import reference as rt
 _FLT_MAX = torch.finfo(torch.float32).max
 _MAX_DEVICE_CANDIDATES = 64
 
+_P, _I = ctypes.c_void_p, ctypes.c_int
+er.lib.coords_mismatch.argtypes = [_I, _P, _P, _P, _P, _P]
+er.lib.coords_mismatch.restype = _I
+er.lib.reuse_rows.argtypes = [_I, _P, _P, _I, _I, _I, _P, _P, _P]
+er.lib.reuse_rows.restype = _I
+er.lib.gather_rows.argtypes = [_P, _I, _I, _I, _P, _P]
+er.lib.gather_rows.restype = _I
+_pinned = {}
+
+
+def _pinned_flags(n):
+    """Process-wide pinned host buffer for reading comparison flags."""
+    buf = _pinned.get("flags")
+    if buf is None or buf.numel() < n:
+        buf = _pinned["flags"] = torch.empty(max(256, n), dtype=torch.int32, pin_memory=True)
+    return buf[:n]
+
 
 class _CudaOps:
     """Device side of the session: comparisons, row gathers, trees."""
 
     lib = er.lib
-
-    def __init__(self):
-        P, I = ctypes.c_void_p, ctypes.c_int
-        lib = self.lib
-        lib.coords_mismatch.argtypes = [I, P, P, P, P, P]
-        lib.coords_mismatch.restype = I
-        lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
-        lib.reuse_rows.restype = I
-        lib.gather_rows.argtypes = [P, I, I, I, P, P]
-        lib.gather_rows.restype = I
-        self.pinned = None
 
     @staticmethod
     def current():
@@ -82,10 +88,7 @@ class _CudaOps:
 
     def fetch(self, flags):
         """Read the flags on the host (the call's one synchronisation)."""
-        n = flags.numel()
-        if self.pinned is None or self.pinned.numel() < n:
-            self.pinned = torch.empty(max(n, 64), dtype=torch.int32, pin_memory=True)
-        host = self.pinned[:n]
+        host = _pinned_flags(flags.numel())
         host.copy_(flags, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return host.tolist()

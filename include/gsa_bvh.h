@@ -80,18 +80,24 @@ int pool_reset_peak(void);
 int build_bvh_batch(const float* x, const int* seg, int b, int prefix,
                     int leaf, void** out, void* stream);
 
-/* Radius query on every tree of a forest in one launch.  Queries of tree i
- * are q[qseg[i]..qseg[i+1]) (qseg on the device, qseg_host the same offsets
- * on the host); tree i uses support prefix m_i = n_i >> (2*level) (n_i for
- * level -1).  out rows follow the query rows. */
-int query_ball_bvh_batch(void* h, const float* q, const int* qseg,
-                         const int* qseg_host, int level, float radius,
-                         int ns, int* out, int* fallback, void* stream);
+/* Radius query on every tree of a forest in one launch.  Tree i answers
+ * qseg[i+1]-qseg[i] queries read from rows q[qstart[i]..) (qstart null: from
+ * row qseg[i]) and writes output rows qseg[i].. of out (ns ints per row).
+ * qstart and qseg are device int arrays, qseg_host the host copy of qseg
+ * (b+1 offsets from 0).  Tree i searches support IDs < m_i where m_i = m if
+ * m > 0, else its level size n_i >> (2*level) (n_i for level -1); m_i must
+ * not exceed that level size.  Passing q = the forest's own points and
+ * qstart = seg answers each scene's own prefix without copying it. */
+int query_ball_bvh_batch(void* h, const float* q, const int* qstart,
+                         const int* qseg, const int* qseg_host, int m,
+                         int level, float radius, int ns, int* out,
+                         int* fallback, void* stream);
 
-/* 3NN on every tree of a forest in one launch (same layout as above). */
-int query_bvh_batch(void* h, const float* q, const int* qseg,
-                    const int* qseg_host, int level, float* d, int* ix,
-                    int* fallback, void* stream);
+/* 3NN on every tree of a forest in one launch (same layout as above; every
+ * tree with queries needs m_i >= 3). */
+int query_bvh_batch(void* h, const float* q, const int* qstart,
+                    const int* qseg, const int* qseg_host, int m, int level,
+                    float* d, int* ix, int* fallback, void* stream);
 
 /* Trees, points, stored levels and leaf size of a handle (any may be null). */
 int bvh_info(void* h, int* trees, int* points, int* levels, int* leaf);
@@ -119,6 +125,28 @@ int reuse_rows(int count, const int* const* cached, const int* flags,
  * `out.copy_(result[:, :k])` of GSA gsa/session.py:128. */
 int gather_rows(const int* src, int src_ld, int rows, int cols, int* dst,
                 void* stream);
+
+/* Batched reuse check over `count` scenes in one launch: flags[p*flag_stride]
+ * = 0 when the nfloat values at a + p*a_stride and b + p*b_stride are all
+ * equal (IEEE ==), else 1; the other flag slots are untouched.  Batched form
+ * of the session's support/query snapshot comparisons (gsa/session.py:104-114)
+ * for scenes laid out at a fixed stride. */
+int coords_mismatch_strided(int count, const float* a, long long a_stride,
+                            const float* b, long long b_stride,
+                            long long nfloat, int* flags, int flag_stride,
+                            void* stream);
+
+/* Batched reuse gather: scene p < count copies
+ * src[p*src_stride + i*src_ld + j] to dst[p*dst_stride + i*cols + j]
+ * (i < rows, j < cols) when flags is null or flags[2p] == flags[2p+1] == 0,
+ * and writes 1 (copied) or 0 to hits[p] (may be null).  Batched form of the
+ * cache-hit copy of gsa/session.py:111. */
+int reuse_rows_batch(int count, const int* src, long long src_stride,
+                     int src_ld, const int* flags, int rows, int cols,
+                     int* dst, long long dst_stride, int* hits, void* stream);
+
+/* Total kernel launches this library has issued since it was loaded. */
+int launch_counter(unsigned long long* total);
 
 /* Farthest-point order of b scenes of n points each (x is [b][n][3]),
  * starting at start[b] (device int[b]); order is device int[b][n].  Ties pick

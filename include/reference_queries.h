@@ -34,6 +34,10 @@ int ball(int b, int n, int m, float r, int ns, const float* q, const float* x,
 int nn3(int b, int n, int m, const float* q, const float* x, float* d,
         int* idx, void* s);
 
+/* Extension (no counterpart in the reference): total kernel launches this
+ * library has issued since it was loaded. */
+int launch_counter(unsigned long long* total);
+
 #ifdef __cplusplus
 }
 #endif

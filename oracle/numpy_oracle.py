@@ -82,10 +82,23 @@ def ball_oracle(q, x, r, k):
     return result
 
 
-def _chunks(nq, nx, budget=1 << 25):
+def _chunks(nq, nx, budget=1 << 23):
     step = max(1, budget // max(1, nx))
     for s in range(0, nq, step):
         yield s, min(nq, s + step)
+
+
+def _distance_lean(q, x):
+    """Same values as :func:`distance` (same float32 operations in the same
+    order) without the (Q, N, 3) temporary."""
+    with np.errstate(over="ignore", under="ignore", invalid="ignore"):
+        d = q[:, None, 0] - x[None, :, 0]
+        acc = d * d
+        d = q[:, None, 1] - x[None, :, 1]
+        acc += d * d
+        d = q[:, None, 2] - x[None, :, 2]
+        acc += d * d
+        return acc
 
 
 def ball_oracle_fast(q, x, r, k):
@@ -99,7 +112,7 @@ def ball_oracle_fast(q, x, r, k):
     result = np.zeros((len(q), k), np.int32)
     r2 = radius_squared(r)
     for s, e in _chunks(len(q), len(x)):
-        mask = distance(q[s:e], x) < r2
+        mask = _distance_lean(q[s:e], x) < r2
         rank = np.cumsum(mask, axis=1, dtype=np.int32)
         keep = mask & (rank <= k)
         rows, cols = np.nonzero(keep)
@@ -156,7 +169,7 @@ def nn_oracle_fast(q, x):
     if len(q) == 0 or len(x) == 0:
         return ed, ei
     for s, e in _chunks(len(q), len(x)):
-        d = distance(q[s:e], x)
+        d = _distance_lean(q[s:e], x)
         d[~np.isfinite(d)] = np.inf
         rows = np.arange(e - s)
         for j in range(min(3, len(x))):
@@ -167,3 +180,25 @@ def nn_oracle_fast(q, x):
             ei[s:e, j] = np.where(ok, col, 0)
             d[rows, col] = np.inf
     return ed, ei
+
+
+def hierarchy_oracle(P, sizes, radii, k=32, fraction=1.0):
+    """Oracle outputs of the PointNeXt-shaped query hierarchy on one scene:
+    per stage s the self rows ``ball(P_s -> P_s, r_s)``, the down-sampling
+    rows (the first ``sizes[s+1]`` self rows, which the reuse cache serves)
+    and ``nn(P_s -> P_{s+1})``.  With ``fraction < 1`` only the first
+    ``ceil(fraction * len)`` queries of each call are answered (a bounded
+    sample for timing).  Returns (outputs dict, rows answered)."""
+    P = np.asarray(P, np.float32)
+    out, rows = {}, 0
+    for s in range(4):
+        ps = P[: sizes[s]]
+        nq = int(np.ceil(fraction * sizes[s]))
+        res = ball_oracle_fast(ps[:nq], ps, radii[s], k)
+        out[f"ball{s}"] = res
+        nh = int(np.ceil(fraction * sizes[s + 1]))
+        out[f"hit{s}"] = res[:nh].copy()
+        d, i = nn_oracle_fast(ps[:nq], P[: sizes[s + 1]])
+        out[f"nnd{s}"], out[f"nni{s}"] = d, i
+        rows += 2 * nq + nh
+    return out, rows

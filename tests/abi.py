@@ -18,8 +18,10 @@ def bvh_lib(name="gsa_bvh"):
     lib.query_ball_bvh.argtypes = [P, P, I, I, I, F, I, P, P, P]
     lib.free_bvh.argtypes = [P, I, P]
     lib.build_bvh_batch.argtypes = [P, P, I, I, I, ctypes.POINTER(P), P]
-    lib.query_ball_bvh_batch.argtypes = [P, P, P, P, I, F, I, P, P, P]
-    lib.query_bvh_batch.argtypes = [P, P, P, P, I, P, P, P, P]
+    lib.query_ball_bvh_batch.argtypes = [P, P, P, P, P, I, I, F, I, P, P, P]
+    lib.query_bvh_batch.argtypes = [P, P, P, P, P, I, I, P, P, P, P]
+    lib.coords_mismatch_strided.argtypes = [I, P, ctypes.c_longlong, P, ctypes.c_longlong, ctypes.c_longlong, P, I, P]
+    lib.reuse_rows_batch.argtypes = [I, P, ctypes.c_longlong, I, P, I, I, P, ctypes.c_longlong, P, P]
     lib.coords_mismatch.argtypes = [I, P, P, P, P, P]
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]

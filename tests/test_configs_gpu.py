@@ -1,0 +1,172 @@
+# SPDX-License-Identifier: Apache-2.0
+"""GPU parity on the five benchmark workloads (seeded synthetic stand-ins).
+
+* unit case: 4096 N(0,1) points, radius 0.4 K16 for the first 128, 3NN of
+  all points against the first 1024, at threshold 1024 (scan 3NN) and 32;
+* room hierarchy: 24,000-point FPS-ordered room, prefixes
+  24000/6000/1500/375/94, r = 0.1/0.2/0.4/0.8, K = 32, reuse enabled --
+  every output equals the oracle, statistics as the reference would count;
+* batched scenes: ``hierarchy.Batch`` over many rooms equals the per-scene
+  ``QuerySession`` run bit for bit (oracle-checked on a sample of scenes);
+* exactness stress: 200,000 clustered points (sigma 1e-3, 20 % duplicates,
+  5 % points at exactly f32(0.25)^2 from a query), radius and 3NN on oracle
+  samples, then a 1-ulp support change must miss the reuse cache and
+  recompute correctly.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import numpy_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def test_unit_case():
+    from gsa_b200 import QuerySession, scenes
+
+    x_np = scenes.unit_case()
+    x = torch.from_numpy(x_np).cuda()
+    for threshold in [1024, 32]:
+        with QuerySession(threshold=threshold) as s:
+            out = torch.empty((128, 16), dtype=torch.int32, device="cuda")
+            s.ball_into(x[:128], x, 0.4, 16, out)
+            d = torch.empty((4096, 3), device="cuda")
+            i = torch.empty((4096, 3), dtype=torch.int32, device="cuda")
+            s.nn_into(x, x[:1024], d, i)
+            assert np.array_equal(out.cpu().numpy(), orc.ball_oracle(x_np[:128], x_np, 0.4, 16))
+            ed, ei = orc.nn_oracle_fast(x_np, x_np[:1024])
+            assert np.array_equal(d.cpu().numpy(), ed) and np.array_equal(i.cpu().numpy(), ei)
+            assert s.stats["builds"] == 1 and s.stats["tree_reuses"] == (1 if threshold == 32 else 0)
+
+
+def _room(seeds):
+    from gsa_b200 import scenes
+
+    return scenes.room_batch(seeds)
+
+
+def _check_hierarchy_against_oracle(P_np, out, sizes, radii):
+    for s in range(4):
+        ps = P_np[: sizes[s]]
+        want = orc.ball_oracle_fast(ps, ps, radii[s], 32)
+        assert np.array_equal(out[f"ball{s}"].cpu().numpy(), want), s
+        assert np.array_equal(out[f"hit{s}"].cpu().numpy(), want[: sizes[s + 1]]), s
+        ed, ei = orc.nn_oracle_fast(ps, P_np[: sizes[s + 1]])
+        assert np.array_equal(out[f"nnd{s}"].cpu().numpy(), ed), s
+        assert np.array_equal(out[f"nni{s}"].cpu().numpy(), ei), s
+
+
+def test_room_hierarchy_session():
+    from gsa_b200 import QuerySession, hierarchy as hz
+
+    P = _room([0])[0]
+    with QuerySession() as s:
+        out = hz.run_session(s, P)
+        torch.cuda.synchronize()
+        st = dict(s.stats)
+    _check_hierarchy_against_oracle(P.cpu().numpy(), out, hz.ROOM_SIZES, hz.ROOM_RADII)
+    # one prefix tree serves levels 24000/6000/1500; 375 and 94 take the scan
+    assert st["builds"] == 1 and st["ball_hits"] == 4 and st["ball_calls"] == 8
+    assert st["nn_calls"] == 4 and st["tree_reuses"] == 3
+    assert st["fallbacks"] == 0
+
+
+def test_batch_equals_session_per_scene():
+    from gsa_b200 import QuerySession, hierarchy as hz
+
+    seeds = list(range(16))
+    X = _room(seeds)
+    eng = hz.Batch()
+    out = eng.run(X)
+    assert out["hits"].sum().item() == len(seeds)
+    torch.cuda.synchronize()
+    for b in range(len(seeds)):
+        with QuerySession() as s:
+            ref = hz.run_session(s, X[b])
+        for key, t in ref.items():
+            rows = t.shape[0]
+            got = out[key][b * rows:(b + 1) * rows]
+            assert torch.equal(got, t), (b, key)
+    _check_hierarchy_against_oracle(X[3].cpu().numpy(), {k: v[3 * v.shape[0] // 16:4 * v.shape[0] // 16] for k, v in out.items() if k.startswith(("ball", "hit", "nn"))}, hz.ROOM_SIZES, hz.ROOM_RADII)
+
+
+def test_batched_reuse_admission_rejects_changed_scene():
+    from tests import abi
+
+    lib = abi.bvh_lib()
+    B, N, n_q = 4, 1000, 250
+    X = torch.randn(B, N, 3, device="cuda")
+    snap = X.clone()
+    snap[2, 700, 1] += 1e-3  # support differs beyond the query prefix
+    snap[3, 10, 0] = float("nan")  # NaN never compares equal
+    flags = torch.full((2 * B,), 7, dtype=torch.int32, device="cuda")
+    st = abi.stream()
+    assert lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, N * 3, flags.data_ptr(), 2, st) == 0
+    assert lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, flags.data_ptr() + 4, 2, st) == 0
+    assert flags.tolist() == [0, 0, 0, 0, 1, 0, 1, 1]
+    rows = torch.randint(0, 999, (B * N, 32), dtype=torch.int32, device="cuda")
+    dst = torch.full((B * n_q, 32), -1, dtype=torch.int32, device="cuda")
+    hits = torch.full((B,), 9, dtype=torch.int32, device="cuda")
+    assert lib.reuse_rows_batch(B, rows.data_ptr(), N * 32, 32, flags.data_ptr(), n_q, 32, dst.data_ptr(), n_q * 32, hits.data_ptr(), st) == 0
+    assert hits.tolist() == [1, 1, 0, 0]
+    for b in range(B):
+        got = dst[b * n_q:(b + 1) * n_q]
+        if b < 2:
+            assert torch.equal(got, rows[b * N:b * N + n_q])
+        else:
+            assert (got == -1).all()
+
+
+def test_clustered_exactness_stress():
+    from gsa_b200 import QuerySession, scenes
+
+    pts, info = scenes.clustered(seed=0)
+    assert info["exact_points"] >= 9000
+    r2 = np.float32(0.25) * np.float32(0.25)
+    for pid, qi in info["anchors"][:200]:
+        d = pts[qi] - pts[pid]
+        sq = d * d
+        assert (sq[0] + sq[1]) + sq[2] == r2
+    x = torch.from_numpy(pts).cuda()
+    nq = info["queries"]
+    rng = np.random.default_rng(1)
+    anchor_q = np.array(sorted({qi for _, qi in info["anchors"]}))
+    sample = np.unique(np.concatenate([rng.choice(nq, 1500, replace=False), anchor_q[:500]]))
+    with QuerySession() as s:
+        out = torch.empty((nq, 32), dtype=torch.int32, device="cuda")
+        s.ball_into(x[:nq], x, 0.25, 32, out)
+        d = torch.empty((len(pts), 3), device="cuda")
+        ids = torch.empty((len(pts), 3), dtype=torch.int32, device="cuda")
+        s.nn_into(x, x[:nq], d, ids)
+        got = out.cpu().numpy()
+        assert np.array_equal(got[sample], orc.ball_oracle_fast(pts[sample], pts, 0.25, 32))
+        nn_sample = np.unique(np.concatenate([rng.choice(len(pts), 2000, replace=False), np.arange(0, 200)]))
+        ed, ei = orc.nn_oracle_fast(pts[nn_sample], pts[:nq])
+        assert np.array_equal(d.cpu().numpy()[nn_sample], ed) and np.array_equal(ids.cpu().numpy()[nn_sample], ei)
+        # exact-r points: strict qualification on a support of anchors only
+        anchors = np.array(info["anchors"][:2000])
+        sub = np.concatenate([pts[anchors[:, 1]], pts[anchors[:, 0]]])
+        xs = torch.from_numpy(sub).cuda()
+        o2 = torch.empty((len(anchors), 32), dtype=torch.int32, device="cuda")
+        s.ball_into(xs[: len(anchors)], xs, 0.25, 32, o2)
+        assert np.array_equal(o2.cpu().numpy(), orc.ball_oracle_fast(sub[: len(anchors)], sub, 0.25, 32))
+        # 1-ulp change of one support coordinate: reuse miss and exact recompute
+        hits, builds = s.stats["ball_hits"], s.stats["builds"]
+        j = int(anchors[0, 0])
+        x2 = x.clone()
+        x2[j, 0] = torch.nextafter(x2[j, 0], torch.tensor(np.inf, device="cuda"))
+        out2 = torch.empty((nq, 32), dtype=torch.int32, device="cuda")
+        s.ball_into(x2[:nq], x2, 0.25, 32, out2)
+        assert s.stats["ball_hits"] == hits and s.stats["builds"] == builds + 1
+        p2 = x2.cpu().numpy()
+        sample2 = np.unique(np.concatenate([sample[:300], [int(anchors[0, 1])]]))
+        assert np.array_equal(out2.cpu().numpy()[sample2], orc.ball_oracle_fast(p2[sample2], p2, 0.25, 32))
+        # the unchanged values still hit
+        out3 = torch.empty((nq // 2, 8), dtype=torch.int32, device="cuda")
+        s.ball_into(x[: nq // 2].clone(), x.clone(), 0.25, 8, out3)
+        assert s.stats["ball_hits"] == hits + 1
+        assert torch.equal(out3, out[: nq // 2, :8])
+        s.close(collect=True)
+        assert s.stats["fallbacks"] == 0

@@ -193,7 +193,7 @@ def test_forest_batch_equals_oracle_per_scene():
         qseg_h = (ctypes.c_int * len(qseg))(*qseg.tolist())
         out = torch.full((len(q), 32), -9, dtype=torch.int32, device="cuda")
         fb = torch.zeros(1, dtype=torch.int32, device="cuda")
-        code = lib.query_ball_bvh_batch(h, q.data_ptr(), qseg_d.data_ptr(), qseg_h, level, 0.3, 32, out.data_ptr(), fb.data_ptr(), abi.stream())
+        code = lib.query_ball_bvh_batch(h, q.data_ptr(), None, qseg_d.data_ptr(), qseg_h, 0, level, 0.3, 32, out.data_ptr(), fb.data_ptr(), abi.stream())
         ok_sizes = all(len(xi) >> (2 * level) >= 1 for xi, qq in zip(xs, qs) if len(qq))
         if not ok_sizes:
             assert code == -2
@@ -207,7 +207,7 @@ def test_forest_batch_equals_oracle_per_scene():
         if all(len(xi) >> (2 * level) >= 3 for xi, qq in zip(xs, qs) if len(qq)):
             d = torch.empty((len(q), 3), device="cuda")
             ix = torch.empty((len(q), 3), dtype=torch.int32, device="cuda")
-            assert lib.query_bvh_batch(h, q.data_ptr(), qseg_d.data_ptr(), qseg_h, level, d.data_ptr(), ix.data_ptr(), fb.data_ptr(), abi.stream()) == 0
+            assert lib.query_bvh_batch(h, q.data_ptr(), None, qseg_d.data_ptr(), qseg_h, 0, level, d.data_ptr(), ix.data_ptr(), fb.data_ptr(), abi.stream()) == 0
             for i, (xi, qi) in enumerate(zip(xs, qs)):
                 m = len(xi) >> (2 * level)
                 ed, ei = orc.nn_oracle_fast(qi, xi[:m])
@@ -278,26 +278,9 @@ def test_reuse_kernels():
     assert torch.equal(out, cached[1][:, :7])
 
 
-def _fps_numpy(p, start):
-    n = len(p)
-    mind = np.full(n, np.inf, np.float32)
-    order = np.empty(n, np.int64)
-    cur = start
-    with np.errstate(over="ignore"):
-        for it in range(n):
-            order[it] = cur
-            d = p - p[cur]
-            sq = d * d
-            dist = (sq[:, 0] + sq[:, 1]) + sq[:, 2]
-            upd = mind >= 0
-            mind = np.where(upd, np.minimum(mind, dist), mind)
-            mind[cur] = -1.0
-            cur = int(np.argmax(mind))
-    return order
-
-
 def test_fps_order_matches_sequential_rule():
     from gsa_b200 import scenes
+    from oracle import fps as fps_cpu
 
     pts = []
     starts = []
@@ -309,7 +292,7 @@ def test_fps_order_matches_sequential_rule():
     x = torch.from_numpy(np.stack(pts)).cuda()
     order = scenes.fps_order(x, starts).numpy()
     for i in range(3):
-        assert np.array_equal(order[i], _fps_numpy(pts[i], starts[i]))
+        assert np.array_equal(order[i], fps_cpu.fps_order(pts[i], starts[i]))
         assert sorted(order[i].tolist()) == list(range(3000))
 
 
