@@ -92,3 +92,26 @@ def test_scan_kernels_equal_reference_cuda():
     assert ref.nn3(b, m, n, q.data_ptr(), x.data_ptr(), d_r.data_ptr(), i_r.data_ptr(), abi.stream()) == 0
     code, d_o, i_o = abi.scan_nn3(q, x, b=b)
     assert code == 0 and torch.equal(d_r, d_o) and torch.equal(i_r, i_o)
+
+
+def test_scan_nn3_overflow_and_nonfinite_equal_reference_cuda():
+    """Squared distances that overflow to +inf, and NaN/inf coordinates: the
+    reference's double comparison against 1e40 rejects +inf and NaN exactly
+    like the finite test, so outputs agree with ours and with the oracle."""
+    from oracle import numpy_oracle as orc
+
+    ref = _lib("reference_queries")
+    P, I = ctypes.c_void_p, ctypes.c_int
+    ref.nn3.argtypes = [I, I, I, P, P, P, P, P]
+    x = np.array([[0, 0, 0], [2e19, 0, 0], [np.inf, 0, 0], [np.nan, 1, 1], [1e19, 1e19, 0], [3, 0, 0], [-2e19, 0, 0]], np.float32)
+    q = np.array([[0, 0, 0], [1e19, 0, 0], [-3e19, 5, 5], [np.nan, 0, 0], [1, 1, 1]], np.float32)
+    xt = torch.from_numpy(x).cuda()
+    qt = torch.from_numpy(q).cuda()
+    d_r = torch.empty((1, len(q), 3), device="cuda")
+    i_r = torch.empty((1, len(q), 3), dtype=torch.int32, device="cuda")
+    assert ref.nn3(1, len(q), len(x), qt.data_ptr(), xt.data_ptr(), d_r.data_ptr(), i_r.data_ptr(), abi.stream()) == 0
+    code, d_o, i_o = abi.scan_nn3(qt, xt)
+    assert code == 0
+    ed, ei = orc.nn_oracle(q, x)
+    assert np.array_equal(d_r.cpu().numpy()[0], ed) and np.array_equal(i_r.cpu().numpy()[0], ei)
+    assert torch.equal(d_r, d_o) and torch.equal(i_r, i_o)
