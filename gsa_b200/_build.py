@@ -34,7 +34,9 @@ FLAGS = [
     "-I" + str(ROOT / "include"),
 ]
 
-_BVH = ["launches.cu", "pool.cu", "build.cu", "query.cu", "reuse.cu", "fps.cu", "gsa_bvh_abi.cu"]
+_BVH = [
+    "launches.cu", "pool.cu", "build.cu", "query.cu", "reuse.cu", "reuse_static.cu", "fps.cu", "gsa_bvh_abi.cu",
+]
 LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),

@@ -148,6 +148,29 @@ int reuse_rows_batch(int count, const int* src, long long src_stride,
 /* Total kernel launches this library has issued since it was loaded. */
 int launch_counter(unsigned long long* total);
 
+/* No counterpart in the reference.  Reuse-cache lookup that allocates
+ * nothing, for callers that cannot allocate device memory at lookup time
+ * (a framework allocator that must not be bypassed, loops where
+ * cudaMalloc/cudaFree would synchronise the device, a fixed device
+ * footprint after start-up).  Same result as coords_mismatch over the pairs
+ * (x, saved_x[c]) with nx floats and (q, saved_q[c]) with nq floats followed
+ * by reuse_rows: the rows of the first candidate c whose support and query
+ * prefix both equal the current ones (IEEE ==) are copied from cached[c]
+ * (row stride src_ld) to dst (rows x cols) and c, or -1, is written to *hit.
+ * saved_x, saved_q, cached are HOST arrays of count device pointers.  The
+ * per-candidate flags live in a fixed 512-byte device array inside the
+ * library (held on every GPU that loads it), so count may not exceed 64:
+ * larger counts return -4.  The first call on a device looks up that array's
+ * address (make it before any stream capture).  Calls share the array:
+ * calls whose GPU work overlaps race.  Returns 0, -2 (bad argument), -4, or
+ * a cudaError_t. */
+int reuse_lookup_static(int count, const float* x, long long nx,
+                        const float* q, long long nq,
+                        const float* const* saved_x,
+                        const float* const* saved_q, const int* const* cached,
+                        int src_ld, int rows, int cols, int* dst, int* hit,
+                        void* stream);
+
 /* Farthest-point order of b scenes of n points each (x is [b][n][3]),
  * starting at start[b] (device int[b]); order is device int[b][n].  Ties pick
  * the lowest index; chosen points are never repeated.  Input generator for
