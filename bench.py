@@ -166,6 +166,61 @@ def run_reference(args, rank, world):
 # our arm
 
 
+class NvmlClocks:
+    """NVML samples (every 5 ms, read-only) of this GPU's SM clock and
+    clock-event reasons during the timed region."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
+
+    def __init__(self, torch, device):
+        import pynvml
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        want = str(torch.cuda.get_device_properties(device).uuid).replace("GPU-", "")
+        self.handle = None
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            uuid = pynvml.nvmlDeviceGetUUID(h)
+            uuid = uuid.decode() if isinstance(uuid, bytes) else uuid
+            if uuid.replace("GPU-", "") == want:
+                self.handle = h
+        if self.handle is None:
+            raise RuntimeError("GPU not found in NVML")
+        self.samples, self.reasons, self.stop_flag = [], set(), False
+
+    def _poll(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+            bits = get_reasons(self.handle)
+            for bit, name in self.REASONS.items():
+                if bits & bit:
+                    self.reasons.add(name)
+            time.sleep(0.005)
+
+    def start(self):
+        import threading
+
+        self.thread = threading.Thread(target=self._poll, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        self.stop_flag = True
+        self.thread.join()
+        mx = self.nv.nvmlDeviceGetMaxClockInfo(self.handle, self.nv.NVML_CLOCK_SM)
+        if not self.samples:
+            return {"error": "no samples"}
+        return {
+            "sm_mhz": statistics.median(self.samples),
+            "sm_max_mhz": mx,
+            "samples": len(self.samples),
+            "reasons": sorted(self.reasons),
+            "source": "NVML",
+        }
+
+
 class Clocks:
     """nvidia-smi samples of this GPU's clocks and throttle reasons."""
 
@@ -286,7 +341,10 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.barrier()
 
-    clocks = Clocks(torch, dev)
+    try:
+        clocks = NvmlClocks(torch, dev)
+    except Exception:
+        clocks = Clocks(torch, dev)
     launches0 = launch_total()
     clocks.start()
     records = []
@@ -315,12 +373,14 @@ def run_ours(args, rank, world, local):
     launches = launch_total() - launches0
 
     step_ms = [s.elapsed_time(e) for s, _, e in records]
-    phase = {}
+    phase, stage = {}, {}
     for s, marks, _ in records:
         prev = s
         for name, e in marks:
+            dt = prev.elapsed_time(e)
             key = name.rstrip("0123456789")
-            phase[key] = phase.get(key, 0.0) + prev.elapsed_time(e)
+            phase[key] = phase.get(key, 0.0) + dt
+            stage[name] = stage.get(name, 0.0) + dt
             prev = e
     total_ms = sum(step_ms)
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -386,6 +446,7 @@ def run_ours(args, rank, world, local):
         "config": config(S),
         "roofline": roofline,
         "phases_ms_per_step": {k: v / args.steps for k, v in phase.items()},
+        "stages_ms_per_step": {k: round(v / args.steps, 4) for k, v in stage.items()},
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
         "clocks": clock_info,

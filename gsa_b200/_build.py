@@ -3,9 +3,10 @@
 
 ``python -m gsa_b200._build`` writes ``gsa_b200/_native/gsa_bvh.so`` and
 ``gsa_b200/_native/reference_queries.so`` (the two library names GSA's
-``gsa/_library.py`` loads), plus ``gsa_bvh_stack4.so``, a test variant whose
-traversal stack holds 4 entries so that the exact full-scan fallback path is
-exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+``gsa/_library.py`` loads), plus two test variants: ``gsa_bvh_walk.so``
+answers every support size with the tree walk (the default library scans
+small prefixes), and ``gsa_bvh_stack4.so`` also has a 4-entry traversal
+stack so that the exact full-scan fallback path is exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
 intrinsics for every distance operation.
 """
@@ -37,10 +38,13 @@ FLAGS = [
 _BVH = [
     "launches.cu", "pool.cu", "build.cu", "query.cu", "reuse.cu", "reuse_static.cu", "fps.cu", "gsa_bvh_abi.cu",
 ]
+_WALK_ONLY = ["-DGSA_RADIUS_SCAN_MAX=0", "-DGSA_KNN_SCAN_MAX=0"]
 LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),
-    "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"]),
+    # test variants: tree walk for every support size, and a 4-entry stack
+    "gsa_bvh_walk": (_BVH, _WALK_ONLY),
+    "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 
 

@@ -24,6 +24,14 @@
 #ifndef GSA_STACK
 #define GSA_STACK 128
 #endif
+// Support prefixes up to these sizes are answered by the warp scans below
+// instead of a tree walk (same results; fewer serial steps per warp).
+#ifndef GSA_RADIUS_SCAN_MAX
+#define GSA_RADIUS_SCAN_MAX 2048
+#endif
+#ifndef GSA_KNN_SCAN_MAX
+#define GSA_KNN_SCAN_MAX 1024
+#endif
 
 namespace gsa {
 namespace {
@@ -336,6 +344,109 @@ __global__ void __launch_bounds__(kQThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-cooperative original-order scans for small support prefixes.  One
+// warp answers one query: the 32 lanes test 32 consecutive support IDs, a
+// ballot orders the hits by ID, and the scan stops once K are found (radius)
+// or after m points (3NN, per-lane top-3 merged across the warp).  A warp's
+// serial work is m/32 steps instead of a tree walk, and there is one warp per
+// query instead of one per 32, which suits small prefixes with few queries.
+constexpr int kScanWarps = 8;
+
+__global__ void __launch_bounds__(kScanWarps * 32)
+    radius_scan_kernel(QArgs a) {
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  int qbase = a.qseg ? a.qseg[b] : 0;
+  int qin = a.qstart ? a.qstart[b] : qbase;
+  int Q = a.qseg ? a.qseg[b + 1] - qbase : a.nq;
+  int m = a.m > 0 ? a.m : level_size(d.n, a.level);
+  int lane = threadIdx.x & 31;
+  long long qi = (long long)blockIdx.x * kScanWarps + (threadIdx.x >> 5);
+  if (qi >= Q) return;  // warp-uniform
+  const float* qp = a.q + 3ll * (qin + qi);
+  float px = qp[0], py = qp[1], pz = qp[2];
+  const float r2 = __fmul_rn(a.radius, a.radius);
+  const int K = a.ns;
+  const float* xs = a.f.x + 3ll * d.p0;
+  int* row = a.out + (size_t)(qbase + qi) * K;
+  int count = 0, first = 0;
+  for (int base = 0; base < m && count < K; base += 32) {
+    int id = base + lane;
+    bool hit = false;
+    if (id < m) {
+      const float* p = xs + 3ll * id;
+      hit = exact_d2(px, py, pz, p[0], p[1], p[2]) < r2;
+    }
+    unsigned bal = __ballot_sync(kFull, hit);
+    if (!bal) continue;
+    if (!count) first = base + __ffs(bal) - 1;
+    int pos = count + __popc(bal & ((1u << lane) - 1u));
+    if (hit && pos < K) row[pos] = id;
+    count += __popc(bal);
+  }
+  count = min(count, K);
+  for (int k = count + lane; k < K; k += 32) row[k] = count ? first : 0;
+}
+
+__global__ void __launch_bounds__(kScanWarps * 32)
+    knn3_scan_kernel(QArgs a) {
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  int qbase = a.qseg ? a.qseg[b] : 0;
+  int qin = a.qstart ? a.qstart[b] : qbase;
+  int Q = a.qseg ? a.qseg[b + 1] - qbase : a.nq;
+  int m = a.m > 0 ? a.m : level_size(d.n, a.level);
+  int lane = threadIdx.x & 31;
+  long long qi = (long long)blockIdx.x * kScanWarps + (threadIdx.x >> 5);
+  if (qi >= Q) return;
+  const float* qp = a.q + 3ll * (qin + qi);
+  float px = qp[0], py = qp[1], pz = qp[2];
+  const float inf = __int_as_float(0x7f800000);
+  float d0 = inf, d1 = inf, d2 = inf;
+  int i0 = INT_MAX, i1 = INT_MAX, i2 = INT_MAX;
+  const float* xs = a.f.x + 3ll * d.p0;
+  for (int id = lane; id < m; id += 32) {
+    const float* p = xs + 3ll * id;
+    insert3(exact_d2(px, py, pz, p[0], p[1], p[2]), id, d0, d1, d2, i0, i1, i2);
+  }
+  for (int o = 16; o; o >>= 1) {
+    float e0 = __shfl_xor_sync(kFull, d0, o), e1 = __shfl_xor_sync(kFull, d1, o),
+          e2 = __shfl_xor_sync(kFull, d2, o);
+    int j0 = __shfl_xor_sync(kFull, i0, o), j1 = __shfl_xor_sync(kFull, i1, o),
+        j2 = __shfl_xor_sync(kFull, i2, o);
+    insert3(e0, j0, d0, d1, d2, i0, i1, i2);
+    insert3(e1, j1, d0, d1, d2, i0, i1, i2);
+    insert3(e2, j2, d0, d1, d2, i0, i1, i2);
+  }
+  if (lane < 3) {
+    float v = lane == 0 ? d0 : (lane == 1 ? d1 : d2);
+    int id = lane == 0 ? i0 : (lane == 1 ? i1 : i2);
+    size_t o = (size_t)(qbase + qi) * 3 + lane;
+    a.dout[o] = v;
+    a.out[o] = id == INT_MAX ? 0 : id;
+  }
+}
+
+// Largest support prefix any tree of the launch searches (host side).
+int max_prefix(const Forest& f, const QuerySet& qs) {
+  if (!qs.qseg_host) return qs.m;
+  int best = 0;
+  for (int b = 0; b < f.B; ++b) {
+    if (qs.qseg_host[b + 1] == qs.qseg_host[b]) continue;
+    best = std::max(best, qs.m ? qs.m : level_size(f.hdesc[b].n, qs.level));
+  }
+  return best;
+}
+
+long long max_queries(const Forest& f, const QuerySet& qs) {
+  if (!qs.qseg_host) return qs.nq;
+  long long best = 0;
+  for (int b = 0; b < f.B; ++b)
+    best = std::max<long long>(best, qs.qseg_host[b + 1] - qs.qseg_host[b]);
+  return best;
+}
+
 // Slots (query positions walked by warps) of one tree, as slot_setup.
 long long tree_slots(int n, int levels, int nq) {
   if (nq > n) return nq;
@@ -381,6 +492,14 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   a.ns = ns;
   a.out = out;
   a.fallback = fallback;
+  if (max_prefix(f, qs) <= GSA_RADIUS_SCAN_MAX) {
+    long long nq = max_queries(f, qs);
+    if (nq <= 0) return cudaSuccess;
+    dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
+    count_launches();
+    radius_scan_kernel<<<grid, kScanWarps * 32, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
   dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
@@ -395,6 +514,14 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
   a.dout = d;
   a.out = ix;
   a.fallback = fallback;
+  if (max_prefix(f, qs) <= GSA_KNN_SCAN_MAX) {
+    long long nq = max_queries(f, qs);
+    if (nq <= 0) return cudaSuccess;
+    dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
+    count_launches();
+    knn3_scan_kernel<<<grid, kScanWarps * 32, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
   dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);

@@ -32,7 +32,7 @@ def levels_of(n):
 def check_ball(h, x, q, m, level, r, ns):
     code, out, fb = h.ball(cuda(q), m, level, r, ns)
     assert code == 0
-    want = orc.ball_oracle(q, x[:m], r, ns)
+    want = orc.ball_oracle_fast(q, x[:m], r, ns)
     got = out.cpu().numpy()
     assert np.array_equal(got, want), (len(x), m, level, r, ns)
     return fb
@@ -47,14 +47,20 @@ def check_knn(h, x, q, m, level):
     return fb
 
 
-@pytest.mark.parametrize("n", [1, 2, 3, 5, 16, 17, 33, 100, 257, 1000, 4099])
+# "gsa_bvh" scans support prefixes up to 2048 (radius) / 1024 (3NN) points and
+# walks the tree above; "gsa_bvh_walk" walks the tree for every size.
+LIBS = ["gsa_bvh", "gsa_bvh_walk"]
+
+
+@pytest.mark.parametrize("lib_name", LIBS)
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 16, 17, 33, 100, 257, 1000, 4099, 9000])
 @pytest.mark.parametrize("leaf", [1, 4, 16, 32])
-def test_prefix_tree_all_levels(n, leaf):
+def test_prefix_tree_all_levels(n, leaf, lib_name):
     rng = np.random.default_rng(n * 31 + leaf)
     x = rng.normal(size=(n, 3)).astype(np.float32)
     if n > 1:
         x[n // 2] = x[0]  # duplicate
-    lib = abi.bvh_lib()
+    lib = abi.bvh_lib(lib_name)
     h = abi.Handle(lib, cuda(x), prefix=1, leaf=leaf)
     assert h.code == 0
     for level, m in enumerate(levels_of(n)):
@@ -100,9 +106,10 @@ def test_plain_tree_and_invalid_levels():
     assert h.free() == 0
 
 
-def test_scales_radii_and_nonfinite():
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_scales_radii_and_nonfinite(lib_name):
     rng = np.random.default_rng(11)
-    lib = abi.bvh_lib()
+    lib = abi.bvh_lib(lib_name)
     for scale in [0.0, 1e-25, 1.0, 1e20]:
         x = (rng.normal(size=(300, 3)) * scale).astype(np.float32)
         h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
@@ -133,11 +140,12 @@ def test_scales_radii_and_nonfinite():
     h.free()
 
 
-def test_duplicates_and_ties():
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_duplicates_and_ties(lib_name):
     rng = np.random.default_rng(12)
     base = rng.integers(0, 4, size=(64, 3)).astype(np.float32)  # lattice, many equal distances
     x = base[rng.integers(0, 64, size=3000)]
-    lib = abi.bvh_lib()
+    lib = abi.bvh_lib(lib_name)
     h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
     q = np.concatenate([x[:200], base + 0.5])
     for level, m in enumerate(levels_of(3000)):
@@ -147,10 +155,11 @@ def test_duplicates_and_ties():
     h.free()
 
 
-def test_queries_outnumber_support_and_unrelated_queries():
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_queries_outnumber_support_and_unrelated_queries(lib_name):
     rng = np.random.default_rng(13)
     x = rng.random((2000, 3)).astype(np.float32)
-    lib = abi.bvh_lib()
+    lib = abi.bvh_lib(lib_name)
     h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
     big = np.concatenate([x, rng.random((3000, 3)).astype(np.float32)])
     check_ball(h, x, big, 2000, 0, 0.05, 32)
@@ -173,13 +182,14 @@ def test_small_stack_fallback_is_exact_and_counted():
     h.free()
 
 
-def test_forest_batch_equals_oracle_per_scene():
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_forest_batch_equals_oracle_per_scene(lib_name):
     rng = np.random.default_rng(15)
-    sizes = [1, 3, 17, 700, 4096, 2500]
+    sizes = [1, 3, 17, 700, 4096, 2500, 12000]
     xs = [rng.normal(size=(n, 3)).astype(np.float32) for n in sizes]
     seg = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
     x = cuda(np.concatenate(xs))
-    lib = abi.bvh_lib()
+    lib = abi.bvh_lib(lib_name)
     h = ctypes.c_void_p()
     seg_c = (ctypes.c_int * len(seg))(*seg.tolist())
     assert lib.build_bvh_batch(x.data_ptr(), seg_c, len(sizes), 1, 16, ctypes.byref(h), abi.stream()) == 0
@@ -202,7 +212,7 @@ def test_forest_batch_equals_oracle_per_scene():
         got = out.cpu().numpy()
         for i, (xi, qi) in enumerate(zip(xs, qs)):
             m = len(xi) >> (2 * level)
-            want = orc.ball_oracle(qi, xi[:m], 0.3, 32)
+            want = orc.ball_oracle_fast(qi, xi[:m], 0.3, 32)
             assert np.array_equal(got[qseg[i]:qseg[i + 1]], want), (i, level)
         if all(len(xi) >> (2 * level) >= 3 for xi, qq in zip(xs, qs) if len(qq)):
             d = torch.empty((len(q), 3), device="cuda")
