@@ -15,7 +15,8 @@
 //      written to `pts` in leaf order and ascending ID inside a leaf; per
 //      level child entries (box of the finite members with ID < n/4^l, the
 //      subtree's minimum ID, child/leaf reference); children stored in
-//      ascending minimum-ID order                    (refit_kernel)
+//      ascending minimum-ID order  (karras_kernel emits leaf records,
+//      leaf_kernel: one warp per leaf, then a one-lane-per-level climb)
 //   6. per level, the IDs < n/4^l in leaf order, used as a spatially coherent
 //      query order for prefix queries               (qorder_* kernels)
 #include <algorithm>
@@ -256,95 +257,83 @@ __device__ __forceinline__ int common_prefix(const uint64_t* k, int n, int i,
   return 64 + __clz(i ^ j);
 }
 
+// Each internal node i > L points ("kept") emits a leaf record for every
+// child holding <= L points: (tree, first, last, i*2 + side); a tree of at most
+// L points emits one root record (tree, 0, n-1, -1).  Records are appended
+// with one atomic per warp.
+__device__ __forceinline__ void emit_leaf(bool want, int4 rec, int4* list,
+                                          int* count) {
+  unsigned mask = __ballot_sync(kFull, want);
+  if (!mask) return;
+  int lane = threadIdx.x & 31;
+  int leader = __ffs(mask) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(count, __popc(mask));
+  base = __shfl_sync(kFull, base, leader);
+  if (want) list[base + __popc(mask & ((1u << lane) - 1u))] = rec;
+}
+
 __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
-                              int4* range, int* parent) {
+                              int* parent, int leaf, int4* leaves,
+                              int* leaf_count) {
   int b = blockIdx.y;
   TreeDesc d = desc[b];
   int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= d.n - 1) return;
-  const uint64_t* k = keys + d.p0;
   int n = d.n;
-  int4* rg = range + (d.p0 - b);
-  int* par = parent + (d.p0 - b);
-  int dir = common_prefix(k, n, i, i + 1) > common_prefix(k, n, i, i - 1) ? 1 : -1;
-  int dmin = common_prefix(k, n, i, i - dir);
-  int lmax = 2;
-  while (common_prefix(k, n, i, i + lmax * dir) > dmin) lmax <<= 1;
-  int l = 0;
-  for (int t = lmax >> 1; t >= 1; t >>= 1)
-    if (common_prefix(k, n, i, i + (l + t) * dir) > dmin) l += t;
-  int j = i + l * dir;
-  int dnode = common_prefix(k, n, i, j);
-  int s = 0, t = l;
-  do {
-    t = (t + 1) >> 1;
-    if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
-  } while (t > 1);
-  int gamma = i + s * dir + min(dir, 0);
-  int first = min(i, j), last = max(i, j);
-  rg[i] = make_int4(first, last, gamma, 0);
-  if (first != gamma) par[gamma] = (i << 1) | 0;
-  if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
+  bool valid = i < n - 1;
+  int4 rec0 = make_int4(b, 0, n - 1, -1), rec1 = rec0;
+  bool want0 = i == 0 && n <= leaf, want1 = false;
+  if (valid) {
+    const uint64_t* k = keys + d.p0;
+    int* par = parent + (d.p0 - b);
+    int dir =
+        common_prefix(k, n, i, i + 1) > common_prefix(k, n, i, i - 1) ? 1 : -1;
+    int dmin = common_prefix(k, n, i, i - dir);
+    int lmax = 2;
+    while (common_prefix(k, n, i, i + lmax * dir) > dmin) lmax <<= 1;
+    int l = 0;
+    for (int t = lmax >> 1; t >= 1; t >>= 1)
+      if (common_prefix(k, n, i, i + (l + t) * dir) > dmin) l += t;
+    int j = i + l * dir;
+    int dnode = common_prefix(k, n, i, j);
+    int s = 0, t = l;
+    do {
+      t = (t + 1) >> 1;
+      if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
+    } while (t > 1);
+    int gamma = i + s * dir + min(dir, 0);
+    int first = min(i, j), last = max(i, j);
+    if (first != gamma) par[gamma] = (i << 1) | 0;
+    if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
+    if (last - first + 1 > leaf) {
+      want0 = gamma - first + 1 <= leaf;
+      want1 = last - gamma <= leaf;
+      rec0 = make_int4(b, first, gamma, (i << 1) | 0);
+      rec1 = make_int4(b, gamma + 1, last, (i << 1) | 1);
+    }
+  }
+  emit_leaf(want0, rec0, leaves, leaf_count);
+  emit_leaf(want1, rec1, leaves, leaf_count);
 }
 
 // ---------------------------------------------------------------------------
 struct RefitArgs {
   const TreeDesc* desc;
   const float* x;
-  const int* perm;     // sorted local point indices
-  const int4* range;
+  const int* perm;  // sorted local point indices
   const int* parent;
   int* counter;
+  const int4* leaves;
+  const int* leaf_count;
   float4* pts;
   Entry* nodes;
   Entry* root;
   int levels;
-  int leaf;
 };
 
 __device__ __forceinline__ Entry* node_entry(Entry* nodes, const TreeDesc& d,
                                              int level, int node, int slot) {
   return nodes + d.node0 + ((size_t)level * (d.n - 1) + node) * 2 + slot;
-}
-
-// Leaf over sorted positions [cf, cl]: points re-ordered by ascending ID and
-// written to pts; one entry per level.
-__device__ void make_leaf(const RefitArgs& a, const TreeDesc& d, int cf, int cl,
-                          Entry* e) {
-  int ids[kMaxLeaf];
-  int c = cl - cf + 1;
-  for (int k = 0; k < c; ++k) {
-    int id = a.perm[d.p0 + cf + k];
-    int pos = k;
-    while (pos > 0 && ids[pos - 1] > id) {
-      ids[pos] = ids[pos - 1];
-      --pos;
-    }
-    ids[pos] = id;
-  }
-  for (int l = 0; l < a.levels; ++l) {
-    e[l].lox = e[l].loy = e[l].loz = INFINITY;
-    e[l].hix = e[l].hiy = e[l].hiz = -INFINITY;
-    e[l].minid = ids[0];
-    e[l].ref = leaf_ref(cf, 1);
-  }
-  for (int k = 0; k < c; ++k) {
-    int id = ids[k];
-    const float* p = a.x + 3ll * (d.p0 + id);
-    float px = p[0], py = p[1], pz = p[2];
-    a.pts[d.p0 + cf + k] = make_float4(px, py, pz, __int_as_float(id));
-    bool fin = finite3(px, py, pz);
-    for (int l = 0; l < a.levels; ++l) {
-      if (id < level_size(d.n, l)) {
-        e[l].ref = leaf_ref(cf, k + 1);
-        if (fin) {
-          e[l].lox = fminf(e[l].lox, px); e[l].loy = fminf(e[l].loy, py);
-          e[l].loz = fminf(e[l].loz, pz); e[l].hix = fmaxf(e[l].hix, px);
-          e[l].hiy = fmaxf(e[l].hiy, py); e[l].hiz = fmaxf(e[l].hiz, pz);
-        }
-      }
-    }
-  }
 }
 
 __device__ __forceinline__ Entry load_entry_cg(const Entry* e) {
@@ -356,72 +345,115 @@ __device__ __forceinline__ Entry load_entry_cg(const Entry* e) {
   return r;
 }
 
-__global__ void refit_kernel(RefitArgs a) {
-  int b = blockIdx.y;
-  TreeDesc d = a.desc[b];
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  Entry e[kMaxLevels];
-  if (d.n <= a.leaf) {
-    if (i == 0) {
-      make_leaf(a, d, 0, d.n - 1, e);
-      for (int l = 0; l < a.levels; ++l) a.root[b * a.levels + l] = e[l];
-    }
-    return;
-  }
-  if (i >= d.n - 1) return;
-  const int4* rg = a.range + (d.p0 - b);
+__device__ __forceinline__ float warp_min(float v) {
+  for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Bottom-up climb from completed node i, one lane per level: order the two
+// child entries by minimum ID, write the union into the parent's slot, and
+// continue while this warp is the second child to arrive.
+__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
+                      int lane) {
   const int* par = a.parent + (d.p0 - b);
   int* cnt = a.counter + (d.p0 - b);
-  int4 r = rg[i];
-  if (r.y - r.x + 1 <= a.leaf) return;  // inside a leaf
-  int leaves = 0;
-  for (int side = 0; side < 2; ++side) {
-    int cf = side ? r.z + 1 : r.x;
-    int cl = side ? r.y : r.z;
-    if (cl - cf + 1 <= a.leaf) {
-      make_leaf(a, d, cf, cl, e);
-      for (int l = 0; l < a.levels; ++l)
-        store_entry(node_entry(a.nodes, d, l, i, side), e[l]);
-      ++leaves;
-    }
-  }
-  if (!leaves) return;
-  __threadfence();
-  int old = atomicAdd(cnt + i, leaves);
-  if (old + leaves < 2) return;
+  bool mine = lane < a.levels;
   // Karras depth is below 97 (64 key bits + 32 index bits); the bound only
   // guards against a corrupted topology.
-  for (int climb = 0; climb < 128; ++climb) {
+  for (int step = 0; step < 128; ++step) {
     __threadfence();
-    Entry c0 = load_entry_cg(node_entry(a.nodes, d, 0, i, 0));
-    Entry c1 = load_entry_cg(node_entry(a.nodes, d, 0, i, 1));
-    bool swap = c1.minid < c0.minid;
-    for (int l = 0; l < a.levels; ++l) {
-      Entry u0 = l ? load_entry_cg(node_entry(a.nodes, d, l, i, 0)) : c0;
-      Entry u1 = l ? load_entry_cg(node_entry(a.nodes, d, l, i, 1)) : c1;
-      if (swap) {
-        store_entry(node_entry(a.nodes, d, l, i, 0), u1);
-        store_entry(node_entry(a.nodes, d, l, i, 1), u0);
+    Entry u;
+    if (mine) {
+      Entry u0 = load_entry_cg(node_entry(a.nodes, d, lane, i, 0));
+      Entry u1 = load_entry_cg(node_entry(a.nodes, d, lane, i, 1));
+      if (u1.minid < u0.minid) {  // same decision on every level
+        store_entry(node_entry(a.nodes, d, lane, i, 0), u1);
+        store_entry(node_entry(a.nodes, d, lane, i, 1), u0);
       }
-      Entry u;
       u.lox = fminf(u0.lox, u1.lox); u.loy = fminf(u0.loy, u1.loy);
       u.loz = fminf(u0.loz, u1.loz); u.hix = fmaxf(u0.hix, u1.hix);
       u.hiy = fmaxf(u0.hiy, u1.hiy); u.hiz = fmaxf(u0.hiz, u1.hiz);
       u.minid = min(u0.minid, u1.minid);
       u.ref = i;
-      e[l] = u;
     }
     if (i == 0) {
-      for (int l = 0; l < a.levels; ++l) a.root[b * a.levels + l] = e[l];
-      break;
+      if (mine) a.root[b * a.levels + lane] = u;
+      return;
     }
     int pc = par[i];
-    int p = pc >> 1, side = pc & 1;
-    for (int l = 0; l < a.levels; ++l)
-      store_entry(node_entry(a.nodes, d, l, p, side), e[l]);
+    int p = pc >> 1;
+    if (mine) store_entry(node_entry(a.nodes, d, lane, p, pc & 1), u);
     __threadfence();
-    if (atomicAdd(cnt + p, 1) == 0) break;
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(cnt + p, 1);
+    if (__shfl_sync(kFull, old, 0) == 0) return;
     i = p;
+  }
+}
+
+// One warp per leaf record: lane k takes sorted position first + k, ranks
+// its original ID among the leaf's IDs, writes pts in ascending ID order, and
+// the warp reduces one entry per level (box of finite members with
+// ID < n/4^l, member count, minimum ID).  Then the owner node is completed by
+// whichever child arrives second.
+__global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
+  int lane = threadIdx.x & 31;
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int warps = (gridDim.x * blockDim.x) >> 5;
+  int total = *a.leaf_count;
+  const float inf = __int_as_float(0x7f800000);
+  for (int r = warp; r < total; r += warps) {
+    int4 rec = a.leaves[r];
+    int b = rec.x, cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
+    TreeDesc d = a.desc[b];
+    bool on = lane < c;
+    int id = on ? a.perm[d.p0 + cf + lane] : INT_MAX;
+    float px = 0.f, py = 0.f, pz = 0.f;
+    if (on) {
+      const float* p = a.x + 3ll * (d.p0 + id);
+      px = p[0];
+      py = p[1];
+      pz = p[2];
+    }
+    int rank = 0;
+    for (int j = 0; j < c; ++j) rank += __shfl_sync(kFull, id, j) < id;
+    if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
+    int minid = id;
+    for (int o = 16; o; o >>= 1) minid = min(minid, __shfl_xor_sync(kFull, minid, o));
+    bool fin = on && finite3(px, py, pz);
+    Entry e;
+    for (int l = 0; l < a.levels; ++l) {
+      bool mem = on && id < level_size(d.n, l);
+      int members = __popc(__ballot_sync(kFull, mem));
+      bool f = mem && fin;
+      Entry t;
+      t.lox = warp_min(f ? px : inf);
+      t.loy = warp_min(f ? py : inf);
+      t.loz = warp_min(f ? pz : inf);
+      t.hix = warp_max(f ? px : -inf);
+      t.hiy = warp_max(f ? py : -inf);
+      t.hiz = warp_max(f ? pz : -inf);
+      t.minid = minid;
+      t.ref = leaf_ref(cf, members ? members : 1);
+      if (lane == l) e = t;
+    }
+    if (code < 0) {
+      if (lane < a.levels) a.root[b * a.levels + lane] = e;
+      continue;
+    }
+    int node = code >> 1;
+    if (lane < a.levels) store_entry(node_entry(a.nodes, d, lane, node, code & 1), e);
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(a.counter + (d.p0 - b) + node, 1);
+    if (__shfl_sync(kFull, old, 0) == 0) continue;
+    climb(a, d, b, node, lane);
   }
 }
 
@@ -553,7 +585,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
       *counter = nullptr;
   unsigned* bounds = nullptr;
-  int4* range = nullptr;
+  int4* leaves = nullptr;  // leaf records; at most one per point
   long long inner = std::max<long long>(1, N - B);
   alloc((void**)&keys, sizeof(uint64_t) * N);
   alloc((void**)&keys2, sizeof(uint64_t) * N);
@@ -561,10 +593,11 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&vals2, sizeof(int) * N);
   alloc((void**)&hist, sizeof(int) * 256ll * B * max_tiles);
   alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
-  alloc((void**)&range, sizeof(int4) * inner);
+  alloc((void**)&leaves, sizeof(int4) * N);
   alloc((void**)&parent, sizeof(int) * inner);
-  alloc((void**)&counter, sizeof(int) * inner);
-  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * inner, s);
+  alloc((void**)&counter, sizeof(int) * (inner + 1));  // + leaf record count
+  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 1), s);
+  int* leaf_count = counter + inner;
 
   for (int b0 = 0; !e && b0 < B; b0 += 256) {
     DescChunk c;
@@ -591,20 +624,23 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
       std::swap(vals, vals2);
     }
     dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, range, parent);
+    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, f->leaf, leaves,
+                                     leaf_count);
     RefitArgs ra;
     ra.desc = f->desc;
     ra.x = x;
     ra.perm = vals;
-    ra.range = range;
     ra.parent = parent;
     ra.counter = counter;
+    ra.leaves = leaves;
+    ra.leaf_count = leaf_count;
     ra.pts = f->pts;
     ra.nodes = f->nodes;
     ra.root = f->root;
     ra.levels = f->levels;
-    ra.leaf = f->leaf;
-    refit_kernel<<<gk, 256, 0, s>>>(ra);
+    // persistent warps over the leaf records (count known on the device)
+    int leaf_blocks = (int)std::min<long long>(148 * 8, std::max<long long>(1, (N + 8 * 8 - 1) / (8 * 8)));
+    leaf_kernel<<<leaf_blocks, 256, 0, s>>>(ra);
     qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels, hist,
                                              max_tiles);
     seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
@@ -615,7 +651,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     count_launches((B + 255) / 256 + 2 + 24 + 2 + 3);
     e = cudaGetLastError();
   }
-  void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, range, parent,
+  void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, leaves, parent,
                      counter};
   for (void* p : scratch) {
     cudaError_t fe = pool_free(p, s);
