@@ -345,62 +345,62 @@ __device__ __forceinline__ Entry load_entry_cg(const Entry* e) {
   return r;
 }
 
-__device__ __forceinline__ float warp_min(float v) {
-  for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(kFull, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
-  return v;
+// Arrival counter increment with acquire-release semantics at device scope:
+// the caller's earlier node-entry stores are visible to whichever thread
+// later observes the incremented count, and that thread sees the sibling's
+// stores, without full memory fences.
+__device__ __forceinline__ int arrive(int* p) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;"
+               : "=r"(old)
+               : "l"(p)
+               : "memory");
+  return old;
 }
 
-// Bottom-up climb from completed node i, one lane per level: order the two
-// child entries by minimum ID, write the union into the parent's slot, and
-// continue while this warp is the second child to arrive.
-__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
-                      int lane) {
+// Bottom-up climb from completed node i, by one thread: order the two child
+// entries by minimum ID (the same order on every level), write their union
+// into the parent's slot, and continue while this thread is the second child
+// to arrive.
+__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
   const int* par = a.parent + (d.p0 - b);
   int* cnt = a.counter + (d.p0 - b);
-  bool mine = lane < a.levels;
   // Karras depth is below 97 (64 key bits + 32 index bits); the bound only
   // guards against a corrupted topology.
   for (int step = 0; step < 128; ++step) {
-    __threadfence();
-    Entry u;
-    if (mine) {
-      Entry u0 = load_entry_cg(node_entry(a.nodes, d, lane, i, 0));
-      Entry u1 = load_entry_cg(node_entry(a.nodes, d, lane, i, 1));
-      if (u1.minid < u0.minid) {  // same decision on every level
-        store_entry(node_entry(a.nodes, d, lane, i, 0), u1);
-        store_entry(node_entry(a.nodes, d, lane, i, 1), u0);
+    bool swap = load_entry_cg(node_entry(a.nodes, d, 0, i, 1)).minid <
+                load_entry_cg(node_entry(a.nodes, d, 0, i, 0)).minid;
+    int pc = i ? par[i] : 0;
+#pragma unroll
+    for (int l = 0; l < kMaxLevels; ++l) {
+      if (l >= a.levels) break;
+      Entry u = load_entry_cg(node_entry(a.nodes, d, l, i, 0));
+      Entry v = load_entry_cg(node_entry(a.nodes, d, l, i, 1));
+      if (swap) {
+        store_entry(node_entry(a.nodes, d, l, i, 0), v);
+        store_entry(node_entry(a.nodes, d, l, i, 1), u);
       }
-      u.lox = fminf(u0.lox, u1.lox); u.loy = fminf(u0.loy, u1.loy);
-      u.loz = fminf(u0.loz, u1.loz); u.hix = fmaxf(u0.hix, u1.hix);
-      u.hiy = fmaxf(u0.hiy, u1.hiy); u.hiz = fmaxf(u0.hiz, u1.hiz);
-      u.minid = min(u0.minid, u1.minid);
-      u.ref = i;
+      Entry e;
+      e.lox = fminf(u.lox, v.lox); e.loy = fminf(u.loy, v.loy);
+      e.loz = fminf(u.loz, v.loz); e.hix = fmaxf(u.hix, v.hix);
+      e.hiy = fmaxf(u.hiy, v.hiy); e.hiz = fmaxf(u.hiz, v.hiz);
+      e.minid = min(u.minid, v.minid);
+      e.ref = i;
+      if (i == 0)
+        a.root[b * a.levels + l] = e;
+      else
+        store_entry(node_entry(a.nodes, d, l, pc >> 1, pc & 1), e);
     }
-    if (i == 0) {
-      if (mine) a.root[b * a.levels + lane] = u;
-      return;
-    }
-    int pc = par[i];
-    int p = pc >> 1;
-    if (mine) store_entry(node_entry(a.nodes, d, lane, p, pc & 1), u);
-    __threadfence();
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(cnt + p, 1);
-    if (__shfl_sync(kFull, old, 0) == 0) return;
-    i = p;
+    if (i == 0 || arrive(cnt + (pc >> 1)) == 0) return;
+    i = pc >> 1;
   }
 }
 
 // One warp per leaf record: lane k takes sorted position first + k, ranks
-// its original ID among the leaf's IDs, writes pts in ascending ID order, and
-// the warp reduces one entry per level (box of finite members with
-// ID < n/4^l, member count, minimum ID).  Then the owner node is completed by
-// whichever child arrives second.
+// its original ID among the leaf's IDs and writes pts in ascending ID order;
+// per level, redux.sync min/max over order-preserving integer keys give the
+// box of the finite members with ID < n/4^l.  Lane 0 writes the entries and
+// completes the owner node if its sibling has arrived already.
 __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   int lane = threadIdx.x & 31;
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -423,37 +423,41 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
     int rank = 0;
     for (int j = 0; j < c; ++j) rank += __shfl_sync(kFull, id, j) < id;
     if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
-    int minid = id;
-    for (int o = 16; o; o >>= 1) minid = min(minid, __shfl_xor_sync(kFull, minid, o));
+    int minid = (int)__reduce_min_sync(kFull, (unsigned)id);
     bool fin = on && finite3(px, py, pz);
-    Entry e;
-    for (int l = 0; l < a.levels; ++l) {
+    unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
+    Entry* own = code < 0 ? nullptr : node_entry(a.nodes, d, 0, code >> 1, code & 1);
+#pragma unroll
+    for (int l = 0; l < kMaxLevels; ++l) {
+      if (l >= a.levels) break;
       bool mem = on && id < level_size(d.n, l);
       int members = __popc(__ballot_sync(kFull, mem));
       bool f = mem && fin;
       Entry t;
-      t.lox = warp_min(f ? px : inf);
-      t.loy = warp_min(f ? py : inf);
-      t.loz = warp_min(f ? pz : inf);
-      t.hix = warp_max(f ? px : -inf);
-      t.hiy = warp_max(f ? py : -inf);
-      t.hiz = warp_max(f ? pz : -inf);
+      t.lox = t.loy = t.loz = inf;
+      t.hix = t.hiy = t.hiz = -inf;
+      if (__ballot_sync(kFull, f)) {
+        t.lox = key_float(__reduce_min_sync(kFull, f ? kx : 0xffffffffu));
+        t.loy = key_float(__reduce_min_sync(kFull, f ? ky : 0xffffffffu));
+        t.loz = key_float(__reduce_min_sync(kFull, f ? kz : 0xffffffffu));
+        t.hix = key_float(__reduce_max_sync(kFull, f ? kx : 0u));
+        t.hiy = key_float(__reduce_max_sync(kFull, f ? ky : 0u));
+        t.hiz = key_float(__reduce_max_sync(kFull, f ? kz : 0u));
+      }
       t.minid = minid;
       t.ref = leaf_ref(cf, members ? members : 1);
-      if (lane == l) e = t;
+      if (lane == 0) {
+        if (own)
+          store_entry(own + (size_t)l * (d.n - 1) * 2, t);
+        else
+          a.root[b * a.levels + l] = t;
+      }
     }
-    if (code < 0) {
-      if (lane < a.levels) a.root[b * a.levels + lane] = e;
-      continue;
+    if (lane == 0 && own) {
+      int node = code >> 1;
+      if (arrive(a.counter + (d.p0 - b) + node) == 1) climb(a, d, b, node);
     }
-    int node = code >> 1;
-    if (lane < a.levels) store_entry(node_entry(a.nodes, d, lane, node, code & 1), e);
-    __threadfence();
     __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(a.counter + (d.p0 - b) + node, 1);
-    if (__shfl_sync(kFull, old, 0) == 0) continue;
-    climb(a, d, b, node, lane);
   }
 }
 
