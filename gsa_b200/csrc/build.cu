@@ -15,8 +15,9 @@
 //      written to `pts` in leaf order and ascending ID inside a leaf; per
 //      level child entries (box of the finite members with ID < n/4^l, the
 //      subtree's minimum ID, child/leaf reference); children stored in
-//      ascending minimum-ID order  (karras_kernel emits leaf records,
-//      leaf_kernel: one warp per leaf, then a one-lane-per-level climb)
+//      ascending minimum-ID order  (karras_kernel emits leaf records and
+//      seeds the arrival counters; leaf_kernel: a half-warp per leaf;
+//      climb_kernel: one thread per climb from each node with two leaves)
 //   6. per level, the IDs < n/4^l in leaf order, used as a spatially coherent
 //      query order for prefix queries               (qorder_* kernels)
 #include <algorithm>
@@ -273,9 +274,14 @@ __device__ __forceinline__ void emit_leaf(bool want, int4 rec, int4* list,
   if (want) list[base + __popc(mask & ((1u << lane) - 1u))] = rec;
 }
 
+// Arrival counters start at the number of leaf children (leaves are complete
+// before any climb starts); nodes whose two children are leaves are marked
+// kClimbStart and begin the bottom-up climb.
+constexpr int kClimbStart = 0x100;
+
 __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
-                              int* parent, int leaf, int4* leaves,
-                              int* leaf_count) {
+                              int* parent, int* counter, int leaf,
+                              int4* leaves, int* leaf_count) {
   int b = blockIdx.y;
   TreeDesc d = desc[b];
   int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -305,12 +311,16 @@ __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
     int first = min(i, j), last = max(i, j);
     if (first != gamma) par[gamma] = (i << 1) | 0;
     if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
+    int leaf_children = 0;
     if (last - first + 1 > leaf) {
       want0 = gamma - first + 1 <= leaf;
       want1 = last - gamma <= leaf;
       rec0 = make_int4(b, first, gamma, (i << 1) | 0);
       rec1 = make_int4(b, gamma + 1, last, (i << 1) | 1);
+      leaf_children = (int)want0 + (int)want1;
     }
+    counter[(d.p0 - b) + i] =
+        leaf_children == 2 ? (kClimbStart | 2) : leaf_children;
   }
   emit_leaf(want0, rec0, leaves, leaf_count);
   emit_leaf(want1, rec1, leaves, leaf_count);
@@ -396,23 +406,29 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
   }
 }
 
-// One warp per leaf record: lane k takes sorted position first + k, ranks
-// its original ID among the leaf's IDs and writes pts in ascending ID order;
-// per level, redux.sync min/max over order-preserving integer keys give the
-// box of the finite members with ID < n/4^l.  Lane 0 writes the entries and
-// completes the owner node if its sibling has arrived already.
+// Groups of G lanes (G = 16 for leaves of up to 16 points, else 32) each take
+// one leaf record: lane k takes sorted position first + k, ranks its
+// original ID among the leaf's IDs and writes pts in ascending ID order; per
+// level, redux.sync min/max over order-preserving integer keys give the box
+// of the finite members with ID < n/4^l; the group's first lane writes the
+// entries into the owner node's slot (or the root).  Two groups per warp
+// keep twice as many leaves in flight; no arrivals here -- the counters were
+// initialised with the leaf-child counts.
+template <int G>
 __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   int lane = threadIdx.x & 31;
-  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int warps = (gridDim.x * blockDim.x) >> 5;
+  int gl = lane & (G - 1);
+  unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
+  int group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
+  int groups = (gridDim.x * blockDim.x) / G;
   int total = *a.leaf_count;
   const float inf = __int_as_float(0x7f800000);
-  for (int r = warp; r < total; r += warps) {
+  for (int r = group; r < total; r += groups) {
     int4 rec = a.leaves[r];
     int b = rec.x, cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
     TreeDesc d = a.desc[b];
-    bool on = lane < c;
-    int id = on ? a.perm[d.p0 + cf + lane] : INT_MAX;
+    bool on = gl < c;
+    int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
     float px = 0.f, py = 0.f, pz = 0.f;
     if (on) {
       const float* p = a.x + 3ll * (d.p0 + id);
@@ -421,9 +437,9 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
       pz = p[2];
     }
     int rank = 0;
-    for (int j = 0; j < c; ++j) rank += __shfl_sync(kFull, id, j) < id;
+    for (int j = 0; j < c; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
     if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
-    int minid = (int)__reduce_min_sync(kFull, (unsigned)id);
+    int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
     bool fin = on && finite3(px, py, pz);
     unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
     Entry* own = code < 0 ? nullptr : node_entry(a.nodes, d, 0, code >> 1, code & 1);
@@ -431,34 +447,41 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
     for (int l = 0; l < kMaxLevels; ++l) {
       if (l >= a.levels) break;
       bool mem = on && id < level_size(d.n, l);
-      int members = __popc(__ballot_sync(kFull, mem));
+      int members = __popc(__ballot_sync(gmask, mem));
       bool f = mem && fin;
       Entry t;
       t.lox = t.loy = t.loz = inf;
       t.hix = t.hiy = t.hiz = -inf;
-      if (__ballot_sync(kFull, f)) {
-        t.lox = key_float(__reduce_min_sync(kFull, f ? kx : 0xffffffffu));
-        t.loy = key_float(__reduce_min_sync(kFull, f ? ky : 0xffffffffu));
-        t.loz = key_float(__reduce_min_sync(kFull, f ? kz : 0xffffffffu));
-        t.hix = key_float(__reduce_max_sync(kFull, f ? kx : 0u));
-        t.hiy = key_float(__reduce_max_sync(kFull, f ? ky : 0u));
-        t.hiz = key_float(__reduce_max_sync(kFull, f ? kz : 0u));
+      if (__ballot_sync(gmask, f)) {
+        t.lox = key_float(__reduce_min_sync(gmask, f ? kx : 0xffffffffu));
+        t.loy = key_float(__reduce_min_sync(gmask, f ? ky : 0xffffffffu));
+        t.loz = key_float(__reduce_min_sync(gmask, f ? kz : 0xffffffffu));
+        t.hix = key_float(__reduce_max_sync(gmask, f ? kx : 0u));
+        t.hiy = key_float(__reduce_max_sync(gmask, f ? ky : 0u));
+        t.hiz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
       }
       t.minid = minid;
       t.ref = leaf_ref(cf, members ? members : 1);
-      if (lane == 0) {
+      if (gl == 0) {
         if (own)
           store_entry(own + (size_t)l * (d.n - 1) * 2, t);
         else
           a.root[b * a.levels + l] = t;
       }
     }
-    if (lane == 0 && own) {
-      int node = code >> 1;
-      if (arrive(a.counter + (d.p0 - b) + node) == 1) climb(a, d, b, node);
-    }
-    __syncwarp();
   }
+}
+
+// One thread per internal node; nodes whose two children are leaves start a
+// climb.  Climbs run as independent threads, so every path of every tree
+// proceeds at once and a tree's refit takes about its depth in steps.
+__global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
+  int b = blockIdx.y;
+  TreeDesc d = a.desc[b];
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= d.n - 1) return;
+  if (!(a.counter[(d.p0 - b) + i] & kClimbStart)) return;
+  climb(a, d, b, i);
 }
 
 // ---------------------------------------------------------------------------
@@ -534,6 +557,26 @@ __global__ void __launch_bounds__(kSortThreads)
 
 inline int blocks_for(long long n, int per) {
   return (int)std::max<long long>(1, (n + per - 1) / per);
+}
+
+// Blocks of the leaf kernel: as many as stay resident on the device at once
+// (queried once per process), but no more than the records can use.
+int leaf_grid(bool half_warps, long long points) {
+  static int resident[2] = {0, 0};
+  int& r = resident[half_warps];
+  if (!r) {
+    int device = 0, sms = 148, per_sm = 4;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (half_warps)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, leaf_kernel<16>, 256, 0);
+    else
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, leaf_kernel<32>, 256, 0);
+    r = std::max(1, sms * std::max(1, per_sm));
+  }
+  long long groups_per_block = half_warps ? 16 : 8;
+  long long useful = (points / 2 + groups_per_block - 1) / groups_per_block;
+  return (int)std::max<long long>(1, std::min<long long>(r, useful));
 }
 
 }  // namespace
@@ -628,8 +671,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
       std::swap(vals, vals2);
     }
     dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, f->leaf, leaves,
-                                     leaf_count);
+    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, counter, f->leaf,
+                                     leaves, leaf_count);
     RefitArgs ra;
     ra.desc = f->desc;
     ra.x = x;
@@ -642,17 +685,23 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     ra.nodes = f->nodes;
     ra.root = f->root;
     ra.levels = f->levels;
-    // persistent warps over the leaf records (count known on the device)
-    int leaf_blocks = (int)std::min<long long>(148 * 8, std::max<long long>(1, (N + 8 * 8 - 1) / (8 * 8)));
-    leaf_kernel<<<leaf_blocks, 256, 0, s>>>(ra);
+    // resident lane groups loop over the leaf records (their count is only
+    // known on the device); at most one record per 2 points on average
+    int leaf_blocks = leaf_grid(f->leaf <= 16, N);
+    if (f->leaf <= 16)
+      leaf_kernel<16><<<leaf_blocks, 256, 0, s>>>(ra);
+    else
+      leaf_kernel<32><<<leaf_blocks, 256, 0, s>>>(ra);
+    climb_kernel<<<gk, 256, 0, s>>>(ra);
     qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels, hist,
                                              max_tiles);
     seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
                                         kSortTile);
     qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
                                                hist, max_tiles, f->qorder);
-    // upload chunks + bounds + morton + 8 x 3 sort + karras + refit + 3 qorder
-    count_launches((B + 255) / 256 + 2 + 24 + 2 + 3);
+    // upload chunks + bounds + morton + 8 x 3 sort + karras + leaf + climb +
+    // 3 qorder
+    count_launches((B + 255) / 256 + 2 + 24 + 3 + 3);
     e = cudaGetLastError();
   }
   void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, leaves, parent,
