@@ -324,8 +324,8 @@ __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
     counter[(d.p0 - b) + i] =
         leaf_children == 2 ? (kClimbStart | 2) : leaf_children;
   }
-  emit_leaf(want0, rec0, leaves, leaf_count);
-  emit_leaf(want1, rec1, leaves, leaf_count);
+  emit_leaf(want0, rec0, leaves + d.p0, leaf_count + b);
+  emit_leaf(want1, rec1, leaves + d.p0, leaf_count + b);
 }
 
 // ---------------------------------------------------------------------------
@@ -429,12 +429,13 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
   int group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
   int groups = (gridDim.x * blockDim.x) / G;
-  int total = *a.leaf_count;
+  const int b = blockIdx.y;
+  const TreeDesc d = a.desc[b];
+  int total = a.leaf_count[b];
   const float inf = __int_as_float(0x7f800000);
   for (int r = group; r < total; r += groups) {
-    int4 rec = a.leaves[r];
-    int b = rec.x, cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
-    TreeDesc d = a.desc[b];
+    int4 rec = a.leaves[d.p0 + r];
+    int cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
     bool on = gl < c;
     int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
     float px = 0.f, py = 0.f, pz = 0.f;
@@ -630,6 +631,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   __shared__ int wcnt[kSmallWarps][256];
   __shared__ unsigned long long warp_tot[32];
   __shared__ float red[2][3][32];
+  __shared__ int s_count;
   const int b = blockIdx.x;
   const TreeDesc d = a.desc[b];
   const int n = d.n;
@@ -747,7 +749,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   for (int i = t; i < n; i += kSmallThreads)
     a.perm[d.p0 + i] = (int)(sk[i] & 0xffffu);
 
-  // 5. Karras topology from the sorted (unique) words
+  // 5. Karras topology from the sorted (unique) words; leaf records are
+  //    counted in shared memory and stored in this tree's own region
+  if (t == 0) s_count = 0;
+  __syncthreads();
   int* par = a.parent + (d.p0 - b);
   int* cnt = a.counter + (d.p0 - b);
   auto cp = [&](int i, int j) -> int {
@@ -787,9 +792,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       }
       cnt[i] = leaf_children == 2 ? (kClimbStart | 2) : leaf_children;
     }
-    emit_leaf(want0, rec0, a.leaves, a.leaf_count);
-    emit_leaf(want1, rec1, a.leaves, a.leaf_count);
+    emit_leaf(want0, rec0, a.leaves + d.p0, &s_count);
+    emit_leaf(want1, rec1, a.leaves + d.p0, &s_count);
   }
+  __syncthreads();
+  if (t == 0) a.leaf_count[b] = s_count;
 }
 
 // Per-level query order of a small tree in one block: thread t
@@ -831,24 +838,13 @@ inline int blocks_for(long long n, int per) {
   return (int)std::max<long long>(1, (n + per - 1) / per);
 }
 
-// Blocks of the leaf kernel: as many as stay resident on the device at once
-// (queried once per process), but no more than the records can use.
-int leaf_grid(bool half_warps, long long points) {
-  static int resident[2] = {0, 0};
-  int& r = resident[half_warps];
-  if (!r) {
-    int device = 0, sms = 148, per_sm = 4;
-    cudaGetDevice(&device);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    if (half_warps)
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, leaf_kernel<16>, 256, 0);
-    else
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, leaf_kernel<32>, 256, 0);
-    r = std::max(1, sms * std::max(1, per_sm));
-  }
+// Blocks per tree of the leaf kernel (grid.y = tree): enough lane groups for
+// one leaf record per 8 points (leaves hold about 10 points on average; the
+// groups loop over any excess), never more than the largest tree can use.
+int leaf_grid(bool half_warps, long long max_points) {
   long long groups_per_block = half_warps ? 16 : 8;
-  long long useful = (points / 2 + groups_per_block - 1) / groups_per_block;
-  return (int)std::max<long long>(1, std::min<long long>(r, useful));
+  long long records = (max_points + 7) / 8;
+  return (int)std::max<long long>(1, (records + groups_per_block - 1) / groups_per_block);
 }
 
 }  // namespace
@@ -922,8 +918,9 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   }
   alloc((void**)&leaves, sizeof(int4) * N);
   alloc((void**)&parent, sizeof(int) * inner);
-  alloc((void**)&counter, sizeof(int) * (inner + 1));  // + leaf record count
-  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 1), s);
+  // arrival counters + one leaf-record count per tree
+  alloc((void**)&counter, sizeof(int) * (inner + B));
+  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + B), s);
   int* leaf_count = counter + inner;
 
   for (int b0 = 0; !e && b0 < B; b0 += 256) {
@@ -989,13 +986,13 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     ra.nodes = f->nodes;
     ra.root = f->root;
     ra.levels = f->levels;
-    // resident lane groups loop over the leaf records (their count is only
-    // known on the device); at most one record per 2 points on average
-    int leaf_blocks = leaf_grid(f->leaf <= 16, N);
+    // lane groups of each tree loop over its leaf records (their count is
+    // only known on the device)
+    dim3 gl(leaf_grid(f->leaf <= 16, max_n), B);
     if (f->leaf <= 16)
-      leaf_kernel<16><<<leaf_blocks, 256, 0, s>>>(ra);
+      leaf_kernel<16><<<gl, 256, 0, s>>>(ra);
     else
-      leaf_kernel<32><<<leaf_blocks, 256, 0, s>>>(ra);
+      leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
     climb_kernel<<<gk, 256, 0, s>>>(ra);
     launches += 2;
     if (small) {
