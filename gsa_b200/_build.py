@@ -42,9 +42,8 @@ _WALK_ONLY = ["-DGSA_RADIUS_SCAN_MAX=0", "-DGSA_KNN_SCAN_MAX=0"]
 LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),
-    # test variants: tree walk for every support size and the general
-    # (multi-launch) build for every tree size; and a 4-entry stack
-    "gsa_bvh_walk": (_BVH, _WALK_ONLY + ["-DGSA_GENERAL_BUILD_ONLY"]),
+    # test variants: tree walk for every support size; and a 4-entry stack
+    "gsa_bvh_walk": (_BVH, _WALK_ONLY),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

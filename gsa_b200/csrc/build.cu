@@ -564,276 +564,6 @@ __global__ void __launch_bounds__(kSortThreads)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Small-tree front end: one 768-thread block builds the topology of a tree
-// of at most kSmallMax points entirely in shared memory -- bounds of the
-// finite points, one 64-bit word per point (48-bit Morton code << 16 | point
-// index; the index makes every word unique, so the sort is stable and Karras'
-// common-prefix needs no tie-break), a 6-pass LSD radix sort of the words
-// (8 bits per pass over bits 16..63), and the Karras topology, leaf records
-// and arrival counters from the sorted words.  It replaces 28 launches of the
-// general path (bounds, Morton, 8 x 3 sort passes, Karras) with one.
-constexpr int kSmallThreads = 768;
-constexpr int kSmallItems = 32;
-constexpr int kSmallMax = kSmallThreads * kSmallItems;  // 24,576 points
-constexpr int kSmallWarps = kSmallThreads / 32;
-constexpr size_t kSmallSmem = sizeof(unsigned long long) * kSmallMax;
-
-struct SmallArgs {
-  const TreeDesc* desc;
-  const float* x;
-  int* perm;
-  int* parent;
-  int* counter;
-  int4* leaves;
-  int* leaf_count;
-  int leaf;
-};
-
-// Inclusive scan of one 64-bit value per thread over the block (<= 32 warps).
-__device__ __forceinline__ unsigned long long block_scan_incl(
-    unsigned long long v, unsigned long long* warp_tot) {
-  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int warps = blockDim.x >> 5;
-  for (int o = 1; o < 32; o <<= 1) {
-    unsigned long long u = __shfl_up_sync(kFull, v, o);
-    if (lane >= o) v += u;
-  }
-  if (lane == 31) warp_tot[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    unsigned long long t = lane < warps ? warp_tot[lane] : 0;
-    for (int o = 1; o < 32; o <<= 1) {
-      unsigned long long u = __shfl_up_sync(kFull, t, o);
-      if (lane >= o) t += u;
-    }
-    if (lane < warps) warp_tot[lane] = t;
-  }
-  __syncthreads();
-  if (warp) v += warp_tot[warp - 1];
-  __syncthreads();
-  return v;
-}
-
-__device__ __forceinline__ uint64_t spread3_16(unsigned v) {
-  uint64_t x = v & 0xffffu;
-  x = (x | x << 32) & 0x1f00000000ffffull;
-  x = (x | x << 16) & 0x1f0000ff0000ffull;
-  x = (x | x << 8) & 0x100f00f00f00f00full;
-  x = (x | x << 4) & 0x10c30c30c30c30c3ull;
-  x = (x | x << 2) & 0x1249249249249249ull;
-  return x;
-}
-
-__global__ void __launch_bounds__(kSmallThreads, 1)
-    small_topology_kernel(SmallArgs a) {
-  extern __shared__ unsigned long long sk[];
-  __shared__ int wcnt[kSmallWarps][256];
-  __shared__ unsigned long long warp_tot[32];
-  __shared__ float red[2][3][32];
-  __shared__ int s_count;
-  const int b = blockIdx.x;
-  const TreeDesc d = a.desc[b];
-  const int n = d.n;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const float* xb = a.x + 3ll * d.p0;
-
-  // 1. bounds of the finite points
-  float lo[3] = {INFINITY, INFINITY, INFINITY};
-  float hi[3] = {-INFINITY, -INFINITY, -INFINITY};
-  for (int i = t; i < n; i += kSmallThreads) {
-    float p0 = xb[3 * i], p1 = xb[3 * i + 1], p2 = xb[3 * i + 2];
-    if (finite3(p0, p1, p2)) {
-      lo[0] = fminf(lo[0], p0); lo[1] = fminf(lo[1], p1); lo[2] = fminf(lo[2], p2);
-      hi[0] = fmaxf(hi[0], p0); hi[1] = fmaxf(hi[1], p1); hi[2] = fmaxf(hi[2], p2);
-    }
-  }
-  for (int k = 0; k < 3; ++k) {
-    for (int o = 16; o; o >>= 1) {
-      lo[k] = fminf(lo[k], __shfl_xor_sync(kFull, lo[k], o));
-      hi[k] = fmaxf(hi[k], __shfl_xor_sync(kFull, hi[k], o));
-    }
-    if (lane == 0) {
-      red[0][k][warp] = lo[k];
-      red[1][k][warp] = hi[k];
-    }
-  }
-  __syncthreads();
-  for (int k = 0; k < 3; ++k) {
-    lo[k] = red[0][k][lane];
-    hi[k] = red[1][k][lane];
-    for (int o = 16; o; o >>= 1) {
-      lo[k] = fminf(lo[k], __shfl_xor_sync(kFull, lo[k], o));
-      hi[k] = fmaxf(hi[k], __shfl_xor_sync(kFull, hi[k], o));
-    }
-  }
-  float ext = 0.f;
-  bool any = lo[0] <= hi[0];
-  for (int k = 0; k < 3; ++k) {
-    if (!any) lo[k] = hi[k] = 0.f;
-    ext = fmaxf(ext, hi[k] - lo[k]);
-  }
-  float scale = (ext > 0.f && isfinite(ext)) ? 65535.f / ext : 0.f;
-
-  // 2. words, warp-striped: item j of lane L of warp w is position
-  //    w*32*ITEMS + j*32 + L (position order = warp, then item, then lane)
-  unsigned long long key[kSmallItems];
-  const int wbase = warp * 32 * kSmallItems;
-#pragma unroll
-  for (int j = 0; j < kSmallItems; ++j) {
-    int pos = wbase + j * 32 + lane;
-    unsigned long long w = ~0ull;
-    if (pos < n) {
-      auto q = [&](float v, int k) {
-        float s = (v - lo[k]) * scale;
-        return !(s >= 0.f) ? 0u : (s >= 65535.f ? 65535u : (unsigned)s);
-      };
-      uint64_t m = (spread3_16(q(xb[3 * pos], 0)) << 2) |
-                   (spread3_16(q(xb[3 * pos + 1], 1)) << 1) |
-                   spread3_16(q(xb[3 * pos + 2], 2));
-      w = (m << 16) | (unsigned)pos;
-    }
-    key[j] = w;
-  }
-
-  // 3. LSD radix sort, 8 bits per pass over bits 16..63
-  const unsigned lt = (1u << lane) - 1u;
-  for (int pass = 0; pass < 6; ++pass) {
-    const int shift = 16 + 8 * pass;
-    for (int dgt = lane; dgt < 256; dgt += 32) wcnt[warp][dgt] = 0;
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < kSmallItems; ++j) {
-      int dgt = (int)((key[j] >> shift) & 255);
-      unsigned peers = __match_any_sync(kFull, dgt);
-      if ((peers & lt) == 0) wcnt[warp][dgt] += __popc(peers);
-      __syncwarp();
-    }
-    __syncthreads();
-    // exclusive scan over (digit, warp), digit-major
-    {
-      constexpr int per = 256 * kSmallWarps / kSmallThreads;  // entries/thread
-      static_assert(per * kSmallThreads == 256 * kSmallWarps, "scan split");
-      int e0 = t * per;  // entry e = digit * warps + warp
-      unsigned long long s = 0;
-      for (int e = e0; e < e0 + per; ++e) s += wcnt[e % kSmallWarps][e / kSmallWarps];
-      unsigned long long incl = block_scan_incl(s, warp_tot);
-      unsigned long long run = incl - s;
-      for (int e = e0; e < e0 + per; ++e) {
-        int& c = wcnt[e % kSmallWarps][e / kSmallWarps];
-        int v = c;
-        c = (int)run;
-        run += v;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < kSmallItems; ++j) {
-      int dgt = (int)((key[j] >> shift) & 255);
-      unsigned peers = __match_any_sync(kFull, dgt);
-      int base = wcnt[warp][dgt];
-      __syncwarp();
-      if ((peers & lt) == 0) wcnt[warp][dgt] = base + __popc(peers);
-      __syncwarp();
-      sk[base + __popc(peers & lt)] = key[j];
-    }
-    __syncthreads();
-    if (pass < 5) {
-#pragma unroll
-      for (int j = 0; j < kSmallItems; ++j) key[j] = sk[wbase + j * 32 + lane];
-      __syncthreads();
-    }
-  }
-
-  // 4. sorted point indices
-  for (int i = t; i < n; i += kSmallThreads)
-    a.perm[d.p0 + i] = (int)(sk[i] & 0xffffu);
-
-  // 5. Karras topology from the sorted (unique) words; leaf records are
-  //    counted in shared memory and stored in this tree's own region
-  if (t == 0) s_count = 0;
-  __syncthreads();
-  int* par = a.parent + (d.p0 - b);
-  int* cnt = a.counter + (d.p0 - b);
-  auto cp = [&](int i, int j) -> int {
-    return (j < 0 || j >= n) ? -1 : __clzll(sk[i] ^ sk[j]);
-  };
-  for (int base = 0; base < max(n - 1, 1); base += kSmallThreads) {
-    int i = base + t;
-    bool valid = i < n - 1;
-    int4 rec0 = make_int4(b, 0, n - 1, -1), rec1 = rec0;
-    bool want0 = i == 0 && n <= a.leaf, want1 = false;
-    if (valid) {
-      int dir = cp(i, i + 1) > cp(i, i - 1) ? 1 : -1;
-      int dmin = cp(i, i - dir);
-      int lmax = 2;
-      while (cp(i, i + lmax * dir) > dmin) lmax <<= 1;
-      int l = 0;
-      for (int s = lmax >> 1; s >= 1; s >>= 1)
-        if (cp(i, i + (l + s) * dir) > dmin) l += s;
-      int j = i + l * dir;
-      int dnode = cp(i, j);
-      int s = 0, u = l;
-      do {
-        u = (u + 1) >> 1;
-        if (cp(i, i + (s + u) * dir) > dnode) s += u;
-      } while (u > 1);
-      int gamma = i + s * dir + min(dir, 0);
-      int first = min(i, j), last = max(i, j);
-      if (first != gamma) par[gamma] = (i << 1) | 0;
-      if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
-      int leaf_children = 0;
-      if (last - first + 1 > a.leaf) {
-        want0 = gamma - first + 1 <= a.leaf;
-        want1 = last - gamma <= a.leaf;
-        rec0 = make_int4(b, first, gamma, (i << 1) | 0);
-        rec1 = make_int4(b, gamma + 1, last, (i << 1) | 1);
-        leaf_children = (int)want0 + (int)want1;
-      }
-      cnt[i] = leaf_children == 2 ? (kClimbStart | 2) : leaf_children;
-    }
-    emit_leaf(want0, rec0, a.leaves + d.p0, &s_count);
-    emit_leaf(want1, rec1, a.leaves + d.p0, &s_count);
-  }
-  __syncthreads();
-  if (t == 0) a.leaf_count[b] = s_count;
-}
-
-// Per-level query order of a small tree in one block: thread t
-// owns positions [t*ITEMS, (t+1)*ITEMS); the four level counts are packed in
-// 16-bit fields of one 64-bit value and scanned once.
-__global__ void __launch_bounds__(kSmallThreads)
-    small_qorder_kernel(const TreeDesc* desc, const float4* pts, int levels,
-                        int* qorder) {
-  __shared__ unsigned long long warp_tot[32];
-  TreeDesc d = desc[blockIdx.x];
-  int n = d.n;
-  int p0 = threadIdx.x * kSmallItems;
-  unsigned long long mine = 0;
-  for (int k = 0; k < kSmallItems; ++k) {
-    int pos = p0 + k;
-    if (pos >= n) break;
-    int id = __float_as_int(pts[d.p0 + pos].w);
-    for (int l = 0; l < levels; ++l)
-      if (id < level_size(n, l)) mine += 1ull << (16 * l);
-  }
-  unsigned long long run = block_scan_incl(mine, warp_tot) - mine;
-  int off[kMaxLevels];
-  int o = 0;
-  for (int l = 0; l < kMaxLevels; ++l) {
-    off[l] = o + (int)((run >> (16 * l)) & 0xffff);
-    o += l < levels ? level_size(n, l) : 0;
-  }
-  int* out = qorder + d.q0;
-  for (int k = 0; k < kSmallItems; ++k) {
-    int pos = p0 + k;
-    if (pos >= n) break;
-    int id = __float_as_int(pts[d.p0 + pos].w);
-    for (int l = 0; l < levels; ++l)
-      if (id < level_size(n, l)) out[off[l]++] = id;
-  }
-}
-
 inline int blocks_for(long long n, int per) {
   return (int)std::max<long long>(1, (n + per - 1) / per);
 }
@@ -896,12 +626,6 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->root, sizeof(Entry) * B * f->levels);
   alloc((void**)&f->qorder, sizeof(int) * std::max<long long>(1, q_total));
   int max_tiles = blocks_for(max_n, kSortTile);
-  // trees of at most kSmallMax points take the one-block-per-tree front end
-#ifdef GSA_GENERAL_BUILD_ONLY
-  const bool small = false;
-#else
-  const bool small = max_n <= kSmallMax;
-#endif
   uint64_t *keys = nullptr, *keys2 = nullptr;
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
       *counter = nullptr;
@@ -909,13 +633,11 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   int4* leaves = nullptr;  // leaf records; at most one per point
   long long inner = std::max<long long>(1, N - B);
   alloc((void**)&vals, sizeof(int) * N);
-  if (!small) {
-    alloc((void**)&keys, sizeof(uint64_t) * N);
-    alloc((void**)&keys2, sizeof(uint64_t) * N);
-    alloc((void**)&vals2, sizeof(int) * N);
-    alloc((void**)&hist, sizeof(int) * 256ll * B * max_tiles);
-    alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
-  }
+  alloc((void**)&keys, sizeof(uint64_t) * N);
+  alloc((void**)&keys2, sizeof(uint64_t) * N);
+  alloc((void**)&vals2, sizeof(int) * N);
+  alloc((void**)&hist, sizeof(int) * 256ll * B * max_tiles);
+  alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
   alloc((void**)&leaves, sizeof(int4) * N);
   alloc((void**)&parent, sizeof(int) * inner);
   // arrival counters + one leaf-record count per tree
@@ -933,27 +655,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   int launches = (B + 255) / 256;
   dim3 gs(max_tiles, B);
   dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-  if (!e && small) {
-    static bool smem_set = false;
-    if (!smem_set) {
-      e = cudaFuncSetAttribute(small_topology_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kSmallSmem);
-      smem_set = !e;
-    }
-    SmallArgs sa;
-    sa.desc = f->desc;
-    sa.x = x;
-    sa.perm = vals;
-    sa.parent = parent;
-    sa.counter = counter;
-    sa.leaves = leaves;
-    sa.leaf_count = leaf_count;
-    sa.leaf = f->leaf;
-    if (!e)
-      small_topology_kernel<<<B, kSmallThreads, kSmallSmem, s>>>(sa);
-    launches += 1;
-  } else if (!e) {
+  if (!e) {
     dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
     bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
     dim3 gm(std::min(blocks_for(max_n, 256), 1024), B);
@@ -994,20 +696,13 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     else
       leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
     climb_kernel<<<gk, 256, 0, s>>>(ra);
-    launches += 2;
-    if (small) {
-      small_qorder_kernel<<<B, kSmallThreads, 0, s>>>(f->desc, f->pts,
-                                                       f->levels, f->qorder);
-      launches += 1;
-    } else {
-      qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
-                                               hist, max_tiles);
-      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
-                                          kSortTile);
-      qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
-                                                 hist, max_tiles, f->qorder);
-      launches += 3;
-    }
+    qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
+                                             hist, max_tiles);
+    seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
+                                        kSortTile);
+    qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
+                                               hist, max_tiles, f->qorder);
+    launches += 5;
     count_launches(launches);
     e = cudaGetLastError();
   }
