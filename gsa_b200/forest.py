@@ -92,9 +92,10 @@ class Forest:
         if isinstance(counts, int):
             counts = [counts] * len(self.sizes)
         qseg, host, dev = self._offsets(counts, q.device)
+        # queries may run on any stream ordered after the build (several
+        # stages can run concurrently); close() must be ordered after them
         if not (
             self.ptr
-            and er._stream() == self.stream
             and er._is_points(q)
             and q.device == self.x.device
             and len(qseg) == len(self.sizes) + 1

@@ -18,6 +18,7 @@ and 3NN traversal of every scene, one batched value check and one batched
 row gather per stage); its outputs equal ``run_session``'s for every scene.
 """
 
+import contextlib
 import ctypes
 
 import torch
@@ -69,6 +70,7 @@ class Batch:
         self.sizes = tuple(sizes)
         self.radii = tuple(radii)
         self.leaf = leaf
+        self._streams = {}
 
     def _level(self, size, n):
         for level in range(4):
@@ -84,46 +86,109 @@ class Batch:
             z[f"hit{s}"] = torch.empty((B * self.sizes[s + 1], K), dtype=torch.int32, device=device)
             z[f"nnd{s}"] = torch.empty((B * self.sizes[s], 3), device=device)
             z[f"nni{s}"] = torch.empty((B * self.sizes[s], 3), dtype=torch.int32, device=device)
-        z["flags"] = torch.zeros(2 * B, dtype=torch.int32, device=device)
-        z["hits"] = torch.zeros(B, dtype=torch.int32, device=device)
+        z["flags"] = torch.zeros((4, 2 * B), dtype=torch.int32, device=device)
+        z["hits"] = torch.zeros((4, B), dtype=torch.int32, device=device)
         z["snapshot"] = torch.empty((B, self.sizes[0], 3), device=device)
         return z
 
-    def run(self, X, out=None, mark=None):
+    def _side_streams(self, device):
+        streams = self._streams.get(device)
+        if streams is None:
+            streams = self._streams[device] = [torch.cuda.Stream(device) for _ in range(8)]
+        return streams
+
+    def run(self, X, out=None, timer=None, concurrent=True):
         """X: CUDA float32 (B, N, 3), N == sizes[0], each scene FPS-ordered.
-        ``mark(name)``, if given, is called after each phase (e.g. to record
-        a CUDA event): build, ball<s>, reuse<s>, nn<s>."""
+
+        After the forest build, the eight query stages (radius + reuse for
+        s = 0..3, 3NN for s = 0..3) depend only on the build, so with
+        ``concurrent`` they run on eight streams and the small, latency-bound
+        stages overlap the large ones; the caller's stream waits for all of
+        them.  ``timer.span(name)``, if given, brackets each stage on the
+        stream it runs on (build, ball<s>, reuse<s>, nn<s>)."""
         B, N = X.shape[0], X.shape[1]
         if not (X.is_cuda and X.is_contiguous() and X.dtype == torch.float32 and N == self.sizes[0]):
             raise ValueError("Batch.run needs contiguous CUDA FP32 (B, sizes[0], 3)")
         out = out if out is not None else self.allocate(B, X.device)
-        mark = mark or (lambda name: None)
-        stream = er._stream()
+        timer = timer or _NoTimer()
+        main = torch.cuda.current_stream()
         snap = out["snapshot"]
-        snap.copy_(X)  # retained snapshot of every support, as the session keeps
-        forest = Forest(X.view(-1, 3), [i * N for i in range(B + 1)], prefix=True, leaf=self.leaf)
-        mark("build")
-        flags, hitflags = out["flags"], out["hits"]
-        for s in range(4):
+        with timer.span("build"):
+            snap.copy_(X)  # retained snapshot of every support, as the session keeps
+            forest = Forest(X.view(-1, 3), [i * N for i in range(B + 1)], prefix=True, leaf=self.leaf)
+
+        def radius_stage(s):
             n_s, n_q = self.sizes[s], self.sizes[s + 1]
             rows = out[f"ball{s}"]
-            forest.ball_prefix(n_s, s, self.radii[s], K, rows)
-            mark(f"ball{s}")
+            flags, hitflags = out["flags"][s], out["hits"][s]
+            with timer.span(f"ball{s}"):
+                forest.ball_prefix(n_s, s, self.radii[s], K, rows)
             # reuse admission: support P_s and query prefix P_{s+1} equal the
             # retained snapshot, then gather the first n_q rows of each scene
-            er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, flags.data_ptr(), 2, stream))
-            er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, flags.data_ptr() + 4, 2, stream))
-            er.check(
-                er.lib.reuse_rows_batch(
-                    B, rows.data_ptr(), n_s * K, K, flags.data_ptr(), n_q, K,
-                    out[f"hit{s}"].data_ptr(), n_q * K, hitflags.data_ptr(), stream,
+            with timer.span(f"reuse{s}"):
+                stream = er._stream()
+                er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, flags.data_ptr(), 2, stream))
+                er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, flags.data_ptr() + 4, 2, stream))
+                er.check(
+                    er.lib.reuse_rows_batch(
+                        B, rows.data_ptr(), n_s * K, K, flags.data_ptr(), n_q, K,
+                        out[f"hit{s}"].data_ptr(), n_q * K, hitflags.data_ptr(), stream,
+                    )
                 )
-            )
-            mark(f"reuse{s}")
-        for s in range(3, -1, -1):
+
+        def nn_stage(s):
             m = self.sizes[s + 1]
             level = self._level(m, N)
-            forest.query_prefix(self.sizes[s], level, out[f"nnd{s}"], out[f"nni{s}"], m=m if m != N >> (2 * level) else 0)
-            mark(f"nn{s}")
+            with timer.span(f"nn{s}"):
+                forest.query_prefix(self.sizes[s], level, out[f"nnd{s}"], out[f"nni{s}"], m=m if m != N >> (2 * level) else 0)
+
+        stages = []
+        for s in range(4):  # largest stages first, so small ones fill gaps
+            stages += [lambda s=s: radius_stage(s), lambda s=s: nn_stage(s)]
+        if concurrent:
+            built = torch.cuda.Event()
+            built.record(main)
+            done = []
+            for job, stream in zip(stages, self._side_streams(X.device)):
+                stream.wait_event(built)
+                with torch.cuda.stream(stream):
+                    job()
+                    ev = torch.cuda.Event()
+                    ev.record(stream)
+                done.append(ev)
+            for ev in done:
+                main.wait_event(ev)
+        else:
+            for job in stages:
+                job()
         forest.close()
         return out
+
+
+class _NoTimer:
+    @contextlib.contextmanager
+    def span(self, name):
+        yield
+
+
+class StageTimer:
+    """CUDA events around each stage, recorded on the stream it runs on."""
+
+    def __init__(self):
+        self.records = []
+
+    @contextlib.contextmanager
+    def span(self, name):
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
+        yield
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        self.records.append((name, start, end))
+
+    def totals(self):
+        """Milliseconds per stage name (call after synchronising)."""
+        t = {}
+        for name, start, end in self.records:
+            t[name] = t.get(name, 0.0) + start.elapsed_time(end)
+        return t

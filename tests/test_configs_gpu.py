@@ -81,7 +81,11 @@ def test_batch_equals_session_per_scene():
     X = _room(seeds)
     eng = hz.Batch()
     out = eng.run(X)
-    assert out["hits"].sum().item() == len(seeds)
+    assert out["hits"].sum().item() == 4 * len(seeds)
+    serial = eng.run(X, eng.allocate(len(seeds), X.device), concurrent=False)
+    for key in out:
+        if key.startswith(("ball", "hit", "nn")):
+            assert torch.equal(out[key], serial[key]), key
     torch.cuda.synchronize()
     for b in range(len(seeds)):
         with QuerySession() as s:
