@@ -8,6 +8,7 @@
 //
 // One 1024-thread block per scene; the running minimum lives in shared memory
 // (4 bytes per point), coordinates are re-read from L2 each step.
+#include <algorithm>
 #include "common.cuh"
 
 namespace gsa {
@@ -79,10 +80,147 @@ __global__ void __launch_bounds__(kFpsThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Large scenes: one cooperative grid (every block resident) per scene, PER
+// points per thread in registers.  Per step each block reduces its best
+// (distance, lowest index), one atomicMax on a packed 64-bit key per block
+// selects the global best, and a grid barrier separates steps.  The winner
+// slot is triple-buffered so it can be cleared two steps ahead without a
+// second barrier.
+constexpr long long kBarrierSpins = 1ll << 24;
+
+__device__ __forceinline__ unsigned order_key(float f) {
+  unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Grid barrier with a bounded wait: on timeout it sets *err and returns.
+__device__ void grid_barrier(unsigned* count, unsigned* gen, int* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned g = *reinterpret_cast<volatile unsigned*>(gen);
+    __threadfence();
+    if (atomicAdd(count, 1u) == gridDim.x - 1) {
+      *count = 0;
+      __threadfence();
+      atomicAdd(gen, 1u);
+    } else {
+      long long spins = 0;
+      while (*reinterpret_cast<volatile unsigned*>(gen) == g) {
+        if (++spins > kBarrierSpins) {
+          atomicExch(err, 1);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+template <int PER>
+__global__ void __launch_bounds__(kFpsThreads)
+    fps_grid_kernel(int n, const float* x, int start, int* order,
+                    unsigned long long* best, unsigned* bar, int* err) {
+  __shared__ unsigned long long wbest[32];
+  const int threads = gridDim.x * kFpsThreads;
+  const int tid = blockIdx.x * kFpsThreads + threadIdx.x;
+  float px[PER], py[PER], pz[PER], md[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int i = tid + k * threads;
+    md[k] = i < n ? __int_as_float(0x7f800000) : -2.f;
+    px[k] = i < n ? x[3ll * i] : 0.f;
+    py[k] = i < n ? x[3ll * i + 1] : 0.f;
+    pz[k] = i < n ? x[3ll * i + 2] : 0.f;
+  }
+  int cur = start;
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int it = 0; it < n; ++it) {
+    if (tid == 0) order[it] = cur;
+    float cx = __ldg(x + 3ll * cur), cy = __ldg(x + 3ll * cur + 1),
+          cz = __ldg(x + 3ll * cur + 2);
+    unsigned long long mine = 0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = tid + k * threads;
+      if (i == cur) {
+        md[k] = -1.f;
+      } else if (md[k] >= 0.f) {
+        md[k] = fminf(md[k], exact_d2(px[k], py[k], pz[k], cx, cy, cz));
+      }
+      if (i < n) {
+        unsigned long long key =
+            ((unsigned long long)order_key(md[k]) << 32) | (0xffffffffu - (unsigned)i);
+        mine = key > mine ? key : mine;
+      }
+    }
+    for (int o = 16; o; o >>= 1) {
+      unsigned long long u = __shfl_xor_sync(kFull, mine, o);
+      mine = u > mine ? u : mine;
+    }
+    if (lane == 0) wbest[warp] = mine;
+    __syncthreads();
+    if (warp == 0) {
+      mine = lane < kFpsThreads / 32 ? wbest[lane] : 0;
+      for (int o = 16; o; o >>= 1) {
+        unsigned long long u = __shfl_xor_sync(kFull, mine, o);
+        mine = u > mine ? u : mine;
+      }
+      if (lane == 0) atomicMax(best + it % 3, mine);
+    }
+    grid_barrier(bar, bar + 1, err);
+    if (*reinterpret_cast<volatile int*>(err)) return;
+    unsigned long long win = *reinterpret_cast<volatile unsigned long long*>(best + it % 3);
+    cur = (int)(0xffffffffu - (unsigned)(win & 0xffffffffu));
+    if (tid == 0) best[(it + 2) % 3] = 0;
+  }
+}
+
+template <int PER>
+cudaError_t launch_fps_grid(int n, const float* x, int start, int* order,
+                            unsigned long long* best, unsigned* bar, int* err,
+                            int blocks, cudaStream_t s) {
+  void* args[] = {&n, &x, &start, &order, &best, &bar, &err};
+  return cudaLaunchCooperativeKernel((const void*)fps_grid_kernel<PER>,
+                                     dim3(blocks), dim3(kFpsThreads), args, 0,
+                                     s);
+}
+
 }  // namespace
 }  // namespace gsa
 
 using namespace gsa;
+
+// See include/gsa_bvh.h.
+GSA_API int fps_order_large(int n, const float* x, int start, int* order,
+                            void* scratch, int* err, void* stream) {
+  if (n < 1 || !x || !order || !scratch || !err || start < 0 || start >= n)
+    return -2;
+  cudaStream_t s = (cudaStream_t)stream;
+  int device = 0, sms = 0, per_sm = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (!e) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (!e)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, fps_grid_kernel<8>, kFpsThreads, 0);
+  if (e) return e;
+  int blocks = sms * std::min(per_sm, 1);
+  long long threads = (long long)blocks * kFpsThreads;
+  unsigned long long* best = static_cast<unsigned long long*>(scratch);
+  unsigned* bar = reinterpret_cast<unsigned*>(best + 3);
+  e = cudaMemsetAsync(scratch, 0, 64, s);
+  if (!e) e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e) return e;
+  if (n > threads * 8) return -2;  // at most 8 points per thread
+  count_launches();
+  if (n <= threads * 2)
+    e = launch_fps_grid<2>(n, x, start, order, best, bar, err, blocks, s);
+  else
+    e = launch_fps_grid<8>(n, x, start, order, best, bar, err, blocks, s);
+  return e ? (int)e : (int)cudaGetLastError();
+}
 
 // See include/gsa_bvh.h.
 GSA_API int fps_order(int b, int n, const float* x, const int* start,

@@ -117,26 +117,44 @@ def _fps_lib():
     P, I = ctypes.c_void_p, ctypes.c_int
     lib.fps_order.argtypes = [I, I, P, P, P, P]
     lib.fps_order.restype = I
+    lib.fps_order_large.argtypes = [I, P, I, P, P, P, P]
+    lib.fps_order_large.restype = I
     return lib
 
 
-def fps_order(points, starts):
+SMALL_FPS_MAX = 51200
+
+
+def fps_order(points, starts, large=None):
     """Farthest-point order of ``b`` scenes of equal size on the GPU.
 
     points: CUDA float32 (b, n, 3) or (n, 3); starts: ints.  Returns an int64
-    CPU tensor (b, n) (or (n,)) of point indices.  Requires n <= 51200.
+    CPU tensor (b, n) (or (n,)) of point indices.  Scenes of more than
+    51,200 points (or ``large=True``) use the cooperative-grid kernel, one
+    scene at a time.
     """
     squeeze = points.ndim == 2
     x = points[None] if squeeze else points
     x = x.contiguous()
     b, n = x.shape[0], x.shape[1]
-    st = torch.as_tensor(list(starts) if not np.isscalar(starts) else [starts], dtype=torch.int32).to(x.device)
+    starts = list(starts) if not np.isscalar(starts) else [starts]
     order = torch.empty((b, n), dtype=torch.int32, device=x.device)
-    code = _fps_lib().fps_order(
-        b, n, x.data_ptr(), st.data_ptr(), order.data_ptr(), torch.cuda.current_stream().cuda_stream
-    )
-    if code:
-        raise RuntimeError(f"fps_order error {code}")
+    lib = _fps_lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    if large or (large is None and n > SMALL_FPS_MAX):
+        scratch = torch.empty(8, dtype=torch.int64, device=x.device)
+        err = torch.zeros(1, dtype=torch.int32, device=x.device)
+        for i in range(b):
+            code = lib.fps_order_large(
+                n, x[i].data_ptr(), int(starts[i]), order[i].data_ptr(), scratch.data_ptr(), err.data_ptr(), stream
+            )
+            if code or err.item():
+                raise RuntimeError(f"fps_order_large error {code} / barrier {err.item()}")
+    else:
+        st = torch.as_tensor(starts, dtype=torch.int32).to(x.device)
+        code = lib.fps_order(b, n, x.data_ptr(), st.data_ptr(), order.data_ptr(), stream)
+        if code:
+            raise RuntimeError(f"fps_order error {code}")
     order = order.long().cpu()
     return order[0] if squeeze else order
 

@@ -178,6 +178,14 @@ int reuse_lookup_static(int count, const float* x, long long nx,
 int fps_order(int b, int n, const float* x, const int* start, int* order,
               void* stream);
 
+/* Farthest-point order of one large scene (up to 8 points per resident
+ * thread, about 1.2 M points on a B200) with a cooperative grid: the same
+ * rule and result as fps_order.  scratch is 64 bytes of device memory, *err
+ * (device int) becomes 1 if a grid barrier wait gives up (the order is then
+ * incomplete).  start is a host int. */
+int fps_order_large(int n, const float* x, int start, int* order,
+                    void* scratch, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

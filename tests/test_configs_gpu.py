@@ -97,6 +97,39 @@ def test_batch_equals_session_per_scene():
     _check_hierarchy_against_oracle(X[3].cpu().numpy(), {k: v[3 * v.shape[0] // 16:4 * v.shape[0] // 16] for k, v in out.items() if k.startswith(("ball", "hit", "nn"))}, hz.ROOM_SIZES, hz.ROOM_RADII)
 
 
+def test_large_scene_hierarchy():
+    """1,000,000-point room in a 20x20x3 m box, FPS-ordered, prefixes
+    1M/250k/62.5k/15.6k(/3.9k), r = 0.05/0.1/0.2/0.4, K = 32: the session and
+    the batched engine agree on every row, oracle samples of every stage
+    match, reuse rows are prefixes of the self rows."""
+    from gsa_b200 import QuerySession, hierarchy as hz, scenes
+
+    sizes, radii = hz.LARGE_SIZES, hz.LARGE_RADII
+    P = scenes.room_batch([11], n=sizes[0], box=(20.0, 20.0, 3.0))
+    with QuerySession() as s:
+        out = hz.run_session(s, P[0], sizes, radii)
+        st = dict(s.stats)
+    # the 3,906-point support of the last decoder stage is not one of the
+    # root's prefix sizes (1M, 250k, 62.5k, 15.6k), so it gets its own tree
+    assert st["builds"] == 2 and st["ball_hits"] == 4 and st["tree_reuses"] == 6
+    batch = hz.Batch(sizes, radii).run(P)
+    torch.cuda.synchronize()
+    for key, t in out.items():
+        assert torch.equal(batch[key], t), key
+    Pn = P[0].cpu().numpy()
+    rng = np.random.default_rng(3)
+    for s_ in range(4):
+        n_s = sizes[s_]
+        rows = out[f"ball{s_}"].cpu().numpy()
+        assert np.array_equal(out[f"hit{s_}"].cpu().numpy(), rows[: sizes[s_ + 1]])
+        pick = np.unique(np.concatenate([rng.choice(n_s, 200, replace=False), [0, n_s - 1]]))
+        want = orc.ball_oracle_fast(Pn[pick], Pn[:n_s], radii[s_], 32)
+        assert np.array_equal(rows[pick], want), s_
+        ed, ei = orc.nn_oracle_fast(Pn[pick], Pn[: sizes[s_ + 1]])
+        assert np.array_equal(out[f"nnd{s_}"].cpu().numpy()[pick], ed), s_
+        assert np.array_equal(out[f"nni{s_}"].cpu().numpy()[pick], ei), s_
+
+
 def test_batched_reuse_admission_rejects_changed_scene():
     from tests import abi
 

@@ -306,6 +306,17 @@ def test_fps_order_matches_sequential_rule():
         assert sorted(order[i].tolist()) == list(range(3000))
 
 
+def test_fps_cooperative_grid_matches_single_block():
+    from gsa_b200 import scenes
+
+    p, st = scenes.room(7, n=20000)
+    p[100] = p[200]
+    x = torch.from_numpy(p).cuda()
+    small = scenes.fps_order(x, st, large=False)
+    large = scenes.fps_order(x, st, large=True)
+    assert torch.equal(small, large)
+
+
 def test_pool_reports_usage():
     from gsa_b200 import runtime
 
