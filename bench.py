@@ -326,11 +326,11 @@ def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
 
-    from gsa_b200 import QuerySession, hierarchy as hz, scenes
+    from gsa_b200 import QuerySession, distributed as gd, hierarchy as hz, scenes
 
     dev = torch.device("cuda", local)
     S = args.scenes
-    seeds = [rank * S + i for i in range(S)]
+    seeds = gd.rank_seeds(rank, S)
     X = scenes.room_batch(seeds)
     eng = hz.Batch(SIZES, RADII)
     out = eng.allocate(S, dev)
@@ -383,10 +383,7 @@ def run_ours(args, rank, world, local):
         key = name.rstrip("0123456789")
         phase[key] = phase.get(key, 0.0) + ms
     serial_ms = sum(phase.values()) / args.steps
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
+    max_ms = gd.max_over_ranks(total_ms, dev)
     ball_rows, hit_rows, nn_rows = rows_per_scene()
     rows = ball_rows + hit_rows + nn_rows
     value = world * S * rows * args.steps / (max_ms / 1000.0)
@@ -430,17 +427,8 @@ def run_ours(args, rank, world, local):
         "kernels": kernels,
     }
 
-    result_sum = torch.zeros(1, dtype=torch.int64, device=dev)
-    for key, v in out.items():
-        if key.startswith(("ball", "hit", "nni")):
-            result_sum += v.to(torch.int64).sum()
-    gathered = [torch.zeros(2, dtype=torch.int64, device=dev) for _ in range(world)]
-    mine = torch.tensor([S * rows, 0], dtype=torch.int64, device=dev)
-    mine[1] = result_sum[0]
-    if world > 1:
-        dist.all_gather(gathered, mine)
-    else:
-        gathered = [mine]
+    # the one data-path-free exchange: every rank's row count and checksum
+    gathered = gd.gather_counts(S * rows, gd.output_checksum(out), dev)
 
     line = {
         "metric": METRIC,
@@ -467,7 +455,7 @@ def run_ours(args, rank, world, local):
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
         "clocks": clock_info,
-        "rank_rows_checksums": [g.tolist() for g in gathered],
+        "rank_rows_checksums": [list(g) for g in gathered],
     }
 
     if not args.no_e2e:
