@@ -589,7 +589,11 @@ def main():
 
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        # keep stdout to the one JSON line (NCCL may print its version)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group(
+            "nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local)
+        )
     try:
         run_ours(args, rank, world, local)
     finally:
