@@ -42,8 +42,9 @@ _WALK_ONLY = ["-DGSA_RADIUS_SCAN_MAX=0", "-DGSA_KNN_SCAN_MAX=0"]
 LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),
-    # test variants: tree walk for every support size; and a 4-entry stack
-    "gsa_bvh_walk": (_BVH, _WALK_ONLY),
+    # test variants: ordered packet walk for every support size; and the
+    # dense-leaf walk for every support size with a 4-entry stack
+    "gsa_bvh_walk": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

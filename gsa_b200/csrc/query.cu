@@ -32,6 +32,11 @@
 #ifndef GSA_KNN_SCAN_MAX
 #define GSA_KNN_SCAN_MAX 1024
 #endif
+// Tree-walk radius queries process visited leaves as dense (query, point)
+// pairs (radius_pairs_kernel); 0 selects the ordered packet walk throughout.
+#ifndef GSA_RADIUS_DENSE
+#define GSA_RADIUS_DENSE 1
+#endif
 
 namespace gsa {
 namespace {
@@ -104,55 +109,47 @@ __device__ __forceinline__ bool radius_test(const Entry& e, float px, float py,
          lower_d2(px, py, pz, e) < r2;
 }
 
+struct RadiusCtx {
+  const Entry* nodes;
+  const Entry* root;
+  const float4* pts;
+  const float* xs;
+  int m, K;
+  float r2;
+  long long max_steps;
+};
+
+// Ordered packet walk for the active lanes: one warp, one query per lane,
+// children visited in ascending minimum-ID order, per-lane first-K list L
+// kept sorted (insertion), "K found and minid >= K-th ID" prunes subtrees.
+// Returns the lane's count; sets overflow (warp-uniform) on stack overflow.
 template <int STACK>
-__global__ void __launch_bounds__(kQThreads)
-    radius_kernel(QArgs a) {
-  __shared__ int lists[kQWarps][32][33];
-  __shared__ int stack[kQWarps][STACK];
-  int b = blockIdx.y;
-  TreeDesc d = a.f.desc[b];
-  Slot s = slot_setup(a, d, b);
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
-  if (t0 >= s.slots) return;  // warp-uniform
-  int qi = slot_query(s, d, (int)t0 + lane);
-  bool active = qi >= 0;
-  float px = 0.f, py = 0.f, pz = 0.f;
-  if (active) {
-    const float* qp = a.q + 3ll * (s.qin + qi);
-    px = qp[0];
-    py = qp[1];
-    pz = qp[2];
-  }
-  const int K = a.ns;
-  const int m = s.m;
-  const float r2 = __fmul_rn(a.radius, a.radius);
-  int* L = lists[warp][lane];
-  int* stk = stack[warp];
+__device__ int walk_ordered(const RadiusCtx& c, bool active, float px,
+                            float py, float pz, int* L, int* stk,
+                            bool& overflow) {
+  const int K = c.K, m = c.m;
+  const float r2 = c.r2;
   int count = 0, bound = INT_MAX;
-  const Entry* nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
-  const float4* pts = a.f.pts + d.p0;
-  Entry cur = load_entry(a.f.root + b * a.f.levels + s.lev);
+  Entry cur = load_entry(c.root);
   bool need = active && radius_test(cur, px, py, pz, m, bound, r2);
   int top = 0;
-  bool overflow = false;
   // A valid tree is visited at most once per node; the cap only guards
   // against a corrupted handle (then the exact scan answers).
-  long long steps = 0, max_steps = 4ll * d.n + 64;
+  long long steps = 0;
   while (true) {
-    if (++steps > max_steps) {
+    if (++steps > c.max_steps) {
       overflow = true;
       break;
     }
     if (!__any_sync(kFull, need)) {
       if (top == 0) break;
       int ei = stk[--top];
-      cur = load_entry(nodes + ei);
+      cur = load_entry(c.nodes + ei);
       need = active && radius_test(cur, px, py, pz, m, bound, r2);
       continue;
     }
     if (cur.ref >= 0) {
-      const Entry* ch = nodes + (size_t)cur.ref * 2;
+      const Entry* ch = c.nodes + (size_t)cur.ref * 2;
       Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
       bool n0 = need && radius_test(c0, px, py, pz, m, bound, r2);
       bool n1 = need && radius_test(c1, px, py, pz, m, bound, r2);
@@ -175,7 +172,7 @@ __global__ void __launch_bounds__(kQThreads)
       int start, cnt;
       leaf_decode(cur.ref, start, cnt);
       for (int j = 0; j < cnt; ++j) {
-        float4 pt = __ldg(pts + start + j);
+        float4 pt = __ldg(c.pts + start + j);
         int id = __float_as_int(pt.w);
         if (id >= m) break;  // leaf points ascend by ID
         bool cand = need && id < bound;
@@ -194,25 +191,221 @@ __global__ void __launch_bounds__(kQThreads)
       need = false;
     }
   }
-  if (overflow && active) {
-    atomicAdd(a.fallback, 1);
-    count = 0;
-    const float* xs = a.f.x + 3ll * d.p0;
-    for (int id = 0; id < m && count < K; ++id) {
-      const float* p = xs + 3ll * id;
-      if (exact_d2(px, py, pz, p[0], p[1], p[2]) < r2) L[count++] = id;
-    }
+  return count;
+}
+
+// Exact original-order scan of one query (stack-overflow fallback).
+__device__ int scan_ordered(const RadiusCtx& c, float px, float py, float pz,
+                            int* L) {
+  int count = 0;
+  for (int id = 0; id < c.m && count < c.K; ++id) {
+    const float* p = c.xs + 3ll * id;
+    if (exact_d2(px, py, pz, p[0], p[1], p[2]) < c.r2) L[count++] = id;
   }
+  return count;
+}
+
+// Row of each lane's query: K IDs, padded with the first, zero when none;
+// written cooperatively, one coalesced row per step.
+__device__ void write_rows(int* out, const int* lists_w, int stride, int qi,
+                           int count, int qbase, int K, int lane) {
   __syncwarp();
   for (int j = 0; j < 32; ++j) {
     int qj = __shfl_sync(kFull, qi, j);
     int cj = __shfl_sync(kFull, count, j);
     if (qj < 0) continue;
     if (lane < K) {
-      int v = cj ? lists[warp][j][lane < cj ? lane : 0] : 0;
-      a.out[(size_t)(s.qbase + qj) * K + lane] = v;
+      const int* row = lists_w + j * stride;
+      out[(size_t)(qbase + qj) * K + lane] = cj ? row[lane < cj ? lane : 0] : 0;
     }
   }
+}
+
+__device__ __forceinline__ RadiusCtx radius_ctx(const QArgs& a,
+                                                const TreeDesc& d, int b,
+                                                const Slot& s) {
+  RadiusCtx c;
+  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  c.root = a.f.root + b * a.f.levels + s.lev;
+  c.pts = a.f.pts + d.p0;
+  c.xs = a.f.x + 3ll * d.p0;
+  c.m = s.m;
+  c.K = a.ns;
+  c.r2 = __fmul_rn(a.radius, a.radius);
+  c.max_steps = 4ll * d.n + 64;
+  return c;
+}
+
+template <int STACK>
+__global__ void __launch_bounds__(kQThreads)
+    radius_kernel(QArgs a) {
+  __shared__ int lists[kQWarps][32][33];
+  __shared__ int stack[kQWarps][STACK];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
+  if (t0 >= s.slots) return;  // warp-uniform
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qin + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  RadiusCtx c = radius_ctx(a, d, b, s);
+  int* L = lists[warp][lane];
+  bool overflow = false;
+  int count = walk_ordered<STACK>(c, active, px, py, pz, L, stack[warp], overflow);
+  if (overflow && active) {
+    atomicAdd(a.fallback, 1);
+    count = scan_ordered(c, px, py, pz, L);
+  }
+  write_rows(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
+}
+
+// Dense-leaf variant.  Internal nodes are walked as a packet (one query per
+// lane), but a visited leaf is processed as (active query x leaf point)
+// pairs spread over all 32 lanes, so lanes that do not need the leaf do not
+// idle through it.  Hits go unordered into per-query shared buffers and are
+// sorted at the end; without an ordered list there is no "K-th ID" pruning,
+// which suits the small-radius stages this walk serves.  A query whose
+// buffer overflows (more than kHitCap points within the radius) is answered
+// again by the ordered walk.  Results are identical to radius_kernel.
+constexpr int kHitCap = 40;  // >= 32 so the buffer can hold a K-list
+
+template <int STACK>
+__global__ void __launch_bounds__(kQThreads)
+    radius_pairs_kernel(QArgs a) {
+  __shared__ int hits[kQWarps][32][kHitCap + 1];
+  __shared__ int hcount[kQWarps][32];
+  __shared__ int amap[kQWarps][32];
+  __shared__ int stack[kQWarps][STACK];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
+  if (t0 >= s.slots) return;  // warp-uniform
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qin + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  RadiusCtx c = radius_ctx(a, d, b, s);
+  const int m = c.m;
+  const float r2 = c.r2;
+  int* H = hits[warp][lane];
+  int* stk = stack[warp];
+  hcount[warp][lane] = 0;
+  __syncwarp();
+  const unsigned lt = (1u << lane) - 1u;
+  Entry cur = load_entry(c.root);
+  bool need = active && radius_test(cur, px, py, pz, m, INT_MAX, r2);
+  int top = 0;
+  bool overflow = false;
+  long long steps = 0;
+  while (true) {
+    if (++steps > c.max_steps) {
+      overflow = true;
+      break;
+    }
+    if (!__any_sync(kFull, need)) {
+      if (top == 0) break;
+      int ei = stk[--top];
+      cur = load_entry(c.nodes + ei);
+      need = active && radius_test(cur, px, py, pz, m, INT_MAX, r2);
+      continue;
+    }
+    if (cur.ref >= 0) {
+      const Entry* ch = c.nodes + (size_t)cur.ref * 2;
+      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
+      bool n0 = need && radius_test(c0, px, py, pz, m, INT_MAX, r2);
+      bool n1 = need && radius_test(c1, px, py, pz, m, INT_MAX, r2);
+      bool a0 = __any_sync(kFull, n0), a1 = __any_sync(kFull, n1);
+      if (a0) {
+        if (a1) {
+          if (top == STACK) {
+            overflow = true;
+            break;
+          }
+          stk[top++] = cur.ref * 2 + 1;
+        }
+        cur = c0;
+        need = n0;
+      } else {
+        cur = c1;
+        need = n1;
+      }
+    } else {
+      int start, cnt;
+      leaf_decode(cur.ref, start, cnt);
+      float4 pj = lane < cnt ? __ldg(c.pts + start + lane)
+                             : make_float4(0.f, 0.f, 0.f, __int_as_float(INT_MAX));
+      int idj = __float_as_int(pj.w);
+      int cm = __popc(__ballot_sync(kFull, idj < m));  // leaf IDs ascend
+      unsigned M = __ballot_sync(kFull, need);
+      if (need) amap[warp][__popc(M & lt)] = lane;
+      __syncwarp();
+      int pairs = __popc(M) * cm;
+      for (int base = 0; base < pairs; base += 32) {
+        int p = base + lane;
+        bool valid = p < pairs;
+        int k = valid ? p / cm : 0;
+        int j = valid ? p - k * cm : 0;
+        int q = amap[warp][k];
+        float qx = __shfl_sync(kFull, px, q), qy = __shfl_sync(kFull, py, q),
+              qz = __shfl_sync(kFull, pz, q);
+        float tx = __shfl_sync(kFull, pj.x, j), ty = __shfl_sync(kFull, pj.y, j),
+              tz = __shfl_sync(kFull, pj.z, j);
+        int tid = __shfl_sync(kFull, idj, j);
+        if (valid && exact_d2(qx, qy, qz, tx, ty, tz) < r2) {
+          int slot = atomicAdd(&hcount[warp][q], 1);
+          if (slot < kHitCap) hits[warp][q][slot] = tid;
+        }
+      }
+      __syncwarp();
+      need = false;
+    }
+  }
+  __syncwarp();
+  int total = hcount[warp][lane];
+  int count = 0;
+  if (!overflow) {
+    bool spill = active && total > kHitCap;
+    if (active && !spill) {
+      for (int i = 1; i < total; ++i) {  // ascending IDs
+        int v = H[i], pos = i;
+        while (pos > 0 && H[pos - 1] > v) {
+          H[pos] = H[pos - 1];
+          --pos;
+        }
+        H[pos] = v;
+      }
+      count = min(total, c.K);
+    }
+    if (__any_sync(kFull, spill)) {
+      bool again = false;
+      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, stk, again);
+      if (spill) count = c2;
+      if (again && spill) {
+        atomicAdd(a.fallback, 1);
+        count = scan_ordered(c, px, py, pz, H);
+      }
+    }
+  } else if (active) {
+    atomicAdd(a.fallback, 1);
+    count = scan_ordered(c, px, py, pz, H);
+  }
+  write_rows(a.out, &hits[warp][0][0], kHitCap + 1, qi, count, s.qbase, c.K,
+             lane);
 }
 
 __device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
@@ -504,7 +697,10 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   if (slots <= 0) return cudaSuccess;
   dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
   count_launches();
-  radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  if (GSA_RADIUS_DENSE)
+    radius_pairs_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  else
+    radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
