@@ -3,10 +3,12 @@
 
 ``python -m gsa_b200._build`` writes ``gsa_b200/_native/gsa_bvh.so`` and
 ``gsa_b200/_native/reference_queries.so`` (the two library names GSA's
-``gsa/_library.py`` loads), plus two test variants: ``gsa_bvh_walk.so``
+``gsa/_library.py`` loads), plus three test variants: ``gsa_bvh_walk.so``
 answers every support size with the tree walk (the default library scans
-small prefixes), and ``gsa_bvh_stack4.so`` also has a 4-entry traversal
-stack so that the exact full-scan fallback path is exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+small prefixes), ``gsa_bvh_ordered.so`` does so with the ordered per-query
+radius walk instead of the packet-frontier kernel, and ``gsa_bvh_stack4.so``
+has a 4-entry traversal stack (8-entry frontier) so that the ordered-walk and
+exact full-scan fallbacks are exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
 intrinsics for every distance operation.
 """
@@ -42,9 +44,10 @@ _WALK_ONLY = ["-DGSA_RADIUS_SCAN_MAX=0", "-DGSA_KNN_SCAN_MAX=0"]
 LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),
-    # test variants: ordered packet walk for every support size; and the
-    # dense-leaf walk for every support size with a 4-entry stack
-    "gsa_bvh_walk": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0"]),
+    # test variants: tree walks for every support size (packet frontier;
+    # ordered per-query walk); and the frontier with a 4-entry stack
+    "gsa_bvh_walk": (_BVH, _WALK_ONLY),
+    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

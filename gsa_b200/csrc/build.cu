@@ -11,15 +11,21 @@
 //   3. stable LSD radix sort, 8 passes of 8 bits, per tree
 //      (sort_upsweep / seg_scan / sort_scatter; all trees in one launch)
 //   4. Karras radix-tree topology on (key, index)    (karras_kernel)
-//   5. bottom-up refit: leaves = maximal subtrees of <= `leaf` points; points
-//      written to `pts` in leaf order and ascending ID inside a leaf; per
-//      level child entries (box of the finite members with ID < n/4^l, the
-//      subtree's minimum ID, child/leaf reference); children stored in
-//      ascending minimum-ID order  (karras_kernel emits leaf records and
-//      seeds the arrival counters; leaf_kernel: a half-warp per leaf;
-//      climb_kernel: one thread per climb from each node with two leaves)
-//   6. per level, the IDs < n/4^l in leaf order, used as a spatially coherent
-//      query order for prefix queries               (qorder_* kernels)
+//   5. per prefix level, the member count (IDs < n/4^l) before every sorted
+//      position                            (member_count / member_prefix)
+//   6. leaves = maximal subtrees of <= `leaf` points (karras_kernel emits
+//      leaf records and seeds the arrival counters); per leaf, a half-warp
+//      writes its points to `pts` in leaf order and ascending ID inside the
+//      leaf, per level the members' IDs to the level's query order (IDs < n/4^l
+//      in leaf order, a spatially coherent order for prefix queries) and
+//      their points to the level's member array, and the leaf's entries
+//                                                  (leaf_kernel)
+//   7. bottom-up refit of the per-level child entries (box of the finite
+//      members with ID < n/4^l, the subtree's minimum ID, child/leaf
+//      reference; children in ascending minimum-ID order); on levels >= 1
+//      every subtree with <= `leaf` members is a leaf over the level's member
+//      array, so coarse levels keep full leaves      (climb_kernel: one
+//      thread per climb from each node with two leaves)
 #include <algorithm>
 #include <new>
 #include "forest.cuh"
@@ -32,15 +38,6 @@ constexpr int kSortThreads = 256;
 constexpr int kSortItems = 8;
 constexpr int kSortTile = kSortThreads * kSortItems;  // 2048 keys per block
 constexpr int kScanThreads = 1024;
-
-__device__ __forceinline__ unsigned float_key(float f) {
-  unsigned u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float key_float(unsigned k) {
-  unsigned u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
-  return __uint_as_float(u);
-}
 
 struct DescChunk {
   TreeDesc d[256];
@@ -335,13 +332,23 @@ struct RefitArgs {
   const int* perm;  // sorted local point indices
   const int* parent;
   int* counter;
+  const int* pref;  // [level-1][N]: level members before a leaf-order position
   const int4* leaves;
   const int* leaf_count;
   float4* pts;
+  float4* lpts;
+  int* qorder;
   Entry* nodes;
   Entry* root;
   int levels;
+  int leaf;  // level leaves hold at most this many members
+  int N;
 };
+
+// Level-leaf reference of `count` members starting at member `start`.
+__device__ __forceinline__ int level_leaf_ref(int start, int count) {
+  return count > 0 ? leaf_ref(start, count) : kEmptyLeaf;
+}
 
 __device__ __forceinline__ Entry* node_entry(Entry* nodes, const TreeDesc& d,
                                              int level, int node, int slot) {
@@ -373,7 +380,10 @@ __device__ __forceinline__ int arrive(int* p) {
 // Bottom-up climb from completed node i, by one thread: order the two child
 // entries by minimum ID (the same order on every level), write their union
 // into the parent's slot, and continue while this thread is the second child
-// to arrive.
+// to arrive.  On levels l >= 1 the node becomes a level leaf when both
+// children are level leaves holding at most `leaf` members together: the
+// members of a subtree are contiguous in the level's member array, the left
+// child's (slot 0 until this node swaps) first.
 __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
   const int* par = a.parent + (d.p0 - b);
   int* cnt = a.counter + (d.p0 - b);
@@ -404,6 +414,15 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
       e.hiy = fmaxf(u[l].hiy, v[l].hiy); e.hiz = fmaxf(u[l].hiz, v[l].hiz);
       e.minid = min(u[l].minid, v[l].minid);
       e.ref = i;
+      if (l > 0 && u[l].ref < 0 && v[l].ref < 0) {
+        int cu = level_leaf_count(u[l].ref), cv = level_leaf_count(v[l].ref);
+        if (cu + cv <= a.leaf) {
+          int su = 0, sv = 0, k;
+          if (cu) leaf_decode(u[l].ref, su, k);
+          if (cv) leaf_decode(v[l].ref, sv, k);
+          e.ref = level_leaf_ref(cu ? su : sv, cu + cv);
+        }
+      }
       if (i == 0)
         a.root[b * a.levels + l] = e;
       else
@@ -419,9 +438,12 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
 // original ID among the leaf's IDs and writes pts in ascending ID order; per
 // level, redux.sync min/max over order-preserving integer keys give the box
 // of the finite members with ID < n/4^l; the group's first lane writes the
-// entries into the owner node's slot (or the root).  Two groups per warp
-// keep twice as many leaves in flight; no arrivals here -- the counters were
-// initialised with the leaf-child counts.
+// entries into the owner node's slot (or the root).  The members of level l
+// are the leaf's first ranks; they go to the level's query order and member
+// array from the leaf's member offset `pref`, which is also the start of the
+// level-l leaf reference.  Two groups per warp keep twice as many leaves in
+// flight; no arrivals here -- the counters were initialised with the
+// leaf-child counts.
 template <int G>
 __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   int lane = threadIdx.x & 31;
@@ -452,11 +474,20 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
     bool fin = on && finite3(px, py, pz);
     unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
     Entry* own = code < 0 ? nullptr : node_entry(a.nodes, d, 0, code >> 1, code & 1);
+    int* qo = a.qorder + d.q0;           // level 0 of this tree's query order
+    float4* lp = a.lpts + (d.q0 - d.p0);  // level 1 of its member arrays
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
       if (l >= a.levels) break;
       bool mem = on && id < level_size(d.n, l);
       int members = __popc(__ballot_sync(gmask, mem));
+      int start = l ? __ldcg(a.pref + (size_t)(l - 1) * a.N + d.p0 + cf) : cf;
+      if (mem) {
+        qo[start + rank] = id;
+        if (l) lp[start + rank] = make_float4(px, py, pz, __int_as_float(id));
+      }
+      qo += level_size(d.n, l);
+      if (l) lp += level_size(d.n, l);
       bool f = mem && fin;
       Entry t;
       t.lox = t.loy = t.loz = inf;
@@ -470,7 +501,7 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
         t.hiz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
       }
       t.minid = minid;
-      t.ref = leaf_ref(cf, members ? members : 1);
+      t.ref = level_leaf_ref(start, members);
       if (gl == 0) {
         if (own)
           store_entry(own + (size_t)l * (d.n - 1) * 2, t);
@@ -496,8 +527,13 @@ __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
 // ---------------------------------------------------------------------------
 // Per level l, the original IDs < n/4^l in leaf order (stable compaction).
 // Counter layout per tree: cnt[(tree*levels + level)*max_tiles + tile].
+// Members of levels 1.. (IDs < n/4^l) before every sorted position: a tile
+// count, an exclusive scan over (level, tile) and a per-tile scan.  Leaves
+// keep their sorted point range, so these are also the counts before every
+// leaf-order position.  Counter layout per tree:
+// cnt[(tree*(levels-1) + level-1)*max_tiles + tile].
 __global__ void __launch_bounds__(kSortThreads)
-    qorder_count(const TreeDesc* desc, const float4* pts, int levels, int* cnt,
+    member_count(const TreeDesc* desc, const int* ids, int levels, int* cnt,
                  int max_tiles) {
   __shared__ int h[kMaxLevels];
   TreeDesc d = desc[blockIdx.y];
@@ -509,53 +545,58 @@ __global__ void __launch_bounds__(kSortThreads)
   for (int j = 0; j < kSortItems; ++j) {
     int idx = base + j * kSortThreads + threadIdx.x;
     if (idx < d.n) {
-      int id = __float_as_int(pts[d.p0 + idx].w);
-      for (int l = 0; l < levels; ++l) c[l] += id < level_size(d.n, l);
+      int id = ids[d.p0 + idx];
+      for (int l = 1; l < levels; ++l) c[l] += id < level_size(d.n, l);
     }
   }
-  for (int l = 0; l < levels; ++l) {
+  for (int l = 1; l < levels; ++l) {
     int v = c[l];
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
     if ((threadIdx.x & 31) == 0) atomicAdd(&h[l], v);
   }
   __syncthreads();
-  if (threadIdx.x < levels)
-    cnt[((size_t)blockIdx.y * levels + threadIdx.x) * max_tiles + blockIdx.x] =
-        h[threadIdx.x];
+  int l = threadIdx.x + 1;
+  if (l < levels)
+    cnt[((size_t)blockIdx.y * (levels - 1) + l - 1) * max_tiles + blockIdx.x] =
+        h[l];
 }
 
 __global__ void __launch_bounds__(kSortThreads)
-    qorder_scatter(const TreeDesc* desc, const float4* pts, int levels,
-                   const int* cnt, int max_tiles, int* qorder) {
+    member_prefix(const TreeDesc* desc, const int* ids, int levels,
+                  const int* cnt, int max_tiles, int* pref, int N) {
   __shared__ int run[kMaxLevels];
   __shared__ int wsum[kSortThreads / 32][kMaxLevels];
   TreeDesc d = desc[blockIdx.y];
   int base = blockIdx.x * kSortTile;
   if (base >= d.n) return;
   int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid < levels)
-    run[tid] =
-        cnt[((size_t)blockIdx.y * levels + tid) * max_tiles + blockIdx.x];
+  if (tid + 1 < levels)
+    run[tid + 1] =
+        cnt[((size_t)blockIdx.y * (levels - 1) + tid) * max_tiles + blockIdx.x];
   __syncthreads();
-  int* out = qorder + d.q0;
   for (int j = 0; j < kSortItems; ++j) {
     int idx = base + j * kSortThreads + tid;
-    int id = idx < d.n ? __float_as_int(pts[d.p0 + idx].w) : INT_MAX;
+    int id = idx < d.n ? ids[d.p0 + idx] : INT_MAX;
     unsigned bal[kMaxLevels];
-    for (int l = 0; l < levels; ++l) {
+#pragma unroll
+    for (int l = 1; l < kMaxLevels; ++l) {
+      if (l >= levels) break;
       bal[l] = __ballot_sync(kFull, id < level_size(d.n, l));
       if (lane == 0) wsum[warp][l] = __popc(bal[l]);
     }
     __syncthreads();
-    for (int l = 0; l < levels; ++l) {
-      if (id < level_size(d.n, l)) {
-        int r = run[l] + __popc(bal[l] & ((1u << lane) - 1u));
-        for (int w = 0; w < warp; ++w) r += wsum[w][l];
-        out[r] = id;
-      }
+    // the scan runs over levels 1.. in turn: `start` is level l's first slot
+    int start = 0;
+#pragma unroll
+    for (int l = 1; l < kMaxLevels; ++l) {
+      if (l >= levels) break;
+      int r = run[l] + __popc(bal[l] & ((1u << lane) - 1u));
+      for (int w = 0; w < warp; ++w) r += wsum[w][l];
+      if (idx < d.n) pref[(size_t)(l - 1) * N + d.p0 + idx] = r - start;
+      start += level_size(d.n, l);
     }
     __syncthreads();
-    if (tid < levels) {
+    if (tid >= 1 && tid < levels) {
       int s = 0;
       for (int w = 0; w < kSortThreads / 32; ++w) s += wsum[w][tid];
       run[tid] += s;
@@ -625,13 +666,15 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->nodes, sizeof(Entry) * std::max<long long>(1, node_entries));
   alloc((void**)&f->root, sizeof(Entry) * B * f->levels);
   alloc((void**)&f->qorder, sizeof(int) * std::max<long long>(1, q_total));
+  alloc((void**)&f->lpts, sizeof(float4) * std::max<long long>(1, q_total - N));
   int max_tiles = blocks_for(max_n, kSortTile);
   uint64_t *keys = nullptr, *keys2 = nullptr;
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
-      *counter = nullptr;
+      *counter = nullptr, *pref = nullptr;
   unsigned* bounds = nullptr;
   int4* leaves = nullptr;  // leaf records; at most one per point
   long long inner = std::max<long long>(1, N - B);
+  alloc((void**)&pref, sizeof(int) * std::max<long long>(1, (f->levels - 1) * N));
   alloc((void**)&vals, sizeof(int) * N);
   alloc((void**)&keys, sizeof(uint64_t) * N);
   alloc((void**)&keys2, sizeof(uint64_t) * N);
@@ -674,6 +717,16 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, counter, f->leaf,
                                      leaves, leaf_count);
     launches += 2 + 24 + 1;
+    if (f->levels > 1) {
+      // members of each prefix level before every sorted position
+      member_count<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
+                                               max_tiles);
+      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels - 1,
+                                          max_tiles, kSortTile);
+      member_prefix<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
+                                                max_tiles, pref, (int)N);
+      launches += 3;
+    }
   }
   if (!e) {
     RefitArgs ra;
@@ -682,12 +735,17 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     ra.perm = vals;
     ra.parent = parent;
     ra.counter = counter;
+    ra.pref = pref;
     ra.leaves = leaves;
     ra.leaf_count = leaf_count;
     ra.pts = f->pts;
+    ra.lpts = f->lpts;
+    ra.qorder = f->qorder;
     ra.nodes = f->nodes;
     ra.root = f->root;
     ra.levels = f->levels;
+    ra.leaf = f->leaf;
+    ra.N = (int)N;
     // lane groups of each tree loop over its leaf records (their count is
     // only known on the device)
     dim3 gl(leaf_grid(f->leaf <= 16, max_n), B);
@@ -696,18 +754,12 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     else
       leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
     climb_kernel<<<gk, 256, 0, s>>>(ra);
-    qorder_count<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
-                                             hist, max_tiles);
-    seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels, max_tiles,
-                                        kSortTile);
-    qorder_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, f->pts, f->levels,
-                                               hist, max_tiles, f->qorder);
-    launches += 5;
+    launches += 2;
     count_launches(launches);
     e = cudaGetLastError();
   }
   void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, leaves, parent,
-                     counter};
+                     counter, pref};
   for (void* p : scratch) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;
@@ -723,7 +775,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
 cudaError_t free_forest(Forest* f, cudaStream_t s) {
   if (!f) return cudaSuccess;
   cudaError_t e = cudaSuccess;
-  void* bufs[] = {f->desc, f->pts, f->nodes, f->root, f->qorder};
+  void* bufs[] = {f->desc, f->pts, f->lpts, f->nodes, f->root, f->qorder};
   for (void* p : bufs) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;

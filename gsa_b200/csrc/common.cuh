@@ -22,6 +22,12 @@ constexpr unsigned kFull = 0xffffffffu;
 // float4.  `minid` is the smallest original support ID in the subtree (all
 // levels); `ref` >= 0 names an internal node, ref < 0 encodes a leaf
 // ~((start << 5) | (count - 1)) whose `count` points are this level's members.
+// Level 0 leaves index `pts` (ascending ID inside a leaf).  On a level l >= 1
+// every subtree with at most `leaf` members of that level is a leaf ("level
+// leaf") indexing that level's member array (level_pts), where the members of
+// any subtree are contiguous; inside a level leaf IDs ascend only within each
+// level-0 leaf it spans.  An empty entry (no finite member) has lo > hi and is
+// never entered.
 struct Entry {
   float lox, loy, loz;
   int minid;
@@ -42,6 +48,7 @@ struct TreeDesc {
 struct ForestView {
   const TreeDesc* desc;
   const float4* pts;    // leaf order; within a leaf ascending ID; w = ID bits
+  const float4* lpts;   // [tree][level 1..][m_l] members of level l, leaf order
   const Entry* nodes;   // [tree][level][node][2]
   const Entry* root;    // [tree][level]
   const int* qorder;    // [tree][level][m_l] original IDs < m_l in leaf order
@@ -53,6 +60,17 @@ __host__ __device__ inline int level_size(int n, int level) {
   return level <= 0 ? n : (n >> (2 * level));
 }
 
+// Leaf-ordered points of one tree's level: `pts` for level 0, else the
+// level's member array (a tree's levels 1.. follow one another in `lpts`,
+// starting at q0 - p0, the member count of the earlier trees' levels 1..).
+__device__ inline const float4* level_pts(const ForestView& f,
+                                          const TreeDesc& d, int level) {
+  if (level <= 0) return f.pts + d.p0;
+  size_t o = (size_t)(d.q0 - d.p0);
+  for (int k = 1; k < level; ++k) o += level_size(d.n, k);
+  return f.lpts + o;
+}
+
 __device__ inline int leaf_ref(int start, int count) {
   return ~((start << 5) | (count - 1));
 }
@@ -60,6 +78,14 @@ __device__ inline void leaf_decode(int ref, int& start, int& count) {
   int v = ~ref;
   start = v >> 5;
   count = (v & 31) + 1;
+}
+// A level leaf with no member of its level (start 2^26 - 1 with 32 points,
+// which no tree of at most kMaxPoints points has).  Its box is empty, so no
+// query enters it; the builder reads its member count as 0.
+constexpr int kEmptyLeaf = INT_MIN;
+__device__ inline int level_leaf_count(int ref) {
+  if (ref == kEmptyLeaf) return 0;
+  return (~ref & 31) + 1;
 }
 
 __device__ inline Entry load_entry(const Entry* e) {
@@ -100,8 +126,34 @@ __device__ __forceinline__ float lower_d2(float qx, float qy, float qz,
                    __fmul_rd(dz, dz));
 }
 
+// Squared box-to-box distance rounded toward -inf at every step.  Each
+// round-down difference is monotone in its arguments, so for every point q of
+// the box [l, h] the result is at most lower_d2(q, b): a node that fails a
+// test against it holds no point within the radius of any such q.
+__device__ __forceinline__ float box_lower_d2(float lx, float ly, float lz,
+                                             float hx, float hy, float hz,
+                                             const Entry& b) {
+  if (b.lox > b.hix) return __int_as_float(0x7f800000);
+  float dx = fmaxf(0.f, fmaxf(__fsub_rd(b.lox, hx), __fsub_rd(lx, b.hix)));
+  float dy = fmaxf(0.f, fmaxf(__fsub_rd(b.loy, hy), __fsub_rd(ly, b.hiy)));
+  float dz = fmaxf(0.f, fmaxf(__fsub_rd(b.loz, hz), __fsub_rd(lz, b.hiz)));
+  return __fadd_rd(__fadd_rd(__fmul_rd(dx, dx), __fmul_rd(dy, dy)),
+                   __fmul_rd(dz, dz));
+}
+
 __device__ __forceinline__ bool finite3(float a, float b, float c) {
   return isfinite(a) && isfinite(b) && isfinite(c);
+}
+
+// Order-preserving unsigned key of a float (finite and infinite values) and
+// its inverse, for integer min/max reductions of coordinates.
+__device__ __forceinline__ unsigned float_key(float f) {
+  unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(unsigned k) {
+  unsigned u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
 }
 
 }  // namespace gsa

@@ -17,6 +17,7 @@ struct Forest {
   std::vector<TreeDesc> hdesc;
   TreeDesc* desc = nullptr;
   float4* pts = nullptr;
+  float4* lpts = nullptr;  // level 1.. member arrays (prefix trees)
   Entry* nodes = nullptr;
   Entry* root = nullptr;
   int* qorder = nullptr;
@@ -26,6 +27,7 @@ struct Forest {
     ForestView v;
     v.desc = desc;
     v.pts = pts;
+    v.lpts = lpts;
     v.nodes = nodes;
     v.root = root;
     v.qorder = qorder;

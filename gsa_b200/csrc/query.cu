@@ -32,8 +32,9 @@
 #ifndef GSA_KNN_SCAN_MAX
 #define GSA_KNN_SCAN_MAX 1024
 #endif
-// Tree-walk radius queries process visited leaves as dense (query, point)
-// pairs (radius_pairs_kernel); 0 selects the ordered packet walk throughout.
+// Tree-walk radius kernel: 1 culls with the warp's packet box and processes
+// leaves as dense (query, point) pairs (radius_frontier_kernel); 0 is the
+// ordered per-query packet walk (radius_kernel) throughout.
 #ifndef GSA_RADIUS_DENSE
 #define GSA_RADIUS_DENSE 1
 #endif
@@ -112,11 +113,12 @@ __device__ __forceinline__ bool radius_test(const Entry& e, float px, float py,
 struct RadiusCtx {
   const Entry* nodes;
   const Entry* root;
-  const float4* pts;
+  const float4* pts;  // the bounds level's leaf-ordered points
   const float* xs;
   int m, K;
   float r2;
   long long max_steps;
+  bool sorted;  // leaf IDs ascend (level 0 leaves)
 };
 
 // Ordered packet walk for the active lanes: one warp, one query per lane,
@@ -174,9 +176,9 @@ __device__ int walk_ordered(const RadiusCtx& c, bool active, float px,
       for (int j = 0; j < cnt; ++j) {
         float4 pt = __ldg(c.pts + start + j);
         int id = __float_as_int(pt.w);
-        if (id >= m) break;  // leaf points ascend by ID
-        bool cand = need && id < bound;
-        if (!__any_sync(kFull, cand)) break;
+        bool cand = need && id < m && id < bound;
+        // in an ascending leaf no later point can qualify
+        if (c.sorted && !__any_sync(kFull, cand)) break;
         if (cand && exact_d2(px, py, pz, pt.x, pt.y, pt.z) < r2) {
           int pos = count < K ? count : K - 1;
           while (pos > 0 && L[pos - 1] > id) {
@@ -227,12 +229,13 @@ __device__ __forceinline__ RadiusCtx radius_ctx(const QArgs& a,
   RadiusCtx c;
   c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
   c.root = a.f.root + b * a.f.levels + s.lev;
-  c.pts = a.f.pts + d.p0;
+  c.pts = level_pts(a.f, d, s.lev);
   c.xs = a.f.x + 3ll * d.p0;
   c.m = s.m;
   c.K = a.ns;
   c.r2 = __fmul_rn(a.radius, a.radius);
   c.max_steps = 4ll * d.n + 64;
+  c.sorted = s.lev == 0;
   return c;
 }
 
@@ -267,28 +270,34 @@ __global__ void __launch_bounds__(kQThreads)
   write_rows(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
 }
 
-// Dense-leaf variant.  Internal nodes are walked as a packet (one query per
-// lane), but a visited leaf is processed as (active query x leaf point)
-// pairs spread over all 32 lanes, so lanes that do not need the leaf do not
-// idle through it.  Hits go unordered into per-query shared buffers and are
-// sorted at the end; without an ordered list there is no "K-th ID" pruning,
-// which suits the small-radius stages this walk serves.  A query whose
-// buffer overflows (more than kHitCap points within the radius) is answered
-// again by the ordered walk.  Results are identical to radius_kernel.
-constexpr int kHitCap = 40;  // >= 32 so the buffer can hold a K-list
+// Packet-frontier variant.  A warp's 32 queries are neighbours in leaf order,
+// so the tree is culled once for all of them against the box of the warp's
+// finite queries (box_lower_d2), 32 child entries per step (one per lane)
+// from a warp frontier stack, instead of a per-query test of two children
+// per step.  Leaves that survive are queued; each queued leaf is then tested
+// per query against its own box and processed as (query x point) pairs with
+// the leaf's points held one per lane (w = leaf count rounded up to a power
+// of two, 32/w queries per step).  Hits go unordered into per-query shared
+// buffers, ranked by ballot, and are sorted at the end.  A frontier that
+// would exceed its stack, or a query with more than kPacketCap hits, is
+// answered by the ordered walk.  Results are identical to radius_kernel.
+constexpr int kFWarps = 4;
+constexpr int kPacketCap = 32;  // per-query hit buffer; holds a K-list (K<=32)
 
 template <int STACK>
-__global__ void __launch_bounds__(kQThreads)
-    radius_pairs_kernel(QArgs a) {
-  __shared__ int hits[kQWarps][32][kHitCap + 1];
-  __shared__ int hcount[kQWarps][32];
-  __shared__ int amap[kQWarps][32];
-  __shared__ int stack[kQWarps][STACK];
+__global__ void __launch_bounds__(kFWarps * 32)
+    radius_frontier_kernel(QArgs a) {
+  constexpr int kFront = 2 * STACK;
+  __shared__ int hits[kFWarps][32][kPacketCap + 1];
+  __shared__ float4 qbuf[kFWarps][32];
+  __shared__ int amap[kFWarps][32];
+  __shared__ int leafq[kFWarps][64];
+  __shared__ int front[kFWarps][kFront];
   int b = blockIdx.y;
   TreeDesc d = a.f.desc[b];
   Slot s = slot_setup(a, d, b);
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long t0 = ((long long)blockIdx.x * kQWarps + warp) * 32;
+  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
   if (t0 >= s.slots) return;  // warp-uniform
   int qi = slot_query(s, d, (int)t0 + lane);
   bool active = qi >= 0;
@@ -302,86 +311,119 @@ __global__ void __launch_bounds__(kQThreads)
   RadiusCtx c = radius_ctx(a, d, b, s);
   const int m = c.m;
   const float r2 = c.r2;
-  int* H = hits[warp][lane];
-  int* stk = stack[warp];
-  hcount[warp][lane] = 0;
-  __syncwarp();
   const unsigned lt = (1u << lane) - 1u;
-  Entry cur = load_entry(c.root);
-  bool need = active && radius_test(cur, px, py, pz, m, INT_MAX, r2);
-  int top = 0;
+  int* H = hits[warp][lane];
+  int* stk = front[warp];
+  int* lq = leafq[warp];
+  // Queries with a non-finite coordinate have no hits (their squared
+  // distances are inf or NaN) and stay out of the packet box.
+  const bool live = active && finite3(px, py, pz);
+  qbuf[warp][lane] = make_float4(px, py, pz, 0.f);
+  int hc = 0;  // this lane's hit count (may exceed kPacketCap)
   bool overflow = false;
-  long long steps = 0;
-  while (true) {
-    if (++steps > c.max_steps) {
-      overflow = true;
-      break;
-    }
-    if (!__any_sync(kFull, need)) {
-      if (top == 0) break;
-      int ei = stk[--top];
-      cur = load_entry(c.nodes + ei);
-      need = active && radius_test(cur, px, py, pz, m, INT_MAX, r2);
-      continue;
-    }
-    if (cur.ref >= 0) {
-      const Entry* ch = c.nodes + (size_t)cur.ref * 2;
-      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
-      bool n0 = need && radius_test(c0, px, py, pz, m, INT_MAX, r2);
-      bool n1 = need && radius_test(c1, px, py, pz, m, INT_MAX, r2);
-      bool a0 = __any_sync(kFull, n0), a1 = __any_sync(kFull, n1);
-      if (a0) {
-        if (a1) {
-          if (top == STACK) {
-            overflow = true;
-            break;
-          }
-          stk[top++] = cur.ref * 2 + 1;
-        }
-        cur = c0;
-        need = n0;
-      } else {
-        cur = c1;
-        need = n1;
-      }
-    } else {
-      int start, cnt;
-      leaf_decode(cur.ref, start, cnt);
-      float4 pj = lane < cnt ? __ldg(c.pts + start + lane)
-                             : make_float4(0.f, 0.f, 0.f, __int_as_float(INT_MAX));
-      int idj = __float_as_int(pj.w);
-      int cm = __popc(__ballot_sync(kFull, idj < m));  // leaf IDs ascend
-      unsigned M = __ballot_sync(kFull, need);
-      if (need) amap[warp][__popc(M & lt)] = lane;
-      __syncwarp();
-      int pairs = __popc(M) * cm;
-      for (int base = 0; base < pairs; base += 32) {
-        int p = base + lane;
-        bool valid = p < pairs;
-        int k = valid ? p / cm : 0;
-        int j = valid ? p - k * cm : 0;
-        int q = amap[warp][k];
-        float qx = __shfl_sync(kFull, px, q), qy = __shfl_sync(kFull, py, q),
-              qz = __shfl_sync(kFull, pz, q);
-        float tx = __shfl_sync(kFull, pj.x, j), ty = __shfl_sync(kFull, pj.y, j),
-              tz = __shfl_sync(kFull, pj.z, j);
-        int tid = __shfl_sync(kFull, idj, j);
-        if (valid && exact_d2(qx, qy, qz, tx, ty, tz) < r2) {
-          int slot = atomicAdd(&hcount[warp][q], 1);
-          if (slot < kHitCap) hits[warp][q][slot] = tid;
+  if (__any_sync(kFull, live)) {
+    const float blx = key_float(__reduce_min_sync(kFull, live ? float_key(px) : ~0u));
+    const float bly = key_float(__reduce_min_sync(kFull, live ? float_key(py) : ~0u));
+    const float blz = key_float(__reduce_min_sync(kFull, live ? float_key(pz) : ~0u));
+    const float bhx = key_float(__reduce_max_sync(kFull, live ? float_key(px) : 0u));
+    const float bhy = key_float(__reduce_max_sync(kFull, live ? float_key(py) : 0u));
+    const float bhz = key_float(__reduce_max_sync(kFull, live ? float_key(pz) : 0u));
+    int top = 0, nleaf = 0;
+    {
+      Entry root = load_entry(c.root);
+      if (root.minid < m &&
+          box_lower_d2(blx, bly, blz, bhx, bhy, bhz, root) < r2) {
+        if (root.ref >= 0) {
+          if (lane == 0) stk[0] = root.ref;
+          top = 1;
+        } else {
+          if (lane == 0) lq[0] = -1;  // the root itself is the only leaf
+          nleaf = 1;
         }
       }
-      __syncwarp();
-      need = false;
+    }
+    __syncwarp();
+    long long steps = 0;
+    while (top > 0 || nleaf > 0) {
+      if (++steps > c.max_steps) {
+        overflow = true;
+        break;
+      }
+      if (top > 0) {
+        // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
+        int P = min(top, 16);
+        bool pass = false, inner = false;
+        int ei = 0, ref = 0;
+        if (lane < 2 * P) {
+          ei = 2 * stk[top - P + (lane >> 1)] + (lane & 1);
+          Entry e = load_entry(c.nodes + ei);
+          pass = e.minid < m &&
+                 box_lower_d2(blx, bly, blz, bhx, bhy, bhz, e) < r2;
+          inner = e.ref >= 0;
+          ref = e.ref;
+        }
+        __syncwarp();
+        top -= P;
+        unsigned bi = __ballot_sync(kFull, pass && inner);
+        unsigned bl = __ballot_sync(kFull, pass && !inner);
+        int ni = __popc(bi);
+        if (top + ni > kFront) {
+          overflow = true;
+          break;
+        }
+        if (pass && inner) stk[top + __popc(bi & lt)] = ref;
+        if (pass && !inner) lq[nleaf + __popc(bl & lt)] = ei;
+        top += ni;
+        nleaf += __popc(bl);
+        __syncwarp();
+      }
+      if (nleaf < 32 && top > 0) continue;
+      for (int li = 0; li < nleaf; ++li) {
+        int ei = lq[li];
+        Entry e = load_entry(ei >= 0 ? c.nodes + ei : c.root);
+        bool need = live && lower_d2(px, py, pz, e) < r2;
+        unsigned M = __ballot_sync(kFull, need);
+        if (!M) continue;
+        int start, cnt;
+        leaf_decode(e.ref, start, cnt);
+        const int nA = __popc(M);
+        const int mine = __popc(M & lt);
+        if (need) amap[warp][mine] = lane;
+        __syncwarp();
+        const int logw = cnt <= 1 ? 0 : 32 - __clz(cnt - 1);
+        const int w = 1 << logw, per = 32 >> logw;
+        const int k = lane >> logw, j = lane & (w - 1);
+        const unsigned seg0 = w == 32 ? kFull : (1u << w) - 1u;
+        float4 pt = make_float4(0.f, 0.f, 0.f, __int_as_float(INT_MAX));
+        if (j < cnt) pt = __ldg(c.pts + start + j);
+        const int id = __float_as_int(pt.w);
+        const bool pv = j < cnt && id < m;
+        for (int base = 0; base < nA; base += per) {
+          int idx = base + k;
+          bool valid = pv && idx < nA;
+          int q = amap[warp][idx < nA ? idx : 0];
+          float4 qc = qbuf[warp][q];
+          bool hit = valid && exact_d2(qc.x, qc.y, qc.z, pt.x, pt.y, pt.z) < r2;
+          unsigned hm = __ballot_sync(kFull, hit);
+          if (!hm) continue;  // warp-uniform
+          int at = __shfl_sync(kFull, hc, q);
+          int slot = at + __popc(hm & (seg0 << (k << logw)) & lt);
+          if (hit && slot < kPacketCap) hits[warp][q][slot] = id;
+          int mk = mine - base;
+          if (need && mk >= 0 && mk < per)
+            hc += __popc(hm & (seg0 << (mk << logw)));
+        }
+        __syncwarp();
+      }
+      nleaf = 0;
     }
   }
   __syncwarp();
-  int total = hcount[warp][lane];
   int count = 0;
   if (!overflow) {
-    bool spill = active && total > kHitCap;
+    bool spill = active && hc > kPacketCap;
     if (active && !spill) {
-      for (int i = 1; i < total; ++i) {  // ascending IDs
+      for (int i = 1; i < hc; ++i) {  // ascending IDs
         int v = H[i], pos = i;
         while (pos > 0 && H[pos - 1] > v) {
           H[pos] = H[pos - 1];
@@ -389,7 +431,7 @@ __global__ void __launch_bounds__(kQThreads)
         }
         H[pos] = v;
       }
-      count = min(total, c.K);
+      count = min(hc, c.K);
     }
     if (__any_sync(kFull, spill)) {
       bool again = false;
@@ -400,12 +442,16 @@ __global__ void __launch_bounds__(kQThreads)
         count = scan_ordered(c, px, py, pz, H);
       }
     }
-  } else if (active) {
-    atomicAdd(a.fallback, 1);
-    count = scan_ordered(c, px, py, pz, H);
+  } else {
+    bool again = false;
+    count = walk_ordered<STACK>(c, active, px, py, pz, H, stk, again);
+    if (again && active) {
+      atomicAdd(a.fallback, 1);
+      count = scan_ordered(c, px, py, pz, H);
+    }
   }
-  write_rows(a.out, &hits[warp][0][0], kHitCap + 1, qi, count, s.qbase, c.K,
-             lane);
+  write_rows(a.out, &hits[warp][0][0], kPacketCap + 1, qi, count, s.qbase,
+             c.K, lane);
 }
 
 __device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
@@ -456,7 +502,8 @@ __global__ void __launch_bounds__(kQThreads)
   int i0 = INT_MAX, i1 = INT_MAX, i2 = INT_MAX;
   int* stk = stack[warp];
   const Entry* nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
-  const float4* pts = a.f.pts + d.p0;
+  const float4* pts = level_pts(a.f, d, s.lev);
+  const bool sorted = s.lev == 0;  // leaf IDs ascend
   Entry cur = load_entry(a.f.root + b * a.f.levels + s.lev);
   bool need = active && cur.minid < m && nonempty(cur) &&
               lower_d2(px, py, pz, cur) <= d2;
@@ -507,7 +554,10 @@ __global__ void __launch_bounds__(kQThreads)
       for (int j = 0; j < cnt; ++j) {
         float4 pt = __ldg(pts + start + j);
         int id = __float_as_int(pt.w);
-        if (id >= m) break;
+        if (id >= m) {
+          if (sorted) break;
+          continue;
+        }
         if (need)
           insert3(exact_d2(px, py, pz, pt.x, pt.y, pt.z), id, d0, d1, d2, i0,
                   i1, i2);
@@ -695,12 +745,14 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   }
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
-  dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
   count_launches();
-  if (GSA_RADIUS_DENSE)
-    radius_pairs_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
-  else
+  if (GSA_RADIUS_DENSE) {
+    dim3 grid((unsigned)((slots + kFWarps * 32 - 1) / (kFWarps * 32)), f.B);
+    radius_frontier_kernel<GSA_STACK><<<grid, kFWarps * 32, 0, s>>>(a);
+  } else {
+    dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
     radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

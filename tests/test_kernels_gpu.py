@@ -48,8 +48,10 @@ def check_knn(h, x, q, m, level):
 
 
 # "gsa_bvh" scans support prefixes up to 2048 (radius) / 1024 (3NN) points and
-# walks the tree above; "gsa_bvh_walk" walks the tree for every size.
-LIBS = ["gsa_bvh", "gsa_bvh_walk"]
+# walks the tree above (packet-frontier radius kernel); "gsa_bvh_walk" walks
+# the tree for every size; "gsa_bvh_ordered" does so with the ordered
+# per-query radius walk.
+LIBS = ["gsa_bvh", "gsa_bvh_walk", "gsa_bvh_ordered"]
 
 
 @pytest.mark.parametrize("lib_name", LIBS)
