@@ -76,7 +76,7 @@ def config(scenes):
 def parse():
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--scenes", type=int, default=SCENES)
@@ -311,7 +311,7 @@ def hbm_peak():
 
 def dram_bytes_per_query():
     """Measured DRAM bytes per radius query from the committed ncu summary."""
-    p = ROOT / "profiles" / "radius_kernel_room64.md"
+    p = ROOT / "profiles" / "radius_frontier_kernel_room64.md"
     try:
         for line in p.read_text().splitlines():
             if line.strip().startswith("dram_bytes_per_query:"):
@@ -403,7 +403,7 @@ def run_ours(args, rank, world, local):
                 "queries_per_step": queries // args.steps, "achieved_gbs": gbs}
 
     kernels = {
-        "radius_kernel": kernel_line(["ball0", "ball1"], [0, 1], radius_q),
+        "radius_frontier_kernel": kernel_line(["ball0", "ball1"], [0, 1], radius_q),
         "radius_scan_kernel": kernel_line(["ball2", "ball3"], [2, 3], radius_q),
         "knn3_kernel": kernel_line(["nn0", "nn1"], [0, 1], 36),
         "knn3_scan_kernel": kernel_line(["nn2", "nn3"], [2, 3], 36),
@@ -411,7 +411,7 @@ def run_ours(args, rank, world, local):
     name = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     kl = kernels[name]
     achieved = kl["achieved_gbs"]
-    dbq = dram_bytes_per_query() if name == "radius_kernel" else None
+    dbq = dram_bytes_per_query() if name == "radius_frontier_kernel" else None
     traffic = None if dbq is None else dbq * kl["queries_per_step"] / kl["launches_per_step"]
     roofline = {
         "bound": "hbm",
