@@ -388,9 +388,9 @@ def run_ours(args, rank, world, local):
     rows = ball_rows + hit_rows + nn_rows
     value = world * S * rows * args.steps / (max_ms / 1000.0)
 
-    # Roofline per query kernel (serialized pass): stages 0-1 of the radius
-    # query and of 3NN walk the tree, stages 2-3 scan (support prefixes of
-    # at most 2048 / 1024 points).  Algorithmic bytes per query: radius
+    # Roofline per query kernel (serialized pass): stages 0-2 of the radius
+    # query and of 3NN walk the tree, stage 3 scans (support prefixes of at
+    # most 512 / 128 points).  Algorithmic bytes per query: radius
     # 12 + 4K (query + K ids), 3NN 12 + 12 + 12 (query, 3 dists, 3 ids).
     peak, peak_kind = hbm_peak()
     radius_q = 12 + 4 * K
@@ -403,10 +403,10 @@ def run_ours(args, rank, world, local):
                 "queries_per_step": queries // args.steps, "achieved_gbs": gbs}
 
     kernels = {
-        "radius_frontier_kernel": kernel_line(["ball0", "ball1"], [0, 1], radius_q),
-        "radius_scan_kernel": kernel_line(["ball2", "ball3"], [2, 3], radius_q),
-        "knn3_kernel": kernel_line(["nn0", "nn1"], [0, 1], 36),
-        "knn3_scan_kernel": kernel_line(["nn2", "nn3"], [2, 3], 36),
+        "radius_frontier_kernel": kernel_line(["ball0", "ball1", "ball2"], [0, 1, 2], radius_q),
+        "radius_scan_kernel": kernel_line(["ball3"], [3], radius_q),
+        "knn3_frontier_kernel": kernel_line(["nn0", "nn1", "nn2"], [0, 1, 2], 36),
+        "knn3_scan_kernel": kernel_line(["nn3"], [3], 36),
     }
     name = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     kl = kernels[name]

@@ -5,10 +5,10 @@
 ``gsa_b200/_native/reference_queries.so`` (the two library names GSA's
 ``gsa/_library.py`` loads), plus three test variants: ``gsa_bvh_walk.so``
 answers every support size with the tree walk (the default library scans
-small prefixes), ``gsa_bvh_ordered.so`` does so with the ordered per-query
-radius walk instead of the packet-frontier kernel, and ``gsa_bvh_stack4.so``
-has a 4-entry traversal stack (8-entry frontier) so that the ordered-walk and
-exact full-scan fallbacks are exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+small prefixes), ``gsa_bvh_ordered.so`` does so with the per-query walks
+(ordered radius, nearest-first 3NN) instead of the packet-frontier kernels,
+and ``gsa_bvh_stack4.so`` has a 4-entry traversal stack (8-entry frontier)
+so that the per-query-walk and exact full-scan fallbacks are exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
 intrinsics for every distance operation.
 """
@@ -45,9 +45,9 @@ LIBS = {
     "gsa_bvh": (_BVH, []),
     "reference_queries": (["launches.cu", "reference_queries.cu"], []),
     # test variants: tree walks for every support size (packet frontier;
-    # ordered per-query walk); and the frontier with a 4-entry stack
+    # per-query walks); and the frontier with a 4-entry stack
     "gsa_bvh_walk": (_BVH, _WALK_ONLY),
-    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0"]),
+    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0", "-DGSA_KNN_FRONTIER=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

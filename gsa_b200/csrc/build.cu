@@ -338,6 +338,7 @@ struct RefitArgs {
   float4* pts;
   float4* lpts;
   int* qorder;
+  int* wrank;
   Entry* nodes;
   Entry* root;
   int levels;
@@ -486,6 +487,9 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
         qo[start + rank] = id;
         if (l) lp[start + rank] = make_float4(px, py, pz, __int_as_float(id));
       }
+      // members before this point in leaf order (the leaf's members first)
+      if (on)
+        a.wrank[(size_t)(d.p0 + id) * a.levels + l] = start + min(rank, members);
       qo += level_size(d.n, l);
       if (l) lp += level_size(d.n, l);
       bool f = mem && fin;
@@ -667,6 +671,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->root, sizeof(Entry) * B * f->levels);
   alloc((void**)&f->qorder, sizeof(int) * std::max<long long>(1, q_total));
   alloc((void**)&f->lpts, sizeof(float4) * std::max<long long>(1, q_total - N));
+  alloc((void**)&f->wrank, sizeof(int) * N * f->levels);
   int max_tiles = blocks_for(max_n, kSortTile);
   uint64_t *keys = nullptr, *keys2 = nullptr;
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
@@ -741,6 +746,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     ra.pts = f->pts;
     ra.lpts = f->lpts;
     ra.qorder = f->qorder;
+    ra.wrank = f->wrank;
     ra.nodes = f->nodes;
     ra.root = f->root;
     ra.levels = f->levels;
@@ -775,7 +781,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
 cudaError_t free_forest(Forest* f, cudaStream_t s) {
   if (!f) return cudaSuccess;
   cudaError_t e = cudaSuccess;
-  void* bufs[] = {f->desc, f->pts, f->lpts, f->nodes, f->root, f->qorder};
+  void* bufs[] = {f->desc,  f->pts,    f->lpts,  f->nodes,
+                  f->root,  f->qorder, f->wrank};
   for (void* p : bufs) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;

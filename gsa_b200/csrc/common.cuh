@@ -52,6 +52,8 @@ struct ForestView {
   const Entry* nodes;   // [tree][level][node][2]
   const Entry* root;    // [tree][level]
   const int* qorder;    // [tree][level][m_l] original IDs < m_l in leaf order
+  const int* wrank;     // [point][level] members of the level before the
+                        // point's leaf-order position
   const float* x;       // borrowed original coordinates (AoS, 3 floats)
   int levels;           // 4 for prefix trees, 1 otherwise
 };

@@ -21,6 +21,7 @@ struct Forest {
   Entry* nodes = nullptr;
   Entry* root = nullptr;
   int* qorder = nullptr;
+  int* wrank = nullptr;
   const float* x = nullptr;  // borrowed
 
   ForestView view() const {
@@ -31,6 +32,7 @@ struct Forest {
     v.nodes = nodes;
     v.root = root;
     v.qorder = qorder;
+    v.wrank = wrank;
     v.x = x;
     v.levels = levels;
     return v;

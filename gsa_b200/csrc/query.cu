@@ -25,18 +25,26 @@
 #define GSA_STACK 128
 #endif
 // Support prefixes up to these sizes are answered by the warp scans below
-// instead of a tree walk (same results; fewer serial steps per warp).
+// instead of a tree walk (same results).  Timed on the room hierarchy: a
+// 375-point radius prefix scans in 27 us against 48 us for the frontier
+// kernel, a 1500-point one takes 175 us against 64 us; a 375-point 3NN prefix
+// 135 us against 64 us.
 #ifndef GSA_RADIUS_SCAN_MAX
-#define GSA_RADIUS_SCAN_MAX 2048
+#define GSA_RADIUS_SCAN_MAX 512
 #endif
 #ifndef GSA_KNN_SCAN_MAX
-#define GSA_KNN_SCAN_MAX 1024
+#define GSA_KNN_SCAN_MAX 128
 #endif
 // Tree-walk radius kernel: 1 culls with the warp's packet box and processes
 // leaves as dense (query, point) pairs (radius_frontier_kernel); 0 is the
 // ordered per-query packet walk (radius_kernel) throughout.
 #ifndef GSA_RADIUS_DENSE
 #define GSA_RADIUS_DENSE 1
+#endif
+// Tree-walk 3NN kernel: 1 collects candidates within a per-query window bound
+// (knn3_frontier_kernel); 0 is the nearest-first per-query walk (knn3_kernel).
+#ifndef GSA_KNN_FRONTIER
+#define GSA_KNN_FRONTIER 1
 #endif
 
 namespace gsa {
@@ -270,190 +278,6 @@ __global__ void __launch_bounds__(kQThreads)
   write_rows(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
 }
 
-// Packet-frontier variant.  A warp's 32 queries are neighbours in leaf order,
-// so the tree is culled once for all of them against the box of the warp's
-// finite queries (box_lower_d2), 32 child entries per step (one per lane)
-// from a warp frontier stack, instead of a per-query test of two children
-// per step.  Leaves that survive are queued; each queued leaf is then tested
-// per query against its own box and processed as (query x point) pairs with
-// the leaf's points held one per lane (w = leaf count rounded up to a power
-// of two, 32/w queries per step).  Hits go unordered into per-query shared
-// buffers, ranked by ballot, and are sorted at the end.  A frontier that
-// would exceed its stack, or a query with more than kPacketCap hits, is
-// answered by the ordered walk.  Results are identical to radius_kernel.
-constexpr int kFWarps = 4;
-constexpr int kPacketCap = 32;  // per-query hit buffer; holds a K-list (K<=32)
-
-template <int STACK>
-__global__ void __launch_bounds__(kFWarps * 32)
-    radius_frontier_kernel(QArgs a) {
-  constexpr int kFront = 2 * STACK;
-  __shared__ int hits[kFWarps][32][kPacketCap + 1];
-  __shared__ float4 qbuf[kFWarps][32];
-  __shared__ int amap[kFWarps][32];
-  __shared__ int leafq[kFWarps][64];
-  __shared__ int front[kFWarps][kFront];
-  int b = blockIdx.y;
-  TreeDesc d = a.f.desc[b];
-  Slot s = slot_setup(a, d, b);
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
-  if (t0 >= s.slots) return;  // warp-uniform
-  int qi = slot_query(s, d, (int)t0 + lane);
-  bool active = qi >= 0;
-  float px = 0.f, py = 0.f, pz = 0.f;
-  if (active) {
-    const float* qp = a.q + 3ll * (s.qin + qi);
-    px = qp[0];
-    py = qp[1];
-    pz = qp[2];
-  }
-  RadiusCtx c = radius_ctx(a, d, b, s);
-  const int m = c.m;
-  const float r2 = c.r2;
-  const unsigned lt = (1u << lane) - 1u;
-  int* H = hits[warp][lane];
-  int* stk = front[warp];
-  int* lq = leafq[warp];
-  // Queries with a non-finite coordinate have no hits (their squared
-  // distances are inf or NaN) and stay out of the packet box.
-  const bool live = active && finite3(px, py, pz);
-  qbuf[warp][lane] = make_float4(px, py, pz, 0.f);
-  int hc = 0;  // this lane's hit count (may exceed kPacketCap)
-  bool overflow = false;
-  if (__any_sync(kFull, live)) {
-    const float blx = key_float(__reduce_min_sync(kFull, live ? float_key(px) : ~0u));
-    const float bly = key_float(__reduce_min_sync(kFull, live ? float_key(py) : ~0u));
-    const float blz = key_float(__reduce_min_sync(kFull, live ? float_key(pz) : ~0u));
-    const float bhx = key_float(__reduce_max_sync(kFull, live ? float_key(px) : 0u));
-    const float bhy = key_float(__reduce_max_sync(kFull, live ? float_key(py) : 0u));
-    const float bhz = key_float(__reduce_max_sync(kFull, live ? float_key(pz) : 0u));
-    int top = 0, nleaf = 0;
-    {
-      Entry root = load_entry(c.root);
-      if (root.minid < m &&
-          box_lower_d2(blx, bly, blz, bhx, bhy, bhz, root) < r2) {
-        if (root.ref >= 0) {
-          if (lane == 0) stk[0] = root.ref;
-          top = 1;
-        } else {
-          if (lane == 0) lq[0] = -1;  // the root itself is the only leaf
-          nleaf = 1;
-        }
-      }
-    }
-    __syncwarp();
-    long long steps = 0;
-    while (top > 0 || nleaf > 0) {
-      if (++steps > c.max_steps) {
-        overflow = true;
-        break;
-      }
-      if (top > 0) {
-        // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
-        int P = min(top, 16);
-        bool pass = false, inner = false;
-        int ei = 0, ref = 0;
-        if (lane < 2 * P) {
-          ei = 2 * stk[top - P + (lane >> 1)] + (lane & 1);
-          Entry e = load_entry(c.nodes + ei);
-          pass = e.minid < m &&
-                 box_lower_d2(blx, bly, blz, bhx, bhy, bhz, e) < r2;
-          inner = e.ref >= 0;
-          ref = e.ref;
-        }
-        __syncwarp();
-        top -= P;
-        unsigned bi = __ballot_sync(kFull, pass && inner);
-        unsigned bl = __ballot_sync(kFull, pass && !inner);
-        int ni = __popc(bi);
-        if (top + ni > kFront) {
-          overflow = true;
-          break;
-        }
-        if (pass && inner) stk[top + __popc(bi & lt)] = ref;
-        if (pass && !inner) lq[nleaf + __popc(bl & lt)] = ei;
-        top += ni;
-        nleaf += __popc(bl);
-        __syncwarp();
-      }
-      if (nleaf < 32 && top > 0) continue;
-      for (int li = 0; li < nleaf; ++li) {
-        int ei = lq[li];
-        Entry e = load_entry(ei >= 0 ? c.nodes + ei : c.root);
-        bool need = live && lower_d2(px, py, pz, e) < r2;
-        unsigned M = __ballot_sync(kFull, need);
-        if (!M) continue;
-        int start, cnt;
-        leaf_decode(e.ref, start, cnt);
-        const int nA = __popc(M);
-        const int mine = __popc(M & lt);
-        if (need) amap[warp][mine] = lane;
-        __syncwarp();
-        const int logw = cnt <= 1 ? 0 : 32 - __clz(cnt - 1);
-        const int w = 1 << logw, per = 32 >> logw;
-        const int k = lane >> logw, j = lane & (w - 1);
-        const unsigned seg0 = w == 32 ? kFull : (1u << w) - 1u;
-        float4 pt = make_float4(0.f, 0.f, 0.f, __int_as_float(INT_MAX));
-        if (j < cnt) pt = __ldg(c.pts + start + j);
-        const int id = __float_as_int(pt.w);
-        const bool pv = j < cnt && id < m;
-        for (int base = 0; base < nA; base += per) {
-          int idx = base + k;
-          bool valid = pv && idx < nA;
-          int q = amap[warp][idx < nA ? idx : 0];
-          float4 qc = qbuf[warp][q];
-          bool hit = valid && exact_d2(qc.x, qc.y, qc.z, pt.x, pt.y, pt.z) < r2;
-          unsigned hm = __ballot_sync(kFull, hit);
-          if (!hm) continue;  // warp-uniform
-          int at = __shfl_sync(kFull, hc, q);
-          int slot = at + __popc(hm & (seg0 << (k << logw)) & lt);
-          if (hit && slot < kPacketCap) hits[warp][q][slot] = id;
-          int mk = mine - base;
-          if (need && mk >= 0 && mk < per)
-            hc += __popc(hm & (seg0 << (mk << logw)));
-        }
-        __syncwarp();
-      }
-      nleaf = 0;
-    }
-  }
-  __syncwarp();
-  int count = 0;
-  if (!overflow) {
-    bool spill = active && hc > kPacketCap;
-    if (active && !spill) {
-      for (int i = 1; i < hc; ++i) {  // ascending IDs
-        int v = H[i], pos = i;
-        while (pos > 0 && H[pos - 1] > v) {
-          H[pos] = H[pos - 1];
-          --pos;
-        }
-        H[pos] = v;
-      }
-      count = min(hc, c.K);
-    }
-    if (__any_sync(kFull, spill)) {
-      bool again = false;
-      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, stk, again);
-      if (spill) count = c2;
-      if (again && spill) {
-        atomicAdd(a.fallback, 1);
-        count = scan_ordered(c, px, py, pz, H);
-      }
-    }
-  } else {
-    bool again = false;
-    count = walk_ordered<STACK>(c, active, px, py, pz, H, stk, again);
-    if (again && active) {
-      atomicAdd(a.fallback, 1);
-      count = scan_ordered(c, px, py, pz, H);
-    }
-  }
-  write_rows(a.out, &hits[warp][0][0], kPacketCap + 1, qi, count, s.qbase,
-             c.K, lane);
-}
-
 __device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
                                         float& d2, int& i0, int& i1, int& i2) {
   if (!isfinite(v)) return;
@@ -477,6 +301,126 @@ __device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
   }
 }
 
+// The three best (d2, id) of a query, in order; (inf, INT_MAX) when missing.
+struct Top3 {
+  float d0, d1, d2;
+  int i0, i1, i2;
+};
+
+__device__ __forceinline__ Top3 empty_top3() {
+  const float inf = __int_as_float(0x7f800000);
+  return Top3{inf, inf, inf, INT_MAX, INT_MAX, INT_MAX};
+}
+
+struct KnnCtx {
+  const Entry* nodes;
+  const Entry* root;
+  const float4* pts;  // the bounds level's leaf-ordered points
+  const float* xs;
+  int m;
+  long long max_steps;
+  bool sorted;  // leaf IDs ascend (level 0 leaves)
+};
+
+__device__ __forceinline__ KnnCtx knn_ctx(const QArgs& a, const TreeDesc& d,
+                                          int b, const Slot& s) {
+  KnnCtx c;
+  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  c.root = a.f.root + b * a.f.levels + s.lev;
+  c.pts = level_pts(a.f, d, s.lev);
+  c.xs = a.f.x + 3ll * d.p0;
+  c.m = s.m;
+  c.max_steps = 4ll * d.n + 64;
+  c.sorted = s.lev == 0;
+  return c;
+}
+
+// Nearest-first packet walk for the active lanes (one query per lane): the
+// children a lane needs are visited in the order most needing lanes prefer,
+// subtrees with a lower bound above the lane's third distance are skipped.
+// Returns true (warp-uniform) on stack overflow or a step cap.
+template <int STACK>
+__device__ bool walk_knn3(const KnnCtx& c, bool active, float px, float py,
+                          float pz, Top3& t, int* stk) {
+  const int m = c.m;
+  Entry cur = load_entry(c.root);
+  bool need = active && cur.minid < m && nonempty(cur) &&
+              lower_d2(px, py, pz, cur) <= t.d2;
+  int top = 0;
+  long long steps = 0;
+  while (true) {
+    if (++steps > c.max_steps) return true;
+    if (!__any_sync(kFull, need)) {
+      if (top == 0) return false;
+      int ei = stk[--top];
+      cur = load_entry(c.nodes + ei);
+      need = active && cur.minid < m && nonempty(cur) &&
+             lower_d2(px, py, pz, cur) <= t.d2;
+      continue;
+    }
+    if (cur.ref >= 0) {
+      const Entry* ch = c.nodes + (size_t)cur.ref * 2;
+      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
+      float l0 = lower_d2(px, py, pz, c0), l1 = lower_d2(px, py, pz, c1);
+      bool n0 = need && c0.minid < m && nonempty(c0) && l0 <= t.d2;
+      bool n1 = need && c1.minid < m && nonempty(c1) && l1 <= t.d2;
+      unsigned b0 = __ballot_sync(kFull, n0), b1 = __ballot_sync(kFull, n1);
+      if (b0 && b1) {
+        unsigned both = b0 & b1;
+        unsigned pref1 = __ballot_sync(kFull, n0 && n1 && l1 < l0);
+        bool first1 = 2 * __popc(pref1) > __popc(both);
+        if (top == STACK) return true;
+        stk[top++] = cur.ref * 2 + (first1 ? 0 : 1);
+        cur = first1 ? c1 : c0;
+        need = first1 ? n1 : n0;
+      } else if (b0) {
+        cur = c0;
+        need = n0;
+      } else {
+        cur = c1;
+        need = n1;
+      }
+    } else {
+      int start, cnt;
+      leaf_decode(cur.ref, start, cnt);
+      for (int j = 0; j < cnt; ++j) {
+        float4 pt = __ldg(c.pts + start + j);
+        int id = __float_as_int(pt.w);
+        if (id >= m) {
+          if (c.sorted) break;
+          continue;
+        }
+        if (need)
+          insert3(exact_d2(px, py, pz, pt.x, pt.y, pt.z), id, t.d0, t.d1, t.d2,
+                  t.i0, t.i1, t.i2);
+      }
+      need = false;
+    }
+  }
+}
+
+// Exact original-order scan of one query (stack-overflow fallback).
+__device__ Top3 scan_knn3(const KnnCtx& c, float px, float py, float pz) {
+  Top3 t = empty_top3();
+  for (int id = 0; id < c.m; ++id) {
+    const float* p = c.xs + 3ll * id;
+    insert3(exact_d2(px, py, pz, p[0], p[1], p[2]), id, t.d0, t.d1, t.d2, t.i0,
+            t.i1, t.i2);
+  }
+  return t;
+}
+
+__device__ __forceinline__ void write_top3(const QArgs& a, const Slot& s,
+                                           int qi, const Top3& t) {
+  size_t o = (size_t)(s.qbase + qi) * 3;
+  a.dout[o] = t.d0;
+  a.dout[o + 1] = t.d1;
+  a.dout[o + 2] = t.d2;
+  a.out[o] = t.i0 == INT_MAX ? 0 : t.i0;
+  a.out[o + 1] = t.i1 == INT_MAX ? 0 : t.i1;
+  a.out[o + 2] = t.i2 == INT_MAX ? 0 : t.i2;
+}
+
 template <int STACK>
 __global__ void __launch_bounds__(kQThreads)
     knn3_kernel(QArgs a) {
@@ -496,95 +440,432 @@ __global__ void __launch_bounds__(kQThreads)
     py = qp[1];
     pz = qp[2];
   }
-  const int m = s.m;
-  const float inf = __int_as_float(0x7f800000);
-  float d0 = inf, d1 = inf, d2 = inf;
-  int i0 = INT_MAX, i1 = INT_MAX, i2 = INT_MAX;
-  int* stk = stack[warp];
-  const Entry* nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
-  const float4* pts = level_pts(a.f, d, s.lev);
-  const bool sorted = s.lev == 0;  // leaf IDs ascend
-  Entry cur = load_entry(a.f.root + b * a.f.levels + s.lev);
-  bool need = active && cur.minid < m && nonempty(cur) &&
-              lower_d2(px, py, pz, cur) <= d2;
-  int top = 0;
-  bool overflow = false;
-  long long steps = 0, max_steps = 4ll * d.n + 64;
-  while (true) {
-    if (++steps > max_steps) {
-      overflow = true;
-      break;
-    }
-    if (!__any_sync(kFull, need)) {
-      if (top == 0) break;
-      int ei = stk[--top];
-      cur = load_entry(nodes + ei);
-      need = active && cur.minid < m && nonempty(cur) &&
-             lower_d2(px, py, pz, cur) <= d2;
-      continue;
-    }
-    if (cur.ref >= 0) {
-      const Entry* ch = nodes + (size_t)cur.ref * 2;
-      Entry c0 = load_entry(ch), c1 = load_entry(ch + 1);
-      float l0 = lower_d2(px, py, pz, c0), l1 = lower_d2(px, py, pz, c1);
-      bool n0 = need && c0.minid < m && nonempty(c0) && l0 <= d2;
-      bool n1 = need && c1.minid < m && nonempty(c1) && l1 <= d2;
-      unsigned b0 = __ballot_sync(kFull, n0), b1 = __ballot_sync(kFull, n1);
-      if (b0 && b1) {
-        unsigned both = b0 & b1;
-        unsigned pref1 = __ballot_sync(kFull, n0 && n1 && l1 < l0);
-        bool first1 = 2 * __popc(pref1) > __popc(both);
-        if (top == STACK) {
-          overflow = true;
-          break;
-        }
-        stk[top++] = cur.ref * 2 + (first1 ? 0 : 1);
-        cur = first1 ? c1 : c0;
-        need = first1 ? n1 : n0;
-      } else if (b0) {
-        cur = c0;
-        need = n0;
-      } else {
-        cur = c1;
-        need = n1;
-      }
-    } else {
-      int start, cnt;
-      leaf_decode(cur.ref, start, cnt);
-      for (int j = 0; j < cnt; ++j) {
-        float4 pt = __ldg(pts + start + j);
-        int id = __float_as_int(pt.w);
-        if (id >= m) {
-          if (sorted) break;
-          continue;
-        }
-        if (need)
-          insert3(exact_d2(px, py, pz, pt.x, pt.y, pt.z), id, d0, d1, d2, i0,
-                  i1, i2);
-      }
-      need = false;
-    }
-  }
+  KnnCtx c = knn_ctx(a, d, b, s);
+  Top3 t = empty_top3();
+  bool overflow = walk_knn3<STACK>(c, active, px, py, pz, t, stack[warp]);
   if (overflow && active) {
     atomicAdd(a.fallback, 1);
-    d0 = d1 = d2 = inf;
-    i0 = i1 = i2 = INT_MAX;
-    const float* xs = a.f.x + 3ll * d.p0;
-    for (int id = 0; id < m; ++id) {
-      const float* p = xs + 3ll * id;
-      insert3(exact_d2(px, py, pz, p[0], p[1], p[2]), id, d0, d1, d2, i0, i1,
-              i2);
+    t = scan_knn3(c, px, py, pz);
+  }
+  if (active) write_top3(a, s, qi, t);
+}
+
+// ---------------------------------------------------------------------------
+// Packet-frontier kernels.  A warp's 32 queries are neighbours in leaf order,
+// so the tree is culled once for all of them against the box of the warp's
+// queries (box_lower_d2), 32 child entries per step (one per lane) from a
+// warp frontier stack, instead of a per-query test of two children per step.
+// Leaves that survive are queued and handled in batches of up to 32: one
+// lane loads each queued leaf's entry (one round trip for the batch), every
+// query tests every batch leaf's box from shuffled registers, and the leaves
+// some query needs are processed as (query x point) pairs, the leaf's points
+// held one per lane (w = count rounded up to a power of two, 32/w queries
+// per step), with the next leaf's points already loading.  A hit is ranked
+// by ballot into a per-query shared buffer.
+//
+// Radius (KNN = false): every query's bound is r*r, a hit is d2 < r*r, the
+// buffer holds IDs; more than kPacketCap hits, or a frontier overflow, sends
+// the query to the ordered walk.  3NN (KNN = true): the bound B of a query
+// starts as the third distance within a window of the level's members around
+// its own member rank, a hit is d2 <= B and the buffer holds point positions;
+// a buffer that could overflow is first cut to its best three (lowering B).
+// Every point of the final answer satisfies the hit test at every moment, so
+// both answers are exact.
+constexpr int kFWarps = 4;
+constexpr int kPacketCap = 32;  // radius hits per query; holds a K-list (K<=32)
+constexpr int kCandCap = 35;    // 3NN candidates: three kept + a leaf of 32
+constexpr int kWindow = 8;      // 3NN bound: 2*kWindow members
+
+// Box of the warp's packet queries and the node-test bound (r*r or the
+// largest B of the packet).
+struct Packet {
+  float lx, ly, lz, hx, hy, hz, R2;
+};
+
+__device__ __forceinline__ Packet make_packet(bool in, float px, float py,
+                                              float pz, float b) {
+  Packet p;
+  p.lx = key_float(__reduce_min_sync(kFull, in ? float_key(px) : ~0u));
+  p.ly = key_float(__reduce_min_sync(kFull, in ? float_key(py) : ~0u));
+  p.lz = key_float(__reduce_min_sync(kFull, in ? float_key(pz) : ~0u));
+  p.hx = key_float(__reduce_max_sync(kFull, in ? float_key(px) : 0u));
+  p.hy = key_float(__reduce_max_sync(kFull, in ? float_key(py) : 0u));
+  p.hz = key_float(__reduce_max_sync(kFull, in ? float_key(pz) : 0u));
+  p.R2 = key_float(__reduce_max_sync(kFull, in ? float_key(b) : 0u));
+  return p;
+}
+
+template <bool KNN>
+__device__ __forceinline__ bool within(float d2, float bound) {
+  return KNN ? d2 <= bound : d2 < bound;
+}
+
+// One queued leaf's points for the pair steps: lane k*w + j holds point j.
+struct LeafPts {
+  float4 pt;
+  int start, cnt, logw;
+};
+
+__device__ __forceinline__ LeafPts leaf_points(const float4* pts, int ref,
+                                               int lane) {
+  LeafPts L;
+  leaf_decode(ref, L.start, L.cnt);
+  L.logw = L.cnt <= 1 ? 0 : 32 - __clz(L.cnt - 1);
+  int j = lane & ((1 << L.logw) - 1);
+  L.pt = j < L.cnt ? __ldg(pts + L.start + j)
+                   : make_float4(0.f, 0.f, 0.f, __int_as_float(INT_MAX));
+  return L;
+}
+
+// Per-warp shared state of a frontier kernel.
+template <int CAP, int FRONT>
+struct WarpBufs {
+  int buf[32][CAP + 1];  // per-query hits (IDs) or candidates (positions)
+  float4 q[32];          // query coordinates and bound
+  int amap[32];          // pair step: active-query slot -> lane
+  int leafq[64];         // queued leaf entries (-1: the root)
+  int front[FRONT];      // frontier stack of internal nodes
+};
+
+// Best three of a lane's candidate positions, kept at the row's front.
+__device__ __forceinline__ Top3 cut_candidates(const float4* pts, int* row,
+                                               int& nc, float px, float py,
+                                               float pz) {
+  Top3 t = empty_top3();
+  int q0 = 0, q1 = 0, q2 = 0;
+  for (int i = 0; i < nc; ++i) {
+    int pos = row[i];
+    float4 pt = __ldg(pts + pos);
+    int id = __float_as_int(pt.w);
+    float v = exact_d2(px, py, pz, pt.x, pt.y, pt.z);
+    if (!isfinite(v)) continue;
+    if (v < t.d2 || (v == t.d2 && id < t.i2)) {
+      if (v < t.d1 || (v == t.d1 && id < t.i1)) {
+        t.d2 = t.d1; t.i2 = t.i1; q2 = q1;
+        if (v < t.d0 || (v == t.d0 && id < t.i0)) {
+          t.d1 = t.d0; t.i1 = t.i0; q1 = q0;
+          t.d0 = v; t.i0 = id; q0 = pos;
+        } else {
+          t.d1 = v; t.i1 = id; q1 = pos;
+        }
+      } else {
+        t.d2 = v; t.i2 = id; q2 = pos;
+      }
     }
   }
-  if (active) {
-    size_t o = (size_t)(s.qbase + qi) * 3;
-    a.dout[o] = d0;
-    a.dout[o + 1] = d1;
-    a.dout[o + 2] = d2;
-    a.out[o] = i0 == INT_MAX ? 0 : i0;
-    a.out[o + 1] = i1 == INT_MAX ? 0 : i1;
-    a.out[o + 2] = i2 == INT_MAX ? 0 : i2;
+  nc = (t.i0 != INT_MAX) + (t.i1 != INT_MAX) + (t.i2 != INT_MAX);
+  row[0] = q0;
+  row[1] = q1;
+  row[2] = q2;
+  return t;
+}
+
+// One batch of queued leaves lq[0..nleaf) (see the section comment).  `in`:
+// the lane's query takes part; `bound`: its current bound (r*r or B, also in
+// W.q[lane].w); `nc`: its buffer count.
+template <bool KNN, int CAP, int FRONT>
+__device__ void leaf_batches(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
+                             const Entry* root, const float4* pts, int nleaf,
+                             int m, bool in, float px, float py, float pz,
+                             float& bound, int& nc) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int b0 = 0; b0 < nleaf; b0 += 32) {
+    const int nb = min(32, nleaf - b0);
+    Entry le;
+    le.lox = le.loy = le.loz = 1.f;
+    le.hix = le.hiy = le.hiz = 0.f;  // empty
+    le.minid = INT_MAX;
+    le.ref = -1;
+    if (lane < nb) {
+      int ei = W.leafq[b0 + lane];
+      le = load_entry(ei >= 0 ? nodes + ei : root);
+    }
+    unsigned myM = 0;  // lane li: queries that need batch leaf li
+    for (int li = 0; li < nb; ++li) {
+      Entry e;
+      e.lox = __shfl_sync(kFull, le.lox, li);
+      e.loy = __shfl_sync(kFull, le.loy, li);
+      e.loz = __shfl_sync(kFull, le.loz, li);
+      e.hix = __shfl_sync(kFull, le.hix, li);
+      e.hiy = __shfl_sync(kFull, le.hiy, li);
+      e.hiz = __shfl_sync(kFull, le.hiz, li);
+      bool need = in && within<KNN>(lower_d2(px, py, pz, e), bound);
+      unsigned M = __ballot_sync(kFull, need);
+      if (lane == li) myM = M;
+    }
+    unsigned act = __ballot_sync(kFull, myM != 0);
+    if (!act) continue;
+    int cur = __ffs(act) - 1;
+    act &= act - 1;
+    LeafPts L = leaf_points(pts, __shfl_sync(kFull, le.ref, cur), lane);
+    while (true) {
+      // start loading the next needed leaf's points
+      const int nxt = act ? __ffs(act) - 1 : -1;
+      if (act) act &= act - 1;
+      const int nref = __shfl_sync(kFull, le.ref, nxt < 0 ? 0 : nxt);
+      LeafPts Ln;
+      if (nxt >= 0) Ln = leaf_points(pts, nref, lane);
+      const unsigned M = __shfl_sync(kFull, myM, cur);
+      const bool need = (M >> lane) & 1u;
+      if (KNN && __any_sync(kFull, need && nc + L.cnt > CAP)) {
+        if (need && nc + L.cnt > CAP) {
+          Top3 t = cut_candidates(pts, W.buf[lane], nc, px, py, pz);
+          if (nc == 3) {
+            bound = t.d2;
+            W.q[lane].w = bound;
+          }
+        }
+      }
+      const int nA = __popc(M);
+      const int mine = __popc(M & lt);
+      if (need) W.amap[mine] = lane;
+      __syncwarp();
+      const int logw = L.logw;
+      const int w = 1 << logw, per = 32 >> logw;
+      const int k = lane >> logw, j = lane & (w - 1);
+      const unsigned seg0 = w == 32 ? kFull : (1u << w) - 1u;
+      const int id = __float_as_int(L.pt.w);
+      const bool pv = j < L.cnt && id < m;
+      for (int base = 0; base < nA; base += per) {
+        int idx = base + k;
+        bool valid = pv && idx < nA;
+        int q = W.amap[idx < nA ? idx : 0];
+        float4 qc = W.q[q];
+        bool hit = valid && within<KNN>(exact_d2(qc.x, qc.y, qc.z, L.pt.x,
+                                                 L.pt.y, L.pt.z),
+                                        qc.w);
+        unsigned hm = __ballot_sync(kFull, hit);
+        if (!hm) continue;  // warp-uniform
+        int at = __shfl_sync(kFull, nc, q);
+        int slot = at + __popc(hm & (seg0 << (k << logw)) & lt);
+        if (hit && (KNN || slot < CAP)) W.buf[q][slot] = KNN ? L.start + j : id;
+        int mk = mine - base;
+        if (need && mk >= 0 && mk < per)
+          nc += __popc(hm & (seg0 << (mk << logw)));
+      }
+      __syncwarp();
+      if (nxt < 0) break;
+      cur = nxt;
+      L = Ln;
+    }
   }
+}
+
+// Frontier walk of the packet; leaves go through leaf_batches.  Returns
+// true (warp-uniform) when the frontier would exceed its stack or the step
+// cap is reached.
+template <bool KNN, int CAP, int FRONT>
+__device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
+                              const Entry* root, const float4* pts,
+                              long long max_steps, int m, const Packet& pk,
+                              bool in, float px, float py, float pz,
+                              float& bound, int& nc) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  int top = 0, nleaf = 0;
+  {
+    Entry r = load_entry(root);
+    if (r.minid < m &&
+        within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy, pk.hz, r),
+                    pk.R2)) {
+      if (r.ref >= 0) {
+        if (lane == 0) W.front[0] = r.ref;
+        top = 1;
+      } else {
+        if (lane == 0) W.leafq[0] = -1;  // the root itself is the only leaf
+        nleaf = 1;
+      }
+    }
+  }
+  __syncwarp();
+  long long steps = 0;
+  while (top > 0 || nleaf > 0) {
+    if (++steps > max_steps) return true;
+    if (top > 0) {
+      // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
+      int P = min(top, 16);
+      bool pass = false, inner = false;
+      int ei = 0, ref = 0;
+      if (lane < 2 * P) {
+        ei = 2 * W.front[top - P + (lane >> 1)] + (lane & 1);
+        Entry e = load_entry(nodes + ei);
+        pass = e.minid < m &&
+               within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy,
+                                        pk.hz, e),
+                           pk.R2);
+        inner = e.ref >= 0;
+        ref = e.ref;
+      }
+      __syncwarp();
+      top -= P;
+      unsigned bi = __ballot_sync(kFull, pass && inner);
+      unsigned bl = __ballot_sync(kFull, pass && !inner);
+      int ni = __popc(bi);
+      if (top + ni > FRONT) return true;
+      if (pass && inner) W.front[top + __popc(bi & lt)] = ref;
+      if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei;
+      top += ni;
+      nleaf += __popc(bl);
+      __syncwarp();
+    }
+    if (nleaf < 32 && top > 0) continue;
+    leaf_batches<KNN>(W, nodes, root, pts, nleaf, m, in, px, py, pz, bound,
+                      nc);
+    nleaf = 0;
+    __syncwarp();
+  }
+  return false;
+}
+
+template <int STACK>
+__global__ void __launch_bounds__(kFWarps * 32)
+    radius_frontier_kernel(QArgs a) {
+  __shared__ WarpBufs<kPacketCap, 2 * STACK> wb[kFWarps];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
+  if (t0 >= s.slots) return;  // warp-uniform
+  WarpBufs<kPacketCap, 2 * STACK>& W = wb[warp];
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qin + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  RadiusCtx c = radius_ctx(a, d, b, s);
+  int* H = W.buf[lane];
+  // Queries with a non-finite coordinate have no hits (their squared
+  // distances are inf or NaN) and stay out of the packet box.
+  const bool live = active && finite3(px, py, pz);
+  float bound = c.r2;
+  W.q[lane] = make_float4(px, py, pz, bound);
+  int hc = 0;  // this lane's hit count (may exceed kPacketCap)
+  bool overflow = false;
+  if (__any_sync(kFull, live)) {
+    Packet pk = make_packet(live, px, py, pz, bound);
+    overflow = frontier_walk<false>(W, c.nodes, c.root, c.pts, c.max_steps,
+                                    c.m, pk, live, px, py, pz, bound, hc);
+  }
+  __syncwarp();
+  int count = 0;
+  if (!overflow) {
+    bool spill = active && hc > kPacketCap;
+    if (active && !spill) {
+      for (int i = 1; i < hc; ++i) {  // ascending IDs
+        int v = H[i], pos = i;
+        while (pos > 0 && H[pos - 1] > v) {
+          H[pos] = H[pos - 1];
+          --pos;
+        }
+        H[pos] = v;
+      }
+      count = min(hc, c.K);
+    }
+    if (__any_sync(kFull, spill)) {
+      bool again = false;
+      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, W.front, again);
+      if (spill) count = c2;
+      if (again && spill) {
+        atomicAdd(a.fallback, 1);
+        count = scan_ordered(c, px, py, pz, H);
+      }
+    }
+  } else {
+    bool again = false;
+    count = walk_ordered<STACK>(c, active, px, py, pz, H, W.front, again);
+    if (again && active) {
+      atomicAdd(a.fallback, 1);
+      count = scan_ordered(c, px, py, pz, H);
+    }
+  }
+  write_rows(a.out, &W.buf[0][0], kPacketCap + 1, qi, count, s.qbase, c.K,
+             lane);
+}
+
+template <int STACK>
+__global__ void __launch_bounds__(kFWarps * 32)
+    knn3_frontier_kernel(QArgs a) {
+  __shared__ WarpBufs<kCandCap, 2 * STACK> wb[kFWarps];
+  int b = blockIdx.y;
+  TreeDesc d = a.f.desc[b];
+  Slot s = slot_setup(a, d, b);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
+  if (t0 >= s.slots) return;  // warp-uniform
+  WarpBufs<kCandCap, 2 * STACK>& W = wb[warp];
+  int qi = slot_query(s, d, (int)t0 + lane);
+  bool active = qi >= 0;
+  float px = 0.f, py = 0.f, pz = 0.f;
+  if (active) {
+    const float* qp = a.q + 3ll * (s.qin + qi);
+    px = qp[0];
+    py = qp[1];
+    pz = qp[2];
+  }
+  KnnCtx c = knn_ctx(a, d, b, s);
+  const int m = c.m;
+  const float inf = __int_as_float(0x7f800000);
+  // Non-finite queries have no finite distance: their rows stay (inf, 0).
+  const bool live = active && finite3(px, py, pz);
+  float B = inf;
+  if (live) {
+    // window of the level's members around the query's member rank (a query
+    // that is not a support point of this tree uses the first members)
+    const int nl = level_size(d.n, s.lev);
+    int r0 = qi < d.n ? __ldg(a.f.wrank + (size_t)(d.p0 + qi) * a.f.levels + s.lev) : 0;
+    int lo = max(0, min(r0 - kWindow, nl - 2 * kWindow));
+    int hi = min(nl, lo + 2 * kWindow);
+    float w0 = inf, w1 = inf, w2 = inf;
+    for (int k = lo; k < hi; ++k) {
+      float4 pt = __ldg(c.pts + k);
+      if (__float_as_int(pt.w) >= m) continue;
+      float v = exact_d2(px, py, pz, pt.x, pt.y, pt.z);
+      if (v < w2) {
+        if (v < w1) {
+          w2 = w1;
+          if (v < w0) {
+            w1 = w0;
+            w0 = v;
+          } else {
+            w1 = v;
+          }
+        } else {
+          w2 = v;
+        }
+      }
+    }
+    B = w2;  // inf unless three finite distances were seen
+  }
+  const bool inpk = live && B < inf;
+  W.q[lane] = make_float4(px, py, pz, B);
+  int nc = 0;  // this lane's candidates
+  bool overflow = false;
+  if (__any_sync(kFull, inpk)) {
+    Packet pk = make_packet(inpk, px, py, pz, B);
+    overflow = frontier_walk<true>(W, c.nodes, c.root, c.pts, c.max_steps, m,
+                                   pk, inpk, px, py, pz, B, nc);
+  }
+  __syncwarp();
+  Top3 t = empty_top3();
+  if (!overflow && inpk) t = cut_candidates(c.pts, W.buf[lane], nc, px, py, pz);
+  // lanes without a finite window bound, or every lane after an overflow
+  bool rest = live && (overflow || !inpk);
+  if (__any_sync(kFull, rest)) {
+    Top3 u = empty_top3();
+    bool again = walk_knn3<STACK>(c, rest, px, py, pz, u, W.front);
+    if (again && rest) {
+      atomicAdd(a.fallback, 1);
+      u = scan_knn3(c, px, py, pz);
+    }
+    if (rest) t = u;
+  }
+  if (active) write_top3(a, s, qi, t);
 }
 
 // ---------------------------------------------------------------------------
@@ -772,9 +1053,14 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
   }
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
-  dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
   count_launches();
-  knn3_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  if (GSA_KNN_FRONTIER) {
+    dim3 grid((unsigned)((slots + kFWarps * 32 - 1) / (kFWarps * 32)), f.B);
+    knn3_frontier_kernel<GSA_STACK><<<grid, kFWarps * 32, 0, s>>>(a);
+  } else {
+    dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
+    knn3_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

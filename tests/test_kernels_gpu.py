@@ -47,10 +47,10 @@ def check_knn(h, x, q, m, level):
     return fb
 
 
-# "gsa_bvh" scans support prefixes up to 2048 (radius) / 1024 (3NN) points and
-# walks the tree above (packet-frontier radius kernel); "gsa_bvh_walk" walks
-# the tree for every size; "gsa_bvh_ordered" does so with the ordered
-# per-query radius walk.
+# "gsa_bvh" scans support prefixes up to 512 (radius) / 128 (3NN) points and
+# walks the tree above (packet-frontier radius and 3NN kernels);
+# "gsa_bvh_walk" walks the tree for every size; "gsa_bvh_ordered" does so
+# with the per-query walks (ordered radius, nearest-first 3NN).
 LIBS = ["gsa_bvh", "gsa_bvh_walk", "gsa_bvh_ordered"]
 
 
