@@ -7,8 +7,8 @@
 // so any valid hierarchy gives bit-identical answers; this one is built with
 // no host synchronisation:
 //   1. per-tree bounds of the finite points          (bounds_kernel)
-//   2. 63-bit Morton keys, local point index values  (morton_kernel)
-//   3. stable LSD radix sort, 8 passes of 8 bits, per tree
+//   2. 48-bit Morton keys, local point index values  (morton_kernel)
+//   3. stable LSD radix sort, 6 passes of 8 bits, per tree
 //      (sort_upsweep / seg_scan / sort_scatter; all trees in one launch)
 //   4. Karras radix-tree topology on (key, index)    (karras_kernel)
 //   5. per prefix level, the member count (IDs < n/4^l) before every sorted
@@ -97,10 +97,17 @@ __device__ __forceinline__ uint64_t spread3(unsigned v) {
   return x;
 }
 
+// Morton keys use kAxisBits per axis: 48-bit keys sort in six 8-bit radix
+// passes (the tree only has to be a valid hierarchy; 65,536 cells per axis
+// keep it tight for these scenes, and equal keys are ordered by index).
+constexpr int kAxisBits = 16;
+constexpr unsigned kAxisMax = (1u << kAxisBits) - 1u;
+constexpr int kSortPasses = (3 * kAxisBits + 7) / 8;
+
 __device__ __forceinline__ unsigned quantize(float v, float lo, float scale) {
   float t = (v - lo) * scale;
   if (!(t >= 0.f)) return 0u;  // also NaN
-  if (t >= 2097151.f) return 2097151u;
+  if (t >= (float)kAxisMax) return kAxisMax;
   return (unsigned)t;
 }
 
@@ -116,7 +123,7 @@ __global__ void morton_kernel(const TreeDesc* desc, const float* x,
     float h = any ? key_float(b[3 + k]) : 0.f;
     ext = fmaxf(ext, h - lo[k]);
   }
-  float scale = (ext > 0.f && isfinite(ext)) ? 2097151.f / ext : 0.f;
+  float scale = (ext > 0.f && isfinite(ext)) ? (float)kAxisMax / ext : 0.f;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
        i += gridDim.x * blockDim.x) {
     const float* p = x + 3ll * (d.p0 + i);
@@ -259,10 +266,11 @@ __device__ __forceinline__ int common_prefix(const uint64_t* k, int n, int i,
 
 // Each internal node i > L points ("kept") emits a leaf record for every
 // child holding <= L points: (tree, first, last, i*2 + side); a tree of at most
-// L points emits one root record (tree, 0, n-1, -1).  Records are appended
-// with one atomic per warp.
-__device__ __forceinline__ void emit_leaf(bool want, int4 rec, int4* list,
-                                          int* count) {
+// L points emits one root record (tree, 0, n-1, -1).  Kept nodes whose two
+// children are leaves are listed as climb starts.  Lists are appended with
+// one atomic per warp.
+template <typename T>
+__device__ __forceinline__ void emit(bool want, T rec, T* list, int* count) {
   unsigned mask = __ballot_sync(kFull, want);
   if (!mask) return;
   int lane = threadIdx.x & 31;
@@ -274,13 +282,12 @@ __device__ __forceinline__ void emit_leaf(bool want, int4 rec, int4* list,
 }
 
 // Arrival counters start at the number of leaf children (leaves are complete
-// before any climb starts); nodes whose two children are leaves are marked
-// kClimbStart and begin the bottom-up climb.
-constexpr int kClimbStart = 0x100;
-
+// before any climb starts); a node with two leaf children starts a climb and
+// never receives an arrival.
 __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
                               int* parent, int* counter, int leaf,
-                              int4* leaves, int* leaf_count) {
+                              int4* leaves, int* leaf_count, int* starts,
+                              int* start_count) {
   int b = blockIdx.y;
   TreeDesc d = desc[b];
   int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -318,11 +325,11 @@ __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
       rec1 = make_int4(b, gamma + 1, last, (i << 1) | 1);
       leaf_children = (int)want0 + (int)want1;
     }
-    counter[(d.p0 - b) + i] =
-        leaf_children == 2 ? (kClimbStart | 2) : leaf_children;
+    counter[(d.p0 - b) + i] = leaf_children;
   }
-  emit_leaf(want0, rec0, leaves + d.p0, leaf_count + b);
-  emit_leaf(want1, rec1, leaves + d.p0, leaf_count + b);
+  emit(want0, rec0, leaves + d.p0, leaf_count + b);
+  emit(want1, rec1, leaves + d.p0, leaf_count + b);
+  emit(valid && want0 && want1, i, starts + (d.p0 - b), start_count + b);
 }
 
 // ---------------------------------------------------------------------------
@@ -335,6 +342,8 @@ struct RefitArgs {
   const int* pref;  // [level-1][N]: level members before a leaf-order position
   const int4* leaves;
   const int* leaf_count;
+  const int* starts;  // per tree: nodes with two leaf children
+  const int* start_count;
   float4* pts;
   float4* lpts;
   int* qorder;
@@ -516,16 +525,19 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   }
 }
 
-// One thread per internal node; nodes whose two children are leaves start a
-// climb.  Climbs run as independent threads, so every path of every tree
-// proceeds at once and a tree's refit takes about its depth in steps.
+// One thread per listed climb start (nodes whose two children are leaves; a
+// tree's list is about a third of its leaf count).  Climbs run as
+// independent threads, so every path of every tree proceeds at once and a
+// tree's refit takes about its depth in steps; launching only the starts
+// keeps every climbing thread resident from the first step.
 __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
   int b = blockIdx.y;
   TreeDesc d = a.desc[b];
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= d.n - 1) return;
-  if (!(a.counter[(d.p0 - b) + i] & kClimbStart)) return;
-  climb(a, d, b, i);
+  const int* st = a.starts + (d.p0 - b);
+  int total = a.start_count[b];
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < total;
+       r += gridDim.x * blockDim.x)
+    climb(a, d, b, st[r]);
 }
 
 // ---------------------------------------------------------------------------
@@ -613,6 +625,11 @@ inline int blocks_for(long long n, int per) {
   return (int)std::max<long long>(1, (n + per - 1) / per);
 }
 
+// Blocks per tree of the climb kernel: one thread per 16 points, above the
+// usual start count (about n / 20 with leaves of ~10 points); threads loop
+// over any excess.
+int climb_grid(long long max_points) { return blocks_for((max_points + 15) / 16, 256); }
+
 // Blocks per tree of the leaf kernel (grid.y = tree): enough lane groups for
 // one leaf record per 8 points (leaves hold about 10 points on average; the
 // groups loop over any excess), never more than the largest tree can use.
@@ -675,11 +692,12 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   int max_tiles = blocks_for(max_n, kSortTile);
   uint64_t *keys = nullptr, *keys2 = nullptr;
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
-      *counter = nullptr, *pref = nullptr;
+      *counter = nullptr, *pref = nullptr, *starts = nullptr;
   unsigned* bounds = nullptr;
   int4* leaves = nullptr;  // leaf records; at most one per point
   long long inner = std::max<long long>(1, N - B);
   alloc((void**)&pref, sizeof(int) * std::max<long long>(1, (f->levels - 1) * N));
+  alloc((void**)&starts, sizeof(int) * inner);
   alloc((void**)&vals, sizeof(int) * N);
   alloc((void**)&keys, sizeof(uint64_t) * N);
   alloc((void**)&keys2, sizeof(uint64_t) * N);
@@ -688,10 +706,11 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
   alloc((void**)&leaves, sizeof(int4) * N);
   alloc((void**)&parent, sizeof(int) * inner);
-  // arrival counters + one leaf-record count per tree
-  alloc((void**)&counter, sizeof(int) * (inner + B));
-  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + B), s);
+  // arrival counters + one leaf-record and one climb-start count per tree
+  alloc((void**)&counter, sizeof(int) * (inner + 2 * B));
+  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 2 * B), s);
   int* leaf_count = counter + inner;
+  int* start_count = leaf_count + B;
 
   for (int b0 = 0; !e && b0 < B; b0 += 256) {
     DescChunk c;
@@ -708,7 +727,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
     dim3 gm(std::min(blocks_for(max_n, 256), 1024), B);
     morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, keys, vals);
-    for (int pass = 0; pass < 8; ++pass) {
+    for (int pass = 0; pass < kSortPasses; ++pass) {
       int shift = 8 * pass;
       sort_upsweep<<<gs, kSortThreads, 0, s>>>(f->desc, keys, shift, hist,
                                                max_tiles);
@@ -720,8 +739,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
       std::swap(vals, vals2);
     }
     karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, counter, f->leaf,
-                                     leaves, leaf_count);
-    launches += 2 + 24 + 1;
+                                     leaves, leaf_count, starts, start_count);
+    launches += 2 + 3 * kSortPasses + 1;
     if (f->levels > 1) {
       // members of each prefix level before every sorted position
       member_count<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
@@ -743,6 +762,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     ra.pref = pref;
     ra.leaves = leaves;
     ra.leaf_count = leaf_count;
+    ra.starts = starts;
+    ra.start_count = start_count;
     ra.pts = f->pts;
     ra.lpts = f->lpts;
     ra.qorder = f->qorder;
@@ -759,13 +780,13 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
       leaf_kernel<16><<<gl, 256, 0, s>>>(ra);
     else
       leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
-    climb_kernel<<<gk, 256, 0, s>>>(ra);
+    climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
     launches += 2;
     count_launches(launches);
     e = cudaGetLastError();
   }
-  void* scratch[] = {keys, keys2, vals, vals2, hist, bounds, leaves, parent,
-                     counter, pref};
+  void* scratch[] = {keys, keys2, vals, vals2, hist,   bounds,
+                     leaves, parent, counter, pref, starts};
   for (void* p : scratch) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;
