@@ -7,8 +7,8 @@
 // so any valid hierarchy gives bit-identical answers; this one is built with
 // no host synchronisation:
 //   1. per-tree bounds of the finite points          (bounds_kernel)
-//   2. 48-bit Morton keys, local point index values  (morton_kernel)
-//   3. stable LSD radix sort, 6 passes of 8 bits, per tree
+//   2. Morton keys (30-63 bits by tree size), local point indices (morton_kernel)
+//   3. stable LSD radix sort, 8-bit passes over the key width, per tree
 //      (sort_upsweep / seg_scan / sort_scatter; all trees in one launch)
 //   4. Karras radix-tree topology on (key, index)    (karras_kernel)
 //   5. per prefix level, the member count (IDs < n/4^l) before every sorted
@@ -97,25 +97,32 @@ __device__ __forceinline__ uint64_t spread3(unsigned v) {
   return x;
 }
 
-// Morton keys use kAxisBits per axis: 48-bit keys sort in six 8-bit radix
-// passes (the tree only has to be a valid hierarchy; 65,536 cells per axis
-// keep it tight for these scenes, and equal keys are ordered by index).
-constexpr int kAxisBits = 16;
-constexpr unsigned kAxisMax = (1u << kAxisBits) - 1u;
-constexpr int kSortPasses = (3 * kAxisBits + 7) / 8;
+// Morton keys use `bits` per axis, chosen from the largest tree: five more
+// than a uniform distribution needs to separate its points (ceil(log2 n / 3)),
+// 10..21.  The tree only has to be a valid hierarchy (equal keys are ordered
+// by index), so the width only trades sort passes against tightness: 24,000
+// points take 30-bit keys and four 8-bit radix passes, 1,000,000 take 36-bit
+// keys and five.
+int morton_bits(int max_n) {
+  int lg = 0;
+  while ((1ll << lg) < (long long)max_n) ++lg;
+  return std::min(21, std::max(10, (lg + 2) / 3 + 5));
+}
 
-__device__ __forceinline__ unsigned quantize(float v, float lo, float scale) {
+__device__ __forceinline__ unsigned quantize(float v, float lo, float scale,
+                                             unsigned top) {
   float t = (v - lo) * scale;
   if (!(t >= 0.f)) return 0u;  // also NaN
-  if (t >= (float)kAxisMax) return kAxisMax;
+  if (t >= (float)top) return top;
   return (unsigned)t;
 }
 
 __global__ void morton_kernel(const TreeDesc* desc, const float* x,
-                              const unsigned* bounds, uint64_t* keys,
-                              int* vals) {
+                              const unsigned* bounds, int bits,
+                              uint64_t* keys, int* vals) {
   TreeDesc d = desc[blockIdx.y];
   const unsigned* b = bounds + 6 * blockIdx.y;
+  const unsigned top = (1u << bits) - 1u;
   float lo[3], ext = 0.f;
   bool any = b[0] != 0xffffffffu;
   for (int k = 0; k < 3; ++k) {
@@ -123,13 +130,13 @@ __global__ void morton_kernel(const TreeDesc* desc, const float* x,
     float h = any ? key_float(b[3 + k]) : 0.f;
     ext = fmaxf(ext, h - lo[k]);
   }
-  float scale = (ext > 0.f && isfinite(ext)) ? (float)kAxisMax / ext : 0.f;
+  float scale = (ext > 0.f && isfinite(ext)) ? (float)top / ext : 0.f;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
        i += gridDim.x * blockDim.x) {
     const float* p = x + 3ll * (d.p0 + i);
-    uint64_t key = (spread3(quantize(p[0], lo[0], scale)) << 2) |
-                   (spread3(quantize(p[1], lo[1], scale)) << 1) |
-                   spread3(quantize(p[2], lo[2], scale));
+    uint64_t key = (spread3(quantize(p[0], lo[0], scale, top)) << 2) |
+                   (spread3(quantize(p[1], lo[1], scale, top)) << 1) |
+                   spread3(quantize(p[2], lo[2], scale, top));
     keys[d.p0 + i] = key;
     vals[d.p0 + i] = i;
   }
@@ -726,8 +733,10 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
     bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
     dim3 gm(std::min(blocks_for(max_n, 256), 1024), B);
-    morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, keys, vals);
-    for (int pass = 0; pass < kSortPasses; ++pass) {
+    const int bits = morton_bits(max_n);
+    const int passes = (3 * bits + 7) / 8;
+    morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, bits, keys, vals);
+    for (int pass = 0; pass < passes; ++pass) {
       int shift = 8 * pass;
       sort_upsweep<<<gs, kSortThreads, 0, s>>>(f->desc, keys, shift, hist,
                                                max_tiles);
@@ -740,7 +749,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     }
     karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, counter, f->leaf,
                                      leaves, leaf_count, starts, start_count);
-    launches += 2 + 3 * kSortPasses + 1;
+    launches += 2 + 3 * passes + 1;
     if (f->levels > 1) {
       // members of each prefix level before every sorted position
       member_count<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
