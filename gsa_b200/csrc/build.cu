@@ -476,6 +476,11 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
     int4 rec = a.leaves[d.p0 + r];
     int cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
     bool on = gl < c;
+    // the leaf's member offset on level l (lane l loads it; level 0: cf),
+    // issued together with the point loads
+    int st = cf;
+    if (gl >= 1 && gl < a.levels)
+      st = __ldcg(a.pref + (size_t)(gl - 1) * a.N + d.p0 + cf);
     int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
     float px = 0.f, py = 0.f, pz = 0.f;
     if (on) {
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
       if (l >= a.levels) break;
       bool mem = on && id < level_size(d.n, l);
       int members = __popc(__ballot_sync(gmask, mem));
-      int start = l ? __ldcg(a.pref + (size_t)(l - 1) * a.N + d.p0 + cf) : cf;
+      int start = __shfl_sync(gmask, st, l, G);
       if (mem) {
         qo[start + rank] = id;
         if (l) lp[start + rank] = make_float4(px, py, pz, __int_as_float(id));
