@@ -172,6 +172,31 @@ def test_queries_outnumber_support_and_unrelated_queries(lib_name):
     h.free()
 
 
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_knn_bounds_from_sparse_and_tied_supports(lib_name):
+    """3NN where most window members are non-finite (queries without a
+    finite window bound take the per-query walk), where ties are massive (a
+    query's candidate buffer is cut to its best three many times), and with a
+    support prefix smaller than the level (window members with ID >= m)."""
+    rng = np.random.default_rng(21)
+    lib = abi.bvh_lib(lib_name)
+    n = 6000
+    x = rng.random((n, 3)).astype(np.float32)
+    x[rng.random(n) < 0.9] = np.nan  # 90 % non-finite support points
+    q = np.concatenate([rng.random((1500, 3)).astype(np.float32), x[:500]])
+    h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
+    for level, m in enumerate(levels_of(n)):
+        check_knn(h, x, q, m, level)
+    check_knn(h, x, q, 1000, 1)  # m below the level-1 prefix of 1500
+    h.free()
+    lattice = rng.integers(0, 3, size=(27, 3)).astype(np.float32)
+    x = lattice[rng.integers(0, 27, size=n)]  # ~220 copies of each point
+    h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
+    for level, m in enumerate(levels_of(n)):
+        check_knn(h, x, x[: m], m, level)
+    h.free()
+
+
 def test_small_stack_fallback_is_exact_and_counted():
     rng = np.random.default_rng(14)
     x = rng.random((5000, 3)).astype(np.float32)
