@@ -231,11 +231,21 @@ __global__ void __launch_bounds__(kSortThreads)
   const int* v = vin + d.p0;
   uint64_t* ko = kout + d.p0;
   int* vo = vout + d.p0;
+  // the tile's keys and values in one round trip, then ranked 256 at a time
+  uint64_t keys[kSortItems];
+  int vals[kSortItems];
+#pragma unroll
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + tid;
+    keys[j] = idx < d.n ? k[idx] : 0;
+    vals[j] = idx < d.n ? v[idx] : 0;
+  }
+#pragma unroll
   for (int j = 0; j < kSortItems; ++j) {
     int idx = base + j * kSortThreads + tid;
     bool valid = idx < d.n;
-    uint64_t key = valid ? k[idx] : 0;
-    int val = valid ? v[idx] : 0;
+    uint64_t key = keys[j];
+    int val = vals[j];
     int digit = valid ? (int)((key >> shift) & 255) : 256 + lane;
     unsigned peers = __match_any_sync(kFull, digit);
     int lower = __popc(peers & ((1u << lane) - 1u));
@@ -602,9 +612,16 @@ __global__ void __launch_bounds__(kSortThreads)
     run[tid + 1] =
         cnt[((size_t)blockIdx.y * (levels - 1) + tid) * max_tiles + blockIdx.x];
   __syncthreads();
+  int idv[kSortItems];
+#pragma unroll
   for (int j = 0; j < kSortItems; ++j) {
     int idx = base + j * kSortThreads + tid;
-    int id = idx < d.n ? ids[d.p0 + idx] : INT_MAX;
+    idv[j] = idx < d.n ? ids[d.p0 + idx] : INT_MAX;
+  }
+#pragma unroll
+  for (int j = 0; j < kSortItems; ++j) {
+    int idx = base + j * kSortThreads + tid;
+    int id = idv[j];
     unsigned bal[kMaxLevels];
 #pragma unroll
     for (int l = 1; l < kMaxLevels; ++l) {
