@@ -408,6 +408,18 @@ def run_ours(args, rank, world, local):
         "knn3_frontier_kernel": kernel_line(["nn0", "nn1", "nn2"], [0, 1, 2], 36),
         "knn3_scan_kernel": kernel_line(["nn3"], [3], 36),
     }
+    # Reuse check + row copy (mismatch_strided_kernel, reuse_rows_batch_kernel):
+    # per scene and stage, both value checks read the support and query
+    # prefix twice (input and snapshot, 12 B per point each) and the hit rows
+    # are read and written once (4K B each).
+    reuse_ms = sum(stage.get(f"reuse{s}", 0.0) for s in range(4))
+    reuse_bytes = args.steps * S * sum(24 * (SIZES[s] + SIZES[s + 1]) + 8 * K * SIZES[s + 1] for s in range(4))
+    reuse_line = {
+        "ms_per_step": reuse_ms / args.steps,
+        "launches_per_step": 12,
+        "bytes_per_step": reuse_bytes // args.steps,
+        "achieved_gbs": reuse_bytes / (reuse_ms / 1000.0) / 1e9 if reuse_ms else 0.0,
+    }
     name = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     kl = kernels[name]
     achieved = kl["achieved_gbs"]
@@ -425,6 +437,7 @@ def run_ours(args, rank, world, local):
         "algorithmic_bytes_per_query": radius_q if name.startswith("radius") else 36,
         "note": "achieved = algorithmic bytes of the kernel's launches / their summed CUDA-event time (serialized pass)",
         "kernels": kernels,
+        "reuse_check_and_copy": reuse_line,
     }
 
     # the one data-path-free exchange: every rank's row count and checksum
