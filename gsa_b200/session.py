@@ -20,6 +20,7 @@ statistics replay the reference's short-circuit order over those flags, so
 
 import ctypes
 import math
+import threading
 
 import torch
 
@@ -36,14 +37,18 @@ er.lib.reuse_rows.argtypes = [_I, _P, _P, _I, _I, _I, _P, _P, _P]
 er.lib.reuse_rows.restype = _I
 er.lib.gather_rows.argtypes = [_P, _I, _I, _I, _P, _P]
 er.lib.gather_rows.restype = _I
-_pinned = {}
+_pinned = threading.local()
 
 
 def _pinned_flags(n):
-    """Process-wide pinned host buffer for reading comparison flags."""
-    buf = _pinned.get("flags")
+    """Per-thread pinned host buffer for reading comparison flags (sessions
+    on different host threads and streams never share one)."""
+    buf = getattr(_pinned, "flags", None)
     if buf is None or buf.numel() < n:
-        buf = _pinned["flags"] = torch.empty(max(256, n), dtype=torch.int32, pin_memory=True)
+        # a normal tensor even when first needed inside inference mode, so
+        # later calls outside it can still copy into it
+        with torch.inference_mode(False):
+            buf = _pinned.flags = torch.empty(max(256, n), dtype=torch.int32, pin_memory=True)
     return buf[:n]
 
 
