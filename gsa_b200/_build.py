@@ -47,7 +47,7 @@ LIBS = {
     # test variants: tree walks for every support size (packet frontier;
     # per-query walks); and the frontier with a 4-entry stack
     "gsa_bvh_walk": (_BVH, _WALK_ONLY),
-    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_DENSE=0", "-DGSA_KNN_FRONTIER=0"]),
+    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_FRONTIER=0", "-DGSA_KNN_FRONTIER=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

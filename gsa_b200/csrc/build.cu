@@ -499,8 +499,11 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
       py = p[1];
       pz = p[2];
     }
+    // lanes past the leaf's count hold INT_MAX, so a fixed G-step loop ranks
+    // without diverging between the two half-warp groups of a warp
     int rank = 0;
-    for (int j = 0; j < c; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
+#pragma unroll
+    for (int j = 0; j < G; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
     if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
     int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
     bool fin = on && finite3(px, py, pz);

@@ -7,17 +7,24 @@
 // none); the three smallest finite squared distances in (d2, id) order,
 // missing entries (inf, 0).  Results do not depend on traversal order.
 //
-// Execution model (B200): one warp traverses the tree for 32 queries at once
-// ("packet" traversal).  Queries are visited in the tree's leaf order (for a
-// query array that is a prefix of the support, neighbouring lanes hold
-// neighbouring points), so the 32 lanes need nearly the same nodes; a node is
-// entered when any lane needs it, node entries and leaf points are loaded
-// once per warp as 16-byte broadcast loads, and each lane tests its own query.
-// The radius descent order is ascending subtree minimum ID (stored order of
-// the children), which makes the "K found and minid >= K-th ID" early exit of
-// the reference effective.  The warp stack lives in shared memory; a stack
-// overflow (impossible for STACK >= 97 on a Karras tree of 64-bit keys) falls
-// back to the exact original-order scan and is counted, as in the reference.
+// Execution model (B200): one warp serves 32 queries at once.  Queries are
+// visited in the tree's leaf order (for a query array that is a prefix of the
+// support, neighbouring lanes hold neighbouring points), so the 32 lanes need
+// nearly the same part of the tree.  Three forms:
+//   * packet-frontier kernels (default for the tree): the tree is culled once
+//     against the box of the warp's queries, 32 child entries per step, and
+//     the surviving leaves are processed as dense (query x point) pairs;
+//   * per-query packet walks (walk_ordered, walk_knn3): one query per lane,
+//     a node entered when any lane needs it, node entries and leaf points
+//     loaded once per warp as 16-byte broadcast loads; the radius walk visits
+//     children in ascending minimum-ID order so the reference's "K found and
+//     minid >= K-th ID" early exit applies.  They answer what the frontier
+//     kernels hand back (more than 32 radius hits, no finite 3NN bound,
+//     frontier overflow) and run alone in a test variant;
+//   * warp scans of the support in original order, for small prefixes.
+// A walk's stack overflow (impossible for STACK >= 97 on a Karras tree of
+// 64-bit keys) falls back to the exact original-order scan and is counted,
+// as in the reference.
 #include <algorithm>
 #include "forest.cuh"
 
@@ -38,8 +45,8 @@
 // Tree-walk radius kernel: 1 culls with the warp's packet box and processes
 // leaves as dense (query, point) pairs (radius_frontier_kernel); 0 is the
 // ordered per-query packet walk (radius_kernel) throughout.
-#ifndef GSA_RADIUS_DENSE
-#define GSA_RADIUS_DENSE 1
+#ifndef GSA_RADIUS_FRONTIER
+#define GSA_RADIUS_FRONTIER 1
 #endif
 // Tree-walk 3NN kernel: 1 collects candidates within a per-query window bound
 // (knn3_frontier_kernel); 0 is the nearest-first per-query walk (knn3_kernel).
@@ -1027,7 +1034,7 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   if (slots <= 0) return cudaSuccess;
   count_launches();
-  if (GSA_RADIUS_DENSE) {
+  if (GSA_RADIUS_FRONTIER) {
     dim3 grid((unsigned)((slots + kFWarps * 32 - 1) / (kFWarps * 32)), f.B);
     radius_frontier_kernel<GSA_STACK><<<grid, kFWarps * 32, 0, s>>>(a);
   } else {
