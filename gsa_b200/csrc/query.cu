@@ -238,6 +238,36 @@ __device__ void write_rows(int* out, const int* lists_w, int stride, int qi,
   }
 }
 
+// As write_rows with 16-byte stores, four rows per step (K/4 lanes per row),
+// when K is a multiple of 4 and `out` 16-byte aligned (then every row is);
+// otherwise write_rows.
+__device__ void write_rows4(int* out, const int* lists_w, int stride, int qi,
+                            int count, int qbase, int K, int lane) {
+  if ((K & 3) || (reinterpret_cast<uintptr_t>(out) & 15)) {
+    write_rows(out, lists_w, stride, qi, count, qbase, K, lane);
+    return;
+  }
+  __syncwarp();
+  const int per = K >> 2;            // lanes per row
+  const int rows = 32 / per;         // rows per step (4 at K = 32)
+  const int r = lane / per, c = (lane - r * per) * 4;
+  for (int j0 = 0; j0 < 32; j0 += rows) {
+    const int j = j0 + r;
+    const bool on = r < rows && j < 32;
+    const int qj = __shfl_sync(kFull, qi, on ? j : 0);
+    const int cj = __shfl_sync(kFull, count, on ? j : 0);
+    if (!on || qj < 0) continue;
+    const int* row = lists_w + j * stride;
+    const int first = cj ? row[0] : 0;
+    int4 v;
+    v.x = c < cj ? row[c] : first;
+    v.y = c + 1 < cj ? row[c + 1] : first;
+    v.z = c + 2 < cj ? row[c + 2] : first;
+    v.w = c + 3 < cj ? row[c + 3] : first;
+    *reinterpret_cast<int4*>(out + (size_t)(qbase + qj) * K + c) = v;
+  }
+}
+
 __device__ __forceinline__ RadiusCtx radius_ctx(const QArgs& a,
                                                 const TreeDesc& d, int b,
                                                 const Slot& s) {
@@ -282,7 +312,7 @@ __global__ void __launch_bounds__(kQThreads)
     atomicAdd(a.fallback, 1);
     count = scan_ordered(c, px, py, pz, L);
   }
-  write_rows(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
+  write_rows4(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
 }
 
 __device__ __forceinline__ void insert3(float v, int id, float& d0, float& d1,
@@ -791,8 +821,8 @@ __global__ void __launch_bounds__(kFWarps * 32)
       count = scan_ordered(c, px, py, pz, H);
     }
   }
-  write_rows(a.out, &W.buf[0][0], kPacketCap + 1, qi, count, s.qbase, c.K,
-             lane);
+  write_rows4(a.out, &W.buf[0][0], kPacketCap + 1, qi, count, s.qbase, c.K,
+              lane);
 }
 
 template <int STACK>
