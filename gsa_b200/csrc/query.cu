@@ -1048,6 +1048,38 @@ QArgs make_args(const Forest& f, const QuerySet& qs) {
 
 }  // namespace
 
+namespace {
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// The warp scan answers a launch when its support prefixes are small, or
+// when the tree kernels' grid would not fill the SMs (few queries) and the
+// scan's work, queries x prefix, stays bounded (a 1,000,000-point scene's
+// 15,625 level-3 points against its 3,906-point prefix: 0.36 ms on the tree
+// grid of 122 blocks).  scan_max 0 keeps every launch on the tree.
+bool prefer_scan(const Forest& f, const QuerySet& qs, int scan_max) {
+  const int m = max_prefix(f, qs);
+  if (m <= scan_max) return true;
+  if (scan_max <= 0) return false;
+  long long slots = max_slots(f, qs.qseg_host, qs.nq);
+  long long blocks = (slots + kFWarps * 32 - 1) / (kFWarps * 32) * f.B;
+  if (blocks >= sm_count()) return false;
+  long long q = qs.qseg_host ? qs.qseg_host[f.B] : qs.nq;
+  return q * (long long)m <= (1ll << 26);
+}
+
+}  // namespace
+
 cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
                           int ns, int* out, int* fallback, cudaStream_t s) {
   QArgs a = make_args(f, qs);
@@ -1055,7 +1087,7 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   a.ns = ns;
   a.out = out;
   a.fallback = fallback;
-  if (max_prefix(f, qs) <= GSA_RADIUS_SCAN_MAX) {
+  if (prefer_scan(f, qs, GSA_RADIUS_SCAN_MAX)) {
     long long nq = max_queries(f, qs);
     if (nq <= 0) return cudaSuccess;
     dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
@@ -1082,7 +1114,7 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
   a.dout = d;
   a.out = ix;
   a.fallback = fallback;
-  if (max_prefix(f, qs) <= GSA_KNN_SCAN_MAX) {
+  if (prefer_scan(f, qs, GSA_KNN_SCAN_MAX)) {
     long long nq = max_queries(f, qs);
     if (nq <= 0) return cudaSuccess;
     dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
