@@ -139,14 +139,16 @@ struct RadiusCtx {
 // Ordered packet walk for the active lanes: one warp, one query per lane,
 // children visited in ascending minimum-ID order, per-lane first-K list L
 // kept sorted (insertion), "K found and minid >= K-th ID" prunes subtrees.
-// Returns the lane's count; sets overflow (warp-uniform) on stack overflow.
+// `bound0` (per lane) is an exclusive bound known to hold the first K IDs
+// (INT_MAX when none is known).  Returns the lane's count; sets overflow
+// (warp-uniform) on stack overflow.
 template <int STACK>
 __device__ int walk_ordered(const RadiusCtx& c, bool active, float px,
                             float py, float pz, int* L, int* stk,
-                            bool& overflow) {
+                            bool& overflow, int bound0 = INT_MAX) {
   const int K = c.K, m = c.m;
   const float r2 = c.r2;
-  int count = 0, bound = INT_MAX;
+  int count = 0, bound = bound0;
   Entry cur = load_entry(c.root);
   bool need = active && radius_test(cur, px, py, pz, m, bound, r2);
   int top = 0;
@@ -807,8 +809,16 @@ __global__ void __launch_bounds__(kFWarps * 32)
       count = min(hc, c.K);
     }
     if (__any_sync(kFull, spill)) {
+      // The buffer holds kPacketCap >= K hits, so the first K IDs are all at
+      // most its largest ID: the walk starts with that bound.
+      int b0 = INT_MAX;
+      if (spill) {
+        b0 = H[0];
+        for (int i = 1; i < kPacketCap; ++i) b0 = max(b0, H[i]);
+        b0 += 1;
+      }
       bool again = false;
-      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, W.front, again);
+      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, W.front, again, b0);
       if (spill) count = c2;
       if (again && spill) {
         atomicAdd(a.fallback, 1);
