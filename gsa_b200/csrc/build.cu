@@ -324,18 +324,21 @@ __global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
     for (int t = lmax >> 1; t >= 1; t >>= 1)
       if (common_prefix(k, n, i, i + (l + t) * dir) > dmin) l += t;
     int j = i + l * dir;
-    int dnode = common_prefix(k, n, i, j);
-    int s = 0, t = l;
-    do {
-      t = (t + 1) >> 1;
-      if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
-    } while (t > 1);
-    int gamma = i + s * dir + min(dir, 0);
     int first = min(i, j), last = max(i, j);
-    if (first != gamma) par[gamma] = (i << 1) | 0;
-    if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
     int leaf_children = 0;
+    // Only kept nodes need their split, parent links and leaf records: a
+    // node of at most `leaf` points lies inside a leaf (its parent link is
+    // never followed; a kept node's parent is kept).
     if (last - first + 1 > leaf) {
+      int dnode = common_prefix(k, n, i, j);
+      int s = 0, t = l;
+      do {
+        t = (t + 1) >> 1;
+        if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
+      } while (t > 1);
+      int gamma = i + s * dir + min(dir, 0);
+      if (first != gamma) par[gamma] = (i << 1) | 0;
+      if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
       want0 = gamma - first + 1 <= leaf;
       want1 = last - gamma <= leaf;
       rec0 = make_int4(b, first, gamma, (i << 1) | 0);

@@ -513,9 +513,10 @@ __global__ void __launch_bounds__(kQThreads)
 constexpr int kFWarps = 4;
 constexpr int kPacketCap = 32;  // radius hits per query; holds a K-list (K<=32)
 constexpr int kCandCap = 35;    // 3NN candidates: three kept + a leaf of 32
-constexpr int kWindow = 12;     // 3NN bound: 2*kWindow members (3NN stages
+constexpr int kWindow = 16;     // 3NN bound: 2*kWindow members (3NN stages
                                 // 0-2 of the room hierarchy with 8 / 12 / 16 /
-                                // 24 members: 860 / 789 / 768 / 754 us)
+                                // 24 / 32 members: 860 / 789 / 768 / 754 /
+                                // 736 us)
 
 // Box of the warp's packet queries and the node-test bound (r*r or the
 // largest B of the packet).
