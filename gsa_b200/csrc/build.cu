@@ -568,9 +568,53 @@ __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
     climb(a, d, b, st[r]);
 }
 
+// One warp per (level, tree): the top of the level's tree expanded breadth
+// first while the list still fits 32 entries, stopping at the level's
+// leaves.  The list covers every point of the level exactly once, so a
+// frontier walk may start from it (one step of independent entry loads)
+// instead of descending from the root one dependent step per level.
+__global__ void __launch_bounds__(32) cut_kernel(const TreeDesc* desc,
+                                                 const Entry* nodes,
+                                                 const Entry* root,
+                                                 int levels, int* cut) {
+  __shared__ int next[32];
+  const int l = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+  const TreeDesc d = desc[b];
+  const Entry* nl = nodes + d.node0 + (size_t)l * (d.n - 1) * 2;
+  const unsigned lt = (1u << lane) - 1u;
+  const int rref = root[b * levels + l].ref;
+  int cnt = 1;
+  int ei = -1;  // lane < cnt: the lane's list entry (-1: the root)
+  int ref = lane == 0 ? rref : -1;
+  // each step grows the list by at least one, so at most 31 steps
+  for (int step = 0; step < 32; ++step) {
+    const bool inner = lane < cnt && ref >= 0;
+    const unsigned bi = __ballot_sync(kFull, inner);
+    const int grown = cnt + __popc(bi);
+    if (!bi || grown > 32) break;
+    // in list order: a leaf keeps one slot, an internal node becomes its
+    // two children
+    const int pos = lane + __popc(bi & lt);
+    if (lane < cnt) {
+      if (inner) {
+        next[pos] = 2 * ref;
+        next[pos + 1] = 2 * ref + 1;
+      } else {
+        next[pos] = ei;
+      }
+    }
+    __syncwarp();
+    cnt = grown;
+    ei = lane < cnt ? next[lane] : -1;
+    ref = lane < cnt ? (ei >= 0 ? load_entry(nl + ei).ref : rref) : -1;
+    __syncwarp();
+  }
+  int* out = cut + ((size_t)b * levels + l) * kCutStride;
+  if (lane == 0) out[0] = cnt;
+  if (lane < cnt) out[1 + lane] = ei;
+}
+
 // ---------------------------------------------------------------------------
-// Per level l, the original IDs < n/4^l in leaf order (stable compaction).
-// Counter layout per tree: cnt[(tree*levels + level)*max_tiles + tile].
 // Members of levels 1.. (IDs < n/4^l) before every sorted position: a tile
 // count, an exclusive scan over (level, tile) and a per-tile scan.  Leaves
 // keep their sorted point range, so these are also the counts before every
@@ -724,6 +768,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->qorder, sizeof(int) * std::max<long long>(1, q_total));
   alloc((void**)&f->lpts, sizeof(float4) * std::max<long long>(1, q_total - N));
   alloc((void**)&f->wrank, sizeof(int) * N * f->levels);
+  alloc((void**)&f->cut, sizeof(int) * kCutStride * B * f->levels);
   int max_tiles = blocks_for(max_n, kSortTile);
   uint64_t *keys = nullptr, *keys2 = nullptr;
   int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
@@ -818,7 +863,9 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     else
       leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
     climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
-    launches += 2;
+    cut_kernel<<<dim3(f->levels, B), 32, 0, s>>>(f->desc, f->nodes, f->root,
+                                                 f->levels, f->cut);
+    launches += 3;
     count_launches(launches);
     e = cudaGetLastError();
   }
@@ -840,7 +887,7 @@ cudaError_t free_forest(Forest* f, cudaStream_t s) {
   if (!f) return cudaSuccess;
   cudaError_t e = cudaSuccess;
   void* bufs[] = {f->desc,  f->pts,    f->lpts,  f->nodes,
-                  f->root,  f->qorder, f->wrank};
+                  f->root,  f->qorder, f->wrank, f->cut};
   for (void* p : bufs) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;

@@ -22,6 +22,7 @@ struct Forest {
   Entry* root = nullptr;
   int* qorder = nullptr;
   int* wrank = nullptr;
+  int* cut = nullptr;
   const float* x = nullptr;  // borrowed
 
   ForestView view() const {
@@ -33,6 +34,7 @@ struct Forest {
     v.root = root;
     v.qorder = qorder;
     v.wrank = wrank;
+    v.cut = cut;
     v.x = x;
     v.levels = levels;
     return v;

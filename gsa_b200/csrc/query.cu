@@ -696,29 +696,38 @@ __device__ void leaf_batches(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
 
 // Frontier walk of the packet; leaves go through leaf_batches.  Returns
 // true (warp-uniform) when the frontier would exceed its stack or the step
-// cap is reached.
+// cap is reached.  The walk starts from the level's cut (`cut`: count, then
+// up to 32 entries that cover the tree; -1 is the root), tested in one step.
 template <bool KNN, int CAP, int FRONT>
 __device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
-                              const Entry* root, const float4* pts,
-                              long long max_steps, int m, const Packet& pk,
-                              bool in, float px, float py, float pz,
-                              float& bound, int& nc) {
+                              const Entry* root, const int* cut,
+                              const float4* pts, long long max_steps, int m,
+                              const Packet& pk, bool in, float px, float py,
+                              float pz, float& bound, int& nc) {
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   int top = 0, nleaf = 0;
   {
-    Entry r = load_entry(root);
-    if (r.minid < m &&
-        within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy, pk.hz, r),
-                    pk.R2)) {
-      if (r.ref >= 0) {
-        if (lane == 0) W.front[0] = r.ref;
-        top = 1;
-      } else {
-        if (lane == 0) W.leafq[0] = -1;  // the root itself is the only leaf
-        nleaf = 1;
-      }
+    const int ncut = cut[0];
+    bool pass = false, inner = false;
+    int ei = -1, ref = 0;
+    if (lane < ncut) {
+      ei = cut[1 + lane];
+      Entry e = load_entry(ei >= 0 ? nodes + ei : root);
+      pass = e.minid < m &&
+             within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy,
+                                      pk.hz, e),
+                         pk.R2);
+      inner = e.ref >= 0;
+      ref = e.ref;
     }
+    unsigned bi = __ballot_sync(kFull, pass && inner);
+    unsigned bl = __ballot_sync(kFull, pass && !inner);
+    if (__popc(bi) > FRONT) return true;
+    if (pass && inner) W.front[__popc(bi & lt)] = ref;
+    if (pass && !inner) W.leafq[__popc(bl & lt)] = ei;
+    top = __popc(bi);
+    nleaf = __popc(bl);
   }
   __syncwarp();
   long long steps = 0;
@@ -791,8 +800,10 @@ __global__ void __launch_bounds__(kFWarps * 32)
   bool overflow = false;
   if (__any_sync(kFull, live)) {
     Packet pk = make_packet(live, px, py, pz, bound);
-    overflow = frontier_walk<false>(W, c.nodes, c.root, c.pts, c.max_steps,
-                                    c.m, pk, live, px, py, pz, bound, hc);
+    const int* cut = a.f.cut + ((size_t)b * a.f.levels + s.lev) * kCutStride;
+    overflow = frontier_walk<false>(W, c.nodes, c.root, cut, c.pts,
+                                    c.max_steps, c.m, pk, live, px, py, pz,
+                                    bound, hc);
   }
   __syncwarp();
   int count = 0;
@@ -898,8 +909,9 @@ __global__ void __launch_bounds__(kFWarps * 32)
   bool overflow = false;
   if (__any_sync(kFull, inpk)) {
     Packet pk = make_packet(inpk, px, py, pz, B);
-    overflow = frontier_walk<true>(W, c.nodes, c.root, c.pts, c.max_steps, m,
-                                   pk, inpk, px, py, pz, B, nc);
+    const int* cut = a.f.cut + ((size_t)b * a.f.levels + s.lev) * kCutStride;
+    overflow = frontier_walk<true>(W, c.nodes, c.root, cut, c.pts, c.max_steps,
+                                   m, pk, inpk, px, py, pz, B, nc);
   }
   __syncwarp();
   Top3 t = empty_top3();
