@@ -577,41 +577,61 @@ __global__ void __launch_bounds__(32) cut_kernel(const TreeDesc* desc,
                                                  const Entry* nodes,
                                                  const Entry* root,
                                                  int levels, int* cut) {
-  __shared__ int next[32];
+  constexpr int CH = kCutMax / 32;  // list items per lane: c * 32 + lane
+  __shared__ int next[kCutMax];
   const int l = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
   const TreeDesc d = desc[b];
   const Entry* nl = nodes + d.node0 + (size_t)l * (d.n - 1) * 2;
   const unsigned lt = (1u << lane) - 1u;
   const int rref = root[b * levels + l].ref;
   int cnt = 1;
-  int ei = -1;  // lane < cnt: the lane's list entry (-1: the root)
-  int ref = lane == 0 ? rref : -1;
-  // each step grows the list by at least one, so at most 31 steps
-  for (int step = 0; step < 32; ++step) {
-    const bool inner = lane < cnt && ref >= 0;
-    const unsigned bi = __ballot_sync(kFull, inner);
-    const int grown = cnt + __popc(bi);
-    if (!bi || grown > 32) break;
+  int ei[CH], ref[CH];  // item c * 32 + lane < cnt: entry (-1: the root), ref
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    ei[c] = -1;
+    ref[c] = (c == 0 && lane == 0) ? rref : -1;
+  }
+  // each step grows the list by at least one, so at most kCutMax-1 steps
+  for (int step = 0; step < kCutMax; ++step) {
+    unsigned bi[CH];
+    int grown = cnt, before = 0;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      bi[c] = __ballot_sync(kFull, c * 32 + lane < cnt && ref[c] >= 0);
+      grown += __popc(bi[c]);
+    }
+    if (grown == cnt || grown > kCutMax) break;
     // in list order: a leaf keeps one slot, an internal node becomes its
     // two children
-    const int pos = lane + __popc(bi & lt);
-    if (lane < cnt) {
-      if (inner) {
-        next[pos] = 2 * ref;
-        next[pos + 1] = 2 * ref + 1;
-      } else {
-        next[pos] = ei;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int item = c * 32 + lane;
+      const int pos = item + before + __popc(bi[c] & lt);
+      if (item < cnt) {
+        if ((bi[c] >> lane) & 1u) {
+          next[pos] = 2 * ref[c];
+          next[pos + 1] = 2 * ref[c] + 1;
+        } else {
+          next[pos] = ei[c];
+        }
       }
+      before += __popc(bi[c]);
     }
     __syncwarp();
     cnt = grown;
-    ei = lane < cnt ? next[lane] : -1;
-    ref = lane < cnt ? (ei >= 0 ? load_entry(nl + ei).ref : rref) : -1;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int item = c * 32 + lane;
+      ei[c] = item < cnt ? next[item] : -1;
+      ref[c] = item < cnt ? (ei[c] >= 0 ? load_entry(nl + ei[c]).ref : rref) : -1;
+    }
     __syncwarp();
   }
   int* out = cut + ((size_t)b * levels + l) * kCutStride;
   if (lane == 0) out[0] = cnt;
-  if (lane < cnt) out[1 + lane] = ei;
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+    if (c * 32 + lane < cnt) out[1 + c * 32 + lane] = ei[c];
 }
 
 // ---------------------------------------------------------------------------

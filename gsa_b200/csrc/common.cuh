@@ -14,7 +14,8 @@ namespace gsa {
 void count_launches(int n = 1);
 
 constexpr int kMaxLevels = 4;   // prefixes n, n/4, n/16, n/64
-constexpr int kCutStride = 33;  // per tree and level: count + 32 entries
+constexpr int kCutMax = 32;    // cut entries per tree and level
+constexpr int kCutStride = kCutMax + 1;  // count, then the entries
 constexpr int kMaxLeaf = 32;    // leaf point count fits 5 bits
 constexpr int kMaxPoints = 1 << 26;  // leaf start fits 26 bits
 constexpr unsigned kFull = 0xffffffffu;
@@ -55,7 +56,7 @@ struct ForestView {
   const int* qorder;    // [tree][level][m_l] original IDs < m_l in leaf order
   const int* wrank;     // [point][level] members of the level before the
                         // point's leaf-order position
-  const int* cut;       // [tree][level][kCutStride]: count, then up to 32
+  const int* cut;       // [tree][level][kCutStride]: count, then up to kCutMax
                         // entry indices (-1: the root) that cover the tree
   const float* x;       // borrowed original coordinates (AoS, 3 floats)
   int levels;           // 4 for prefix trees, 1 otherwise

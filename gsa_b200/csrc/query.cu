@@ -697,23 +697,70 @@ __device__ void leaf_batches(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
 // Frontier walk of the packet; leaves go through leaf_batches.  Returns
 // true (warp-uniform) when the frontier would exceed its stack or the step
 // cap is reached.  The walk starts from the level's cut (`cut`: count, then
-// up to 32 entries that cover the tree; -1 is the root), tested in one step.
+// up to kCutMax entries that cover the tree; -1 is the root), tested in one
+// step.  Queued leaves are processed before a round once 32 are waiting, so
+// the queue (64) holds the cut's leaves or one round's on top of fewer than
+// 32.
 template <bool KNN, int CAP, int FRONT>
 __device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
                               const Entry* root, const int* cut,
                               const float4* pts, long long max_steps, int m,
                               const Packet& pk, bool in, float px, float py,
                               float pz, float& bound, int& nc) {
+  static_assert(kCutMax <= 64, "the leaf queue holds the whole cut");
+  constexpr int CH = kCutMax / 32;
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   int top = 0, nleaf = 0;
   {
     const int ncut = cut[0];
+    Entry e[CH];
+    int ei[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      ei[c] = -1;
+      if (c * 32 + lane < ncut) {
+        ei[c] = cut[1 + c * 32 + lane];
+        e[c] = load_entry(ei[c] >= 0 ? nodes + ei[c] : root);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      bool pass = false, inner = false;
+      if (c * 32 + lane < ncut) {
+        pass = e[c].minid < m &&
+               within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy,
+                                        pk.hz, e[c]),
+                           pk.R2);
+        inner = e[c].ref >= 0;
+      }
+      unsigned bi = __ballot_sync(kFull, pass && inner);
+      unsigned bl = __ballot_sync(kFull, pass && !inner);
+      if (top + __popc(bi) > FRONT) return true;
+      if (pass && inner) W.front[top + __popc(bi & lt)] = e[c].ref;
+      if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei[c];
+      top += __popc(bi);
+      nleaf += __popc(bl);
+    }
+  }
+  __syncwarp();
+  long long steps = 0;
+  while (top > 0 || nleaf > 0) {
+    if (++steps > max_steps) return true;
+    if (nleaf >= 32 || top == 0) {
+      leaf_batches<KNN>(W, nodes, root, pts, nleaf, m, in, px, py, pz, bound,
+                        nc);
+      nleaf = 0;
+      __syncwarp();
+      continue;
+    }
+    // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
+    int P = min(top, 16);
     bool pass = false, inner = false;
-    int ei = -1, ref = 0;
-    if (lane < ncut) {
-      ei = cut[1 + lane];
-      Entry e = load_entry(ei >= 0 ? nodes + ei : root);
+    int ei = 0, ref = 0;
+    if (lane < 2 * P) {
+      ei = 2 * W.front[top - P + (lane >> 1)] + (lane & 1);
+      Entry e = load_entry(nodes + ei);
       pass = e.minid < m &&
              within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy,
                                       pk.hz, e),
@@ -721,49 +768,16 @@ __device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
       inner = e.ref >= 0;
       ref = e.ref;
     }
+    __syncwarp();
+    top -= P;
     unsigned bi = __ballot_sync(kFull, pass && inner);
     unsigned bl = __ballot_sync(kFull, pass && !inner);
-    if (__popc(bi) > FRONT) return true;
-    if (pass && inner) W.front[__popc(bi & lt)] = ref;
-    if (pass && !inner) W.leafq[__popc(bl & lt)] = ei;
-    top = __popc(bi);
-    nleaf = __popc(bl);
-  }
-  __syncwarp();
-  long long steps = 0;
-  while (top > 0 || nleaf > 0) {
-    if (++steps > max_steps) return true;
-    if (top > 0) {
-      // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
-      int P = min(top, 16);
-      bool pass = false, inner = false;
-      int ei = 0, ref = 0;
-      if (lane < 2 * P) {
-        ei = 2 * W.front[top - P + (lane >> 1)] + (lane & 1);
-        Entry e = load_entry(nodes + ei);
-        pass = e.minid < m &&
-               within<KNN>(box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy,
-                                        pk.hz, e),
-                           pk.R2);
-        inner = e.ref >= 0;
-        ref = e.ref;
-      }
-      __syncwarp();
-      top -= P;
-      unsigned bi = __ballot_sync(kFull, pass && inner);
-      unsigned bl = __ballot_sync(kFull, pass && !inner);
-      int ni = __popc(bi);
-      if (top + ni > FRONT) return true;
-      if (pass && inner) W.front[top + __popc(bi & lt)] = ref;
-      if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei;
-      top += ni;
-      nleaf += __popc(bl);
-      __syncwarp();
-    }
-    if (nleaf < 32 && top > 0) continue;
-    leaf_batches<KNN>(W, nodes, root, pts, nleaf, m, in, px, py, pz, bound,
-                      nc);
-    nleaf = 0;
+    int ni = __popc(bi);
+    if (top + ni > FRONT) return true;
+    if (pass && inner) W.front[top + __popc(bi & lt)] = ref;
+    if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei;
+    top += ni;
+    nleaf += __popc(bl);
     __syncwarp();
   }
   return false;
