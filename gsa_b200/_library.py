@@ -8,6 +8,8 @@ fallback: a missing library raises immediately.
 import ctypes
 from pathlib import Path
 
+import torch
+
 NATIVE_DIR = Path(__file__).resolve().parent / "_native"
 _loaded = {}
 
@@ -29,3 +31,25 @@ def load(name):
     lib = ctypes.CDLL(str(p))
     _loaded[name] = lib
     return lib
+
+
+_cuda_ready = False
+
+
+def current_stream():
+    """``(device index, raw cudaStream_t)`` of the current CUDA stream: what
+    ``torch.cuda.current_device()`` and ``torch.cuda.current_stream()
+    .cuda_stream`` return, read through torch's C accessors once CUDA is
+    initialised (the public calls re-check the CUDA state on every call, which
+    dominates the host cost of a small query)."""
+    global _cuda_ready
+    if not _cuda_ready:
+        torch.cuda.init()
+        _cuda_ready = True
+    device = torch._C._cuda_getDevice()
+    return device, torch._C._cuda_getCurrentRawStream(device)
+
+
+def stream():
+    """Raw handle of the current CUDA stream."""
+    return current_stream()[1]

@@ -13,7 +13,7 @@ import ctypes
 
 import torch
 
-from ._library import load
+from ._library import load, stream
 
 lib = load("reference_queries")
 P = ctypes.c_void_p
@@ -26,7 +26,7 @@ lib.nn3.restype = I
 
 def call(name, *args):
     values = [a.data_ptr() if isinstance(a, torch.Tensor) else a for a in args]
-    error = getattr(lib, name)(*values, torch.cuda.current_stream().cuda_stream)
+    error = getattr(lib, name)(*values, stream())
     if error:
         raise RuntimeError(f"{name}: CUDA error {error}")
 

@@ -14,7 +14,7 @@ import math
 
 import torch
 
-from ._library import load
+from ._library import current_stream, load, stream as _stream
 
 lib = load("gsa_bvh")
 _ptr, _int = ctypes.c_void_p, ctypes.c_int
@@ -64,10 +64,6 @@ def prefix_sizes(n):
     return [n >> (2 * level) for level in range(4)]
 
 
-def _stream():
-    return torch.cuda.current_stream().cuda_stream
-
-
 def _is_points(x):
     return (
         isinstance(x, torch.Tensor)
@@ -81,7 +77,8 @@ def _is_points(x):
 
 def _is_rows(t, like, rows, width, dtype):
     return (
-        t.device == like.device
+        t.is_cuda
+        and t.get_device() == like.get_device()
         and t.is_contiguous()
         and t.dtype == dtype
         and t.shape == (rows, width)
@@ -95,8 +92,8 @@ class Tree:
         global _pool_device
         if not (
             _is_points(x)
-            and len(x) > 0
-            and x.device.index == torch.cuda.current_device()
+            and x.shape[0] > 0
+            and x.get_device() == current_stream()[0]
             and isinstance(leaf, int)
             and leaf >= 1
         ):
@@ -108,42 +105,40 @@ class Tree:
         _pool_device = x.device.index
         self.x = x
         self.prefix = prefix
-        self.stream = _stream()
+        self.device, self.stream = current_stream()
+        self.sizes = prefix_sizes(x.shape[0]) if prefix else None
         self.ptr = _ptr()
         self.fallback = torch.zeros(1, device=x.device, dtype=torch.int32)
         check(lib.build_bvh(x.data_ptr(), len(x), int(prefix), leaf, ctypes.byref(self.ptr), self.stream))
 
     def level(self, m):
         """Bounds level for support prefix ``m`` (-1 for a plain tree)."""
-        return prefix_sizes(len(self.x)).index(m) if self.prefix else -1
+        return self.sizes.index(m) if self.prefix else -1
 
     def _usable_here(self):
-        return (
-            bool(self.ptr)
-            and torch.cuda.current_device() == self.x.device.index
-            and _stream() == self.stream
-        )
+        return bool(self.ptr) and current_stream() == (self.device, self.stream)
 
     def _check_query(self, q, m, idx, width):
         if not (
             self._usable_here()
-            and q.device == self.x.device
             and _is_points(q)
-            and _is_rows(idx, q, len(q), width, torch.int32)
-            and 1 <= m <= len(self.x)
+            and q.get_device() == self.device
+            and _is_rows(idx, q, q.shape[0], width, torch.int32)
+            and 1 <= m <= self.x.shape[0]
         ):
             raise ValueError("Invalid query buffers, support length, or tree lifetime/device/stream")
 
     def query(self, q, m, d, idx):
         """Exact 3NN of ``q`` against support IDs ``< m``; ``d``/``idx`` (Q, 3)."""
         self._check_query(q, m, idx, 3)
-        if m < 3 or not _is_rows(d, q, len(q), 3, torch.float32):
+        nq = q.shape[0]
+        if m < 3 or not _is_rows(d, q, nq, 3, torch.float32):
             raise ValueError("3NN requires at least 3 supports and FP32 (Q,3) distances")
-        if len(q):
+        if nq:
             check(
                 lib.query_bvh(
-                    self.ptr, q.data_ptr(), len(q), m, self.level(m), d.data_ptr(),
-                    idx.data_ptr(), self.fallback.data_ptr(), _stream(),
+                    self.ptr, q.data_ptr(), nq, m, self.level(m), d.data_ptr(),
+                    idx.data_ptr(), self.fallback.data_ptr(), self.stream,
                 )
             )
         return d, idx
@@ -153,11 +148,12 @@ class Tree:
         self._check_query(q, m, idx, ns)
         if not (isinstance(ns, int) and 1 <= ns <= 32 and math.isfinite(r) and 0 <= r <= _FLT_MAX):
             raise ValueError("Radius query requires K in [1,32] and finite nonnegative FP32 radius")
-        if len(q):
+        nq = q.shape[0]
+        if nq:
             check(
                 lib.query_ball_bvh(
-                    self.ptr, q.data_ptr(), len(q), m, self.level(m), r, ns,
-                    idx.data_ptr(), self.fallback.data_ptr(), _stream(),
+                    self.ptr, q.data_ptr(), nq, m, self.level(m), r, ns,
+                    idx.data_ptr(), self.fallback.data_ptr(), self.stream,
                 )
             )
         return idx
@@ -165,7 +161,7 @@ class Tree:
     def close(self):
         if not self.ptr:
             return
-        if torch.cuda.current_device() != self.x.device.index or _stream() != self.stream:
+        if current_stream() != (self.device, self.stream):
             raise ValueError("Close the tree on its original device and stream")
-        check(lib.free_bvh(self.ptr, 1, _stream()))
+        check(lib.free_bvh(self.ptr, 1, self.stream))
         self.ptr = _ptr()

@@ -20,12 +20,12 @@ statistics replay the reference's short-circuit order over those flags, so
 
 import ctypes
 import math
-import threading
 
 import torch
 
 from . import runtime as er
 from . import reference as rt
+from ._library import current_stream, stream as _stream
 
 _FLT_MAX = torch.finfo(torch.float32).max
 _MAX_DEVICE_CANDIDATES = 64
@@ -37,33 +37,16 @@ er.lib.reuse_rows.argtypes = [_I, _P, _P, _I, _I, _I, _P, _P, _P]
 er.lib.reuse_rows.restype = _I
 er.lib.gather_rows.argtypes = [_P, _I, _I, _I, _P, _P]
 er.lib.gather_rows.restype = _I
-_pinned = threading.local()
-
-
-def _pinned_flags(n):
-    """Per-thread pinned host buffer for reading comparison flags (sessions
-    on different host threads and streams never share one)."""
-    buf = getattr(_pinned, "flags", None)
-    if buf is None or buf.numel() < n:
-        # a normal tensor even when first needed inside inference mode, so
-        # later calls outside it can still copy into it
-        with torch.inference_mode(False):
-            buf = _pinned.flags = torch.empty(max(256, n), dtype=torch.int32, pin_memory=True)
-    return buf[:n]
-
-
 class _CudaOps:
     """Device side of the session: comparisons, row gathers, trees."""
 
     lib = er.lib
 
-    @staticmethod
-    def current():
-        return torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream
+    current = staticmethod(current_stream)
 
     @staticmethod
     def on_device(x, device):
-        return x.is_cuda and x.device.index == device
+        return x.is_cuda and x.get_device() == device
 
     def mismatch(self, pairs, device):
         """Launch one comparison kernel for all (a, b) pairs; returns the
@@ -75,7 +58,7 @@ class _CudaOps:
         c = (ctypes.c_longlong * n)(*[p[0].numel() for p in pairs])
         er.check(
             self.lib.coords_mismatch(
-                n, a, b, c, flags.data_ptr(), torch.cuda.current_stream().cuda_stream
+                n, a, b, c, flags.data_ptr(), _stream()
             )
         )
         return flags
@@ -87,16 +70,15 @@ class _CudaOps:
         er.check(
             self.lib.reuse_rows(
                 n, src, flags.data_ptr(), 32, rows, cols, out.data_ptr(), None,
-                torch.cuda.current_stream().cuda_stream,
+                _stream(),
             )
         )
 
-    def fetch(self, flags):
-        """Read the flags on the host (the call's one synchronisation)."""
-        host = _pinned_flags(flags.numel())
-        host.copy_(flags, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return host.tolist()
+    @staticmethod
+    def fetch(flags):
+        """Read the flags on the host (the call's one synchronisation: a
+        blocking copy on the current stream)."""
+        return flags.tolist()
 
     def copy_cols(self, out, result, k):
         """out[i, j] = result[i, j] for i < len(out), j < k (out contiguous
@@ -107,13 +89,18 @@ class _CudaOps:
         er.check(
             self.lib.gather_rows(
                 result.data_ptr(), result.shape[1], out.shape[0], k, out.data_ptr(),
-                torch.cuda.current_stream().cuda_stream,
+                _stream(),
             )
         )
 
     @staticmethod
     def zeros(rows, device):
         return torch.zeros((rows, 32), device=device, dtype=torch.int32)
+
+    @staticmethod
+    def rows(rows, device):
+        """Result rows that the tree query writes in full."""
+        return torch.empty((rows, 32), device=device, dtype=torch.int32)
 
     @staticmethod
     def snapshot(x):
@@ -164,7 +151,6 @@ class QuerySession:
         return y
 
     def _check(self, x):
-        device, stream = self._ops.current()
         if not (
             not self.closed
             and x.ndim == 2
@@ -172,15 +158,14 @@ class QuerySession:
             and x.is_contiguous()
             and x.dtype == torch.float32
             and self._ops.on_device(x, self.device)
-            and self.device == device
-            and stream == self.stream
+            and self._ops.current() == (self.device, self.stream)
         ):
             raise ValueError(
                 "Use an open session with contiguous FP32 (N,3) tensors on its original CUDA device and stream"
             )
 
     def _tree_candidates(self, x):
-        m = len(x)
+        m = x.shape[0]
         return [(root, tree) for root, tree, sizes in self.trees if m in sizes]
 
     def _pick_tree(self, x, candidates, flags):
@@ -201,7 +186,7 @@ class QuerySession:
         candidates = self._tree_candidates(x)
         flags = []
         if candidates:
-            pairs = [(x, root[: len(x)]) for root, _ in candidates]
+            pairs = [(x, root[: x.shape[0]]) for root, _ in candidates]
             flags = self._ops.fetch(self._ops.mismatch(pairs, x.device))
         return self._pick_tree(x, candidates, flags)
 
@@ -209,11 +194,12 @@ class QuerySession:
     def ball_into(self, q, x, r, k, out):
         self._check(x)
         self._check(q)
+        n, nq = x.shape[0], q.shape[0]
         if not (
-            len(x) >= 1
+            n >= 1
             and isinstance(k, int)
             and 1 <= k <= 32
-            and out.shape == (len(q), k)
+            and out.shape == (nq, k)
             and out.dtype == torch.int32
             and out.device == q.device
             and out.is_contiguous()
@@ -224,10 +210,9 @@ class QuerySession:
                 "ball_into requires nonempty support, finite nonnegative FP32 radius, K in [1,32], and contiguous CUDA int32 output (Q,K)"
             )
         self.stats["ball_calls"] += 1
-        if not len(q):
+        if not nq:
             return
-        n, nq = len(x), len(q)
-        memo = [e for e in self.memo if e[2] == r and n == len(e[0]) and nq <= len(e[1])]
+        memo = [e for e in self.memo if e[2] == r and n == e[0].shape[0] and nq <= e[1].shape[0]]
         trees = self._tree_candidates(x) if n > self.threshold else []
         pairs = []
         for saved_x, saved_q, _, _ in memo:
@@ -254,11 +239,13 @@ class QuerySession:
             self.stats["ball_hits"] += 1
             return
         cap = 32
-        result = self._ops.zeros(nq, q.device)
         if n <= self.threshold:
+            # the scan leaves rows without a hit untouched: start from zeros
+            result = self._ops.zeros(nq, q.device)
             owned_x = self._snapshot(x)
             self.ball_reference(1, n, nq, r, cap, q[None], owned_x[None], result[None])
         else:
+            result = self._ops.rows(nq, q.device)
             tree = self._pick_tree(x, trees, flags[2 * len(memo):])
             owned_x = tree.x[:n]
             tree.ball(q, n, r, cap, result)
@@ -269,9 +256,10 @@ class QuerySession:
     def nn_into(self, q, x, d, ids):
         self._check(x)
         self._check(q)
+        n, nq = x.shape[0], q.shape[0]
         if not (
-            len(x) >= 3
-            and d.shape == ids.shape == (len(q), 3)
+            n >= 3
+            and d.shape == ids.shape == (nq, 3)
             and d.dtype == torch.float32
             and ids.dtype == torch.int32
             and d.device == ids.device == q.device
@@ -282,12 +270,12 @@ class QuerySession:
                 "nn_into requires at least 3 supports and contiguous CUDA FP32 distances/int32 IDs, both (Q,3)"
             )
         self.stats["nn_calls"] += 1
-        if not len(q):
+        if not nq:
             return
-        if len(x) <= self.threshold:
-            self.nn_reference(1, len(q), len(x), q[None], x[None], d[None], ids[None])
+        if n <= self.threshold:
+            self.nn_reference(1, nq, n, q[None], x[None], d[None], ids[None])
         else:
-            self._tree(x).query(q, len(x), d, ids)
+            self._tree(x).query(q, n, d, ids)
 
     def close(self, collect=False):
         if self.closed:

@@ -78,6 +78,12 @@ class OracleOps:
         return torch.zeros((rows, 32), dtype=torch.int32)
 
     @staticmethod
+    def rows(rows, device):
+        # not zero-filled, like the device session's tree result rows: the
+        # tree query must write every row
+        return torch.full((rows, 32), -7, dtype=torch.int32)
+
+    @staticmethod
     def snapshot(x):
         return x.clone()
 
