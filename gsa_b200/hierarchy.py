@@ -44,22 +44,52 @@ def unit_counts(sizes):
     return sum(sizes[:4]), sum(sizes[1:5]), sum(sizes[:4])
 
 
-def run_session(session, P, sizes=ROOM_SIZES, radii=ROOM_RADII):
+def session_outputs(sizes=ROOM_SIZES, device="cuda", flat=None):
+    """Output tensors of one ``run_session`` call as views of one flat int32
+    buffer (distances viewed as FP32), so a scene's results leave the device
+    in a single copy.  Returns ``(flat, outputs)``; pass ``flat`` to reuse a
+    buffer of ``session_words(sizes)`` elements."""
+    if flat is None:
+        flat = torch.empty(session_words(sizes), dtype=torch.int32, device=device)
+    out, at = {}, 0
+
+    def take(key, rows, width, dtype):
+        nonlocal at
+        v = flat[at : at + rows * width].view(rows, width)
+        out[key] = v if dtype == torch.int32 else v.view(dtype)
+        at += rows * width
+
+    for s in range(4):
+        take(f"ball{s}", sizes[s], K, torch.int32)
+        take(f"hit{s}", sizes[s + 1], K, torch.int32)
+    for s in range(3, -1, -1):
+        take(f"nnd{s}", sizes[s], 3, torch.float32)
+        take(f"nni{s}", sizes[s], 3, torch.int32)
+    return flat, out
+
+
+def session_words(sizes=ROOM_SIZES):
+    """32-bit words of one scene's outputs."""
+    return sum(sizes[s] * K + sizes[s + 1] * K + 6 * sizes[s] for s in range(4))
+
+
+def run_session(session, P, sizes=ROOM_SIZES, radii=ROOM_RADII, out=None):
     """Run the hierarchy on one scene through ``QuerySession``; returns the
-    outputs as a dict of device tensors."""
-    out = {}
+    outputs as a dict of device tensors (``out``: preallocated tensors with
+    the same keys, e.g. from ``session_outputs``)."""
+    if out is None:
+        out = {}
+        for s in range(4):
+            out[f"ball{s}"] = torch.empty((sizes[s], K), dtype=torch.int32, device=P.device)
+            out[f"hit{s}"] = torch.empty((sizes[s + 1], K), dtype=torch.int32, device=P.device)
+            out[f"nnd{s}"] = torch.empty((sizes[s], 3), device=P.device)
+            out[f"nni{s}"] = torch.empty((sizes[s], 3), dtype=torch.int32, device=P.device)
     for s in range(4):
         ps, pn = P[: sizes[s]], P[: sizes[s + 1]]
-        rows = torch.empty((sizes[s], K), dtype=torch.int32, device=P.device)
-        session.ball_into(ps, ps, radii[s], K, rows)
-        hits = torch.empty((sizes[s + 1], K), dtype=torch.int32, device=P.device)
-        session.ball_into(pn, ps, radii[s], K, hits)
-        out[f"ball{s}"], out[f"hit{s}"] = rows, hits
+        session.ball_into(ps, ps, radii[s], K, out[f"ball{s}"])
+        session.ball_into(pn, ps, radii[s], K, out[f"hit{s}"])
     for s in range(3, -1, -1):
-        d = torch.empty((sizes[s], 3), device=P.device)
-        i = torch.empty((sizes[s], 3), dtype=torch.int32, device=P.device)
-        session.nn_into(P[: sizes[s]], P[: sizes[s + 1]], d, i)
-        out[f"nnd{s}"], out[f"nni{s}"] = d, i
+        session.nn_into(P[: sizes[s]], P[: sizes[s + 1]], out[f"nnd{s}"], out[f"nni{s}"])
     return out
 
 

@@ -249,7 +249,15 @@ class QuerySession:
             tree = self._pick_tree(x, trees, flags[2 * len(memo):])
             owned_x = tree.x[:n]
             tree.ball(q, n, r, cap, result)
-        self.memo.append((owned_x, self._snapshot(q), r, result))
+        if q.data_ptr() == x.data_ptr() and nq == n:
+            # a self-query: the query snapshot would be a second copy of the
+            # support snapshot's values, so the entry shares it (snapshots
+            # are never written); the byte count is the copy's
+            owned_q = owned_x
+            self.stats["snapshot_bytes"] += owned_q.numel() * owned_q.element_size()
+        else:
+            owned_q = self._snapshot(q)
+        self.memo.append((owned_x, owned_q, r, result))
         self.stats["cache_bytes"] += result.numel() * result.element_size()
         self._ops.copy_cols(out, result, k)
 
