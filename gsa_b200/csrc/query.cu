@@ -73,6 +73,7 @@ struct QArgs {
   int* out;
   float* dout;
   int* fallback;
+  int pw;             // frontier kernels: queries per warp (8, 16 or 32)
 };
 
 __device__ __forceinline__ bool nonempty(const Entry& e) {
@@ -791,10 +792,10 @@ __global__ void __launch_bounds__(kFWarps * 32)
   TreeDesc d = a.f.desc[b];
   Slot s = slot_setup(a, d, b);
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
+  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * a.pw;
   if (t0 >= s.slots) return;  // warp-uniform
   WarpBufs<kPacketCap, 2 * STACK>& W = wb[warp];
-  int qi = slot_query(s, d, (int)t0 + lane);
+  int qi = lane < a.pw ? slot_query(s, d, (int)t0 + lane) : -1;
   bool active = qi >= 0;
   float px = 0.f, py = 0.f, pz = 0.f;
   if (active) {
@@ -871,10 +872,10 @@ __global__ void __launch_bounds__(kFWarps * 32)
   TreeDesc d = a.f.desc[b];
   Slot s = slot_setup(a, d, b);
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * 32;
+  long long t0 = ((long long)blockIdx.x * kFWarps + warp) * a.pw;
   if (t0 >= s.slots) return;  // warp-uniform
   WarpBufs<kCandCap, 2 * STACK>& W = wb[warp];
-  int qi = slot_query(s, d, (int)t0 + lane);
+  int qi = lane < a.pw ? slot_query(s, d, (int)t0 + lane) : -1;
   bool active = qi >= 0;
   float px = 0.f, py = 0.f, pz = 0.f;
   if (active) {
@@ -1080,6 +1081,7 @@ QArgs make_args(const Forest& f, const QuerySet& qs) {
   a.out = nullptr;
   a.dout = nullptr;
   a.fallback = nullptr;
+  a.pw = 32;
   return a;
 }
 
@@ -1099,17 +1101,41 @@ int sm_count() {
   return cached[dev];
 }
 
+// Queries per warp of a frontier launch.  A packet of 32 queries shares one
+// walk of the tree, which is the cheapest per query; a launch whose grid
+// would hold fewer than four blocks per SM (a single scene) takes narrower
+// packets (16, then 8 queries) so that more warps walk at once: each walk is
+// shorter and the launch's latency falls, at some cost in instructions per
+// query (one scene of 24,000 points: radius stage 0 108 -> 90 us, 3NN stage
+// 0 57 -> 51 us; 8 or more such scenes keep 32).
+constexpr int kPacketMin = 8;
+constexpr int kPacketFill = 4;  // blocks per SM below which packets narrow
+int packet_width(const Forest& f, long long slots) {
+  int pw = 32;
+  while (pw > kPacketMin &&
+         (slots + kFWarps * pw - 1) / (kFWarps * pw) * f.B <
+             (long long)kPacketFill * sm_count())
+    pw >>= 1;
+  return pw;
+}
+
 // The warp scan answers a launch when its support prefixes are small, or
 // when the tree kernels' grid would not fill the SMs (few queries) and the
 // scan's work, queries x prefix, stays bounded (a 1,000,000-point scene's
 // 15,625 level-3 points against its 3,906-point prefix: 0.36 ms on the tree
-// grid of 122 blocks).  scan_max 0 keeps every launch on the tree.
-bool prefer_scan(const Forest& f, const QuerySet& qs, int scan_max) {
+// grid of 122 blocks).  `narrow`: count the tree grid at the launch's packet
+// width (radius launches; one scene's 6,000 level-1 radius queries then take
+// the tree, 30 us against 53 us for the scan), else at 32 queries per warp
+// (3NN, whose scan stays faster there: 28 us against 38 us).  scan_max 0
+// keeps every launch on the tree.
+bool prefer_scan(const Forest& f, const QuerySet& qs, int scan_max,
+                 bool narrow) {
   const int m = max_prefix(f, qs);
   if (m <= scan_max) return true;
   if (scan_max <= 0) return false;
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
-  long long blocks = (slots + kFWarps * 32 - 1) / (kFWarps * 32) * f.B;
+  const int pw = narrow ? packet_width(f, slots) : 32;
+  long long blocks = (slots + kFWarps * pw - 1) / (kFWarps * pw) * f.B;
   if (blocks >= sm_count()) return false;
   long long q = qs.qseg_host ? qs.qseg_host[f.B] : qs.nq;
   return q * (long long)m <= (1ll << 26);
@@ -1124,7 +1150,7 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   a.ns = ns;
   a.out = out;
   a.fallback = fallback;
-  if (prefer_scan(f, qs, GSA_RADIUS_SCAN_MAX)) {
+  if (prefer_scan(f, qs, GSA_RADIUS_SCAN_MAX, true)) {
     long long nq = max_queries(f, qs);
     if (nq <= 0) return cudaSuccess;
     dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
@@ -1136,7 +1162,8 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
   if (slots <= 0) return cudaSuccess;
   count_launches();
   if (GSA_RADIUS_FRONTIER) {
-    dim3 grid((unsigned)((slots + kFWarps * 32 - 1) / (kFWarps * 32)), f.B);
+    a.pw = packet_width(f, slots);
+    dim3 grid((unsigned)((slots + kFWarps * a.pw - 1) / (kFWarps * a.pw)), f.B);
     radius_frontier_kernel<GSA_STACK><<<grid, kFWarps * 32, 0, s>>>(a);
   } else {
     dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
@@ -1151,7 +1178,7 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
   a.dout = d;
   a.out = ix;
   a.fallback = fallback;
-  if (prefer_scan(f, qs, GSA_KNN_SCAN_MAX)) {
+  if (prefer_scan(f, qs, GSA_KNN_SCAN_MAX, false)) {
     long long nq = max_queries(f, qs);
     if (nq <= 0) return cudaSuccess;
     dim3 grid((unsigned)((nq + kScanWarps - 1) / kScanWarps), f.B);
@@ -1163,7 +1190,8 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
   if (slots <= 0) return cudaSuccess;
   count_launches();
   if (GSA_KNN_FRONTIER) {
-    dim3 grid((unsigned)((slots + kFWarps * 32 - 1) / (kFWarps * 32)), f.B);
+    a.pw = packet_width(f, slots);
+    dim3 grid((unsigned)((slots + kFWarps * a.pw - 1) / (kFWarps * a.pw)), f.B);
     knn3_frontier_kernel<GSA_STACK><<<grid, kFWarps * 32, 0, s>>>(a);
   } else {
     dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);

@@ -12,143 +12,131 @@
 //    are (inf, 0).  (The reference compares in double against 1e40, which
 //    rejects +inf and NaN exactly like the finite test used here.)
 //
-// B200 execution: each block owns 256 queries of one batch item and streams
-// the support through shared memory in SoA tiles (broadcast reads); radius
-// rows are assembled in shared memory and stored row-by-row with coalesced
-// warp writes.  The block stops streaming once every query has `ns` hits.
+// B200 execution: one warp per query.  Lane l tests support IDs l, l+32, ...
+// in ascending blocks of 32; for the radius scan a ballot orders each block's
+// hits by ID, so the row is written in scan order and the warp stops once it
+// holds `ns` hits.  For 3NN each lane keeps the best three of its IDs and the
+// warp merges them by shuffles in (d2, id) order, which is the order an
+// ascending scan with strict `<` produces.  One warp per query keeps a call
+// with few queries (the small supports the session sends here) spread over
+// the SMs instead of a few threads each scanning the whole support.
 #include <algorithm>
 #include "common.cuh"
 
 namespace gsa {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kTile = 1024;
-constexpr int kSmemK = 32;
+constexpr int kWarps = 8;  // queries per block
 
-__device__ __forceinline__ void load_tile(const float* x, int base, int count,
-                                          float* sx, float* sy, float* sz) {
-  for (int i = threadIdx.x; i < count; i += kThreads) {
-    const float* p = x + 3ll * (base + i);
-    sx[i] = p[0];
-    sy[i] = p[1];
-    sz[i] = p[2];
-  }
-}
-
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kWarps * 32)
     ball_scan_kernel(int n, int m, float radius, int ns, const float* q,
                      const float* x, int* idx) {
-  __shared__ float sx[kTile], sy[kTile], sz[kTile];
-  __shared__ int rows[kThreads][kSmemK + 1];
-  int bi = blockIdx.y;
-  int t = blockIdx.x * kThreads + threadIdx.x;
-  bool valid = t < m;
-  const float* qb = q + 3ll * m * bi;
-  const float* xb = x + 3ll * n * bi;
-  int* ob = idx + (long long)m * ns * bi;
-  float px = 0.f, py = 0.f, pz = 0.f;
-  if (valid) {
-    px = qb[3ll * t];
-    py = qb[3ll * t + 1];
-    pz = qb[3ll * t + 2];
-  }
+  const int lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= m) return;  // warp-uniform
+  const long long row = (long long)m * blockIdx.y + t;
+  const float* qp = q + 3ll * row;
+  const float* xb = x + 3ll * n * blockIdx.y;
+  int* o = idx + row * ns;
+  const float px = qp[0], py = qp[1], pz = qp[2];
   const float r2 = __fmul_rn(radius, radius);
-  const bool in_smem = ns <= kSmemK;
-  int* row = rows[threadIdx.x];
-  int cnt = 0;
-  for (int base = 0; base < n; base += kTile) {
-    if (!__syncthreads_or(valid && cnt < ns)) break;
-    int c = min(kTile, n - base);
-    load_tile(xb, base, c, sx, sy, sz);
-    __syncthreads();
-    if (valid) {
-      for (int k = 0; k < c && cnt < ns; ++k) {
-        if (exact_d2(px, py, pz, sx[k], sy[k], sz[k]) < r2) {
-          int id = base + k;
-          if (in_smem) {
-            row[cnt] = id;
-          } else {
-            int* o = ob + (long long)t * ns;
-            if (cnt == 0)
-              for (int l = 0; l < ns; ++l) o[l] = id;
-            o[cnt] = id;
-          }
-          ++cnt;
-        }
-      }
+  const unsigned lt = (1u << lane) - 1u;
+  int cnt = 0, first = 0;
+  for (int base = 0; base < n && cnt < ns; base += 32) {
+    const int k = base + lane;
+    bool hit = false;
+    if (k < n) {
+      const float* p = xb + 3ll * k;
+      hit = exact_d2(px, py, pz, p[0], p[1], p[2]) < r2;
     }
-    __syncthreads();
+    const unsigned hm = __ballot_sync(kFull, hit);
+    if (!hm) continue;  // warp-uniform
+    if (!cnt) first = base + __ffs(hm) - 1;
+    const int slot = cnt + __popc(hm & lt);
+    if (hit && slot < ns) o[slot] = k;
+    cnt += __popc(hm);
   }
-  if (!in_smem) return;
-  __syncwarp();
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = 0; j < 32; ++j) {
-    int tj = blockIdx.x * kThreads + warp * 32 + j;
-    int cj = __shfl_sync(kFull, cnt, j);
-    if (tj >= m || cj == 0) continue;
-    if (lane < ns) {
-      const int* rj = rows[warp * 32 + j];
-      ob[(long long)tj * ns + lane] = rj[lane < cj ? lane : 0];
-    }
-  }
+  // pad with the first hit; a row without one stays untouched
+  if (cnt)
+    for (int s = cnt + lane; s < ns; s += 32) o[s] = first;
 }
 
-__global__ void __launch_bounds__(kThreads)
+// (d, i) before (e, j) in (squared distance, ID) order.
+__device__ __forceinline__ bool before(float d, int i, float e, int j) {
+  return d < e || (d == e && i < j);
+}
+
+__global__ void __launch_bounds__(kWarps * 32)
     nn3_scan_kernel(int n, int m, const float* q, const float* x, float* d,
                     int* idx) {
-  __shared__ float sx[kTile], sy[kTile], sz[kTile];
-  int bi = blockIdx.y;
-  int t = blockIdx.x * kThreads + threadIdx.x;
-  bool valid = t < n;
-  const float* qb = q + 3ll * n * bi;
-  const float* xb = x + 3ll * m * bi;
-  float px = 0.f, py = 0.f, pz = 0.f;
-  if (valid) {
-    px = qb[3ll * t];
-    py = qb[3ll * t + 1];
-    pz = qb[3ll * t + 2];
-  }
+  const int lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= n) return;  // warp-uniform
+  const long long row = (long long)n * blockIdx.y + t;
+  const float* qp = q + 3ll * row;
+  const float* xb = x + 3ll * m * blockIdx.y;
+  const float px = qp[0], py = qp[1], pz = qp[2];
   const float inf = __int_as_float(0x7f800000);
   float b0 = inf, b1 = inf, b2 = inf;
-  int i0 = 0, i1 = 0, i2 = 0;
-  for (int base = 0; base < m; base += kTile) {
-    int c = min(kTile, m - base);
-    __syncthreads();
-    load_tile(xb, base, c, sx, sy, sz);
-    __syncthreads();
-    if (!valid) continue;
-    for (int k = 0; k < c; ++k) {
-      float v = exact_d2(px, py, pz, sx[k], sy[k], sz[k]);
-      if (v < b2) {  // false for +inf and NaN
-        int id = base + k;
-        if (v < b1) {
-          b2 = b1;
-          i2 = i1;
-          if (v < b0) {
-            b1 = b0;
-            i1 = i0;
-            b0 = v;
-            i0 = id;
-          } else {
-            b1 = v;
-            i1 = id;
-          }
+  int i0 = INT_MAX, i1 = INT_MAX, i2 = INT_MAX;
+  for (int k = lane; k < m; k += 32) {
+    const float* p = xb + 3ll * k;
+    const float v = exact_d2(px, py, pz, p[0], p[1], p[2]);
+    if (v < b2) {  // false for +inf and NaN; ascending k keeps lower IDs
+      if (v < b1) {
+        b2 = b1;
+        i2 = i1;
+        if (v < b0) {
+          b1 = b0;
+          i1 = i0;
+          b0 = v;
+          i0 = k;
         } else {
-          b2 = v;
-          i2 = id;
+          b1 = v;
+          i1 = k;
         }
+      } else {
+        b2 = v;
+        i2 = k;
       }
     }
   }
-  if (valid) {
-    long long o = 3ll * n * bi + 3ll * t;
-    d[o] = b0;
-    d[o + 1] = b1;
-    d[o + 2] = b2;
-    idx[o] = i0;
-    idx[o + 1] = i1;
-    idx[o + 2] = i2;
+  // butterfly merge of two (d2, id)-sorted triples; every lane ends with the
+  // warp's best three
+  for (int off = 16; off; off >>= 1) {
+    const float e0 = __shfl_xor_sync(kFull, b0, off);
+    const float e1 = __shfl_xor_sync(kFull, b1, off);
+    const float e2 = __shfl_xor_sync(kFull, b2, off);
+    const int j0 = __shfl_xor_sync(kFull, i0, off);
+    const int j1 = __shfl_xor_sync(kFull, i1, off);
+    const int j2 = __shfl_xor_sync(kFull, i2, off);
+    bool a = before(b0, i0, e0, j0);
+    const float r0 = a ? b0 : e0;
+    const int s0 = a ? i0 : j0;
+    // heads left after the first pick: (x0, x1) of one list, (y0, y1) of the
+    // other
+    const float x0 = a ? b1 : b0, x1 = a ? b2 : b1;
+    const int u0 = a ? i1 : i0, u1 = a ? i2 : i1;
+    const float y0 = a ? e0 : e1, y1 = a ? e1 : e2;
+    const int w0 = a ? j0 : j1, w1 = a ? j1 : j2;
+    a = before(x0, u0, y0, w0);
+    const float r1 = a ? x0 : y0;
+    const int s1 = a ? u0 : w0;
+    const float z = a ? x1 : x0, y = a ? y0 : y1;
+    const int uz = a ? u1 : u0, wy = a ? w0 : w1;
+    const bool c = before(z, uz, y, wy);
+    b0 = r0;
+    i0 = s0;
+    b1 = r1;
+    i1 = s1;
+    b2 = c ? z : y;
+    i2 = c ? uz : wy;
+  }
+  if (lane < 3) {
+    const float v = lane == 0 ? b0 : (lane == 1 ? b1 : b2);
+    const int id = lane == 0 ? i0 : (lane == 1 ? i1 : i2);
+    d[3 * row + lane] = v;
+    idx[3 * row + lane] = id == INT_MAX ? 0 : id;
   }
 }
 
@@ -163,10 +151,10 @@ GSA_API int ball(int b, int n, int m, float r, int ns, const float* q,
   if (b < 0 || n < 0 || m < 0 || ns < 1) return -2;
   if (!b || !m) return 0;
   if (!q || !idx || (n && !x)) return -2;
-  dim3 grid((m + kThreads - 1) / kThreads, b);
+  dim3 grid((m + kWarps - 1) / kWarps, b);
   count_launches();
-  ball_scan_kernel<<<grid, kThreads, 0, (cudaStream_t)s>>>(n, m, r, ns, q, x,
-                                                           idx);
+  ball_scan_kernel<<<grid, kWarps * 32, 0, (cudaStream_t)s>>>(n, m, r, ns, q,
+                                                             x, idx);
   return cudaGetLastError();
 }
 
@@ -176,8 +164,9 @@ GSA_API int nn3(int b, int n, int m, const float* q, const float* x, float* d,
   if (b < 0 || n < 0 || m < 0) return -2;
   if (!b || !n) return 0;
   if (!q || !d || !idx || (m && !x)) return -2;
-  dim3 grid((n + kThreads - 1) / kThreads, b);
+  dim3 grid((n + kWarps - 1) / kWarps, b);
   count_launches();
-  nn3_scan_kernel<<<grid, kThreads, 0, (cudaStream_t)s>>>(n, m, q, x, d, idx);
+  nn3_scan_kernel<<<grid, kWarps * 32, 0, (cudaStream_t)s>>>(n, m, q, x, d,
+                                                            idx);
   return cudaGetLastError();
 }
