@@ -301,55 +301,81 @@ __device__ __forceinline__ void emit(bool want, T rec, T* list, int* count) {
 // Arrival counters start at the number of leaf children (leaves are complete
 // before any climb starts); a node with two leaf children starts a climb and
 // never receives an arrival.
-__global__ void karras_kernel(const TreeDesc* desc, const uint64_t* keys,
-                              int* parent, int* counter, int leaf,
-                              int4* leaves, int* leaf_count, int* starts,
-                              int* start_count) {
-  int b = blockIdx.y;
-  TreeDesc d = desc[b];
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  int n = d.n;
-  bool valid = i < n - 1;
-  int4 rec0 = make_int4(b, 0, n - 1, -1), rec1 = rec0;
-  bool want0 = i == 0 && n <= leaf, want1 = false;
-  if (valid) {
-    const uint64_t* k = keys + d.p0;
-    int* par = parent + (d.p0 - b);
-    int dir =
+//
+// A node is kept exactly when its range reaches `leaf` positions past i in
+// its direction: the common prefix with a key k positions away only shrinks
+// as k grows, so one comparison at distance `leaf` decides it.  Each block
+// first tests its nodes that way and lists its kept nodes (about one in ten)
+// in shared memory; its warps then run the range, split and record work on
+// the list only, so the long binary searches of high nodes run on dense
+// warps instead of one lane in ten.
+__global__ void __launch_bounds__(256)
+    karras_kernel(const TreeDesc* desc, const uint64_t* keys, int* parent,
+                  int* counter, int leaf, int4* leaves, int* leaf_count,
+                  int* starts, int* start_count) {
+  __shared__ int kept[256];
+  __shared__ int nkept;
+  const int b = blockIdx.y;
+  const TreeDesc d = desc[b];
+  const int n = d.n;
+  const uint64_t* k = keys + d.p0;
+  int* par = parent + (d.p0 - b);
+  int* cnt = counter + (d.p0 - b);
+  if (threadIdx.x == 0) nkept = 0;
+  __syncthreads();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  emit(i == 0 && n <= leaf, make_int4(b, 0, n - 1, -1), leaves + d.p0,
+       leaf_count + b);
+  if (i < n - 1) {
+    const int dir =
         common_prefix(k, n, i, i + 1) > common_prefix(k, n, i, i - 1) ? 1 : -1;
-    int dmin = common_prefix(k, n, i, i - dir);
-    int lmax = 2;
-    while (common_prefix(k, n, i, i + lmax * dir) > dmin) lmax <<= 1;
-    int l = 0;
-    for (int t = lmax >> 1; t >= 1; t >>= 1)
-      if (common_prefix(k, n, i, i + (l + t) * dir) > dmin) l += t;
-    int j = i + l * dir;
-    int first = min(i, j), last = max(i, j);
-    int leaf_children = 0;
-    // Only kept nodes need their split, parent links and leaf records: a
-    // node of at most `leaf` points lies inside a leaf (its parent link is
-    // never followed; a kept node's parent is kept).
-    if (last - first + 1 > leaf) {
-      int dnode = common_prefix(k, n, i, j);
+    const int dmin = common_prefix(k, n, i, i - dir);
+    if (common_prefix(k, n, i, i + leaf * dir) > dmin)
+      kept[atomicAdd(&nkept, 1)] = (i << 1) | (dir > 0);
+    else
+      cnt[i] = 0;
+  }
+  __syncthreads();
+  const int total = nkept;
+  const int lane = threadIdx.x & 31;
+  // smallest power of two above `leaf`: every kept range reaches it
+  const int lstart = 1 << (32 - __clz(leaf));
+  for (int k0 = threadIdx.x & ~31; k0 < total; k0 += blockDim.x) {
+    const bool act = k0 + lane < total;
+    int node = 0;
+    bool want0 = false, want1 = false;
+    int4 rec0 = make_int4(0, 0, 0, 0), rec1 = rec0;
+    if (act) {
+      const int e = kept[k0 + lane];
+      node = e >> 1;
+      const int dir = (e & 1) ? 1 : -1;
+      const int dmin = common_prefix(k, n, node, node - dir);
+      int lmax = lstart;
+      while (common_prefix(k, n, node, node + lmax * dir) > dmin) lmax <<= 1;
+      int l = 0;
+      for (int t = lmax >> 1; t >= 1; t >>= 1)
+        if (common_prefix(k, n, node, node + (l + t) * dir) > dmin) l += t;
+      const int j = node + l * dir;
+      const int first = min(node, j), last = max(node, j);
+      const int dnode = common_prefix(k, n, node, j);
       int s = 0, t = l;
       do {
         t = (t + 1) >> 1;
-        if (common_prefix(k, n, i, i + (s + t) * dir) > dnode) s += t;
+        if (common_prefix(k, n, node, node + (s + t) * dir) > dnode) s += t;
       } while (t > 1);
-      int gamma = i + s * dir + min(dir, 0);
-      if (first != gamma) par[gamma] = (i << 1) | 0;
-      if (last != gamma + 1) par[gamma + 1] = (i << 1) | 1;
+      const int gamma = node + s * dir + min(dir, 0);
+      if (first != gamma) par[gamma] = (node << 1) | 0;
+      if (last != gamma + 1) par[gamma + 1] = (node << 1) | 1;
       want0 = gamma - first + 1 <= leaf;
       want1 = last - gamma <= leaf;
-      rec0 = make_int4(b, first, gamma, (i << 1) | 0);
-      rec1 = make_int4(b, gamma + 1, last, (i << 1) | 1);
-      leaf_children = (int)want0 + (int)want1;
+      rec0 = make_int4(b, first, gamma, (node << 1) | 0);
+      rec1 = make_int4(b, gamma + 1, last, (node << 1) | 1);
+      cnt[node] = (int)want0 + (int)want1;
     }
-    counter[(d.p0 - b) + i] = leaf_children;
+    emit(want0, rec0, leaves + d.p0, leaf_count + b);
+    emit(want1, rec1, leaves + d.p0, leaf_count + b);
+    emit(act && want0 && want1, node, starts + (d.p0 - b), start_count + b);
   }
-  emit(want0, rec0, leaves + d.p0, leaf_count + b);
-  emit(want1, rec1, leaves + d.p0, leaf_count + b);
-  emit(valid && want0 && want1, i, starts + (d.p0 - b), start_count + b);
 }
 
 // ---------------------------------------------------------------------------
@@ -475,26 +501,35 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
 // flight; no arrivals here -- the counters were initialised with the
 // leaf-child counts.
 template <int G>
-__global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
-  int lane = threadIdx.x & 31;
-  int gl = lane & (G - 1);
-  unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
-  int group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
-  int groups = (gridDim.x * blockDim.x) / G;
+__global__ void __launch_bounds__(256, 5) leaf_kernel(RefitArgs a) {
+  constexpr int kPer = 32 / G;  // leaves per warp step
+  const int lane = threadIdx.x & 31;
+  const int gl = lane & (G - 1);
+  const unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
+  // the warp takes kPer consecutive records per step; the loop bound is the
+  // same for the whole warp, so warp-wide votes stay legal
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
   const int b = blockIdx.y;
   const TreeDesc d = a.desc[b];
-  int total = a.leaf_count[b];
+  const int total = a.leaf_count[b];
   const float inf = __int_as_float(0x7f800000);
-  for (int r = group; r < total; r += groups) {
-    int4 rec = a.leaves[d.p0 + r];
-    int cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
-    bool on = gl < c;
+  for (int r0 = warp * kPer; r0 < total; r0 += warps * kPer) {
+    const int r = r0 + lane / G;
+    int cf = 0, c = 0, code = -1;
+    if (r < total) {
+      int4 rec = a.leaves[d.p0 + r];
+      cf = rec.y;
+      c = rec.z - rec.y + 1;
+      code = rec.w;
+    }
+    const bool on = gl < c;
     // the leaf's member offset on level l (lane l loads it; level 0: cf),
     // issued together with the point loads
     int st = cf;
-    if (gl >= 1 && gl < a.levels)
+    if (r < total && gl >= 1 && gl < a.levels)
       st = __ldcg(a.pref + (size_t)(gl - 1) * a.N + d.p0 + cf);
-    int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
+    const int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
     float px = 0.f, py = 0.f, pz = 0.f;
     if (on) {
       const float* p = a.x + 3ll * (d.p0 + id);
@@ -508,47 +543,61 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
 #pragma unroll
     for (int j = 0; j < G; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
     if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
-    int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
-    bool fin = on && finite3(px, py, pz);
-    unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
+    const int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
+    const bool fin = on && finite3(px, py, pz);
+    const unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
     Entry* own = code < 0 ? nullptr : node_entry(a.nodes, d, 0, code >> 1, code & 1);
     int* qo = a.qorder + d.q0;           // level 0 of this tree's query order
     float4* lp = a.lpts + (d.q0 - d.p0);  // level 1 of its member arrays
+    int w[kMaxLevels];
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
+      w[l] = 0;
       if (l >= a.levels) break;
-      bool mem = on && id < level_size(d.n, l);
-      int members = __popc(__ballot_sync(gmask, mem));
-      int start = __shfl_sync(gmask, st, l, G);
+      const bool mem = on && id < level_size(d.n, l);
+      const int members = __popc(__ballot_sync(gmask, mem));
+      const int start = __shfl_sync(gmask, st, l, G);
       if (mem) {
         qo[start + rank] = id;
         if (l) lp[start + rank] = make_float4(px, py, pz, __int_as_float(id));
       }
       // members before this point in leaf order (the leaf's members first)
-      if (on)
-        a.wrank[(size_t)(d.p0 + id) * a.levels + l] = start + min(rank, members);
+      w[l] = start + min(rank, members);
       qo += level_size(d.n, l);
       if (l) lp += level_size(d.n, l);
-      bool f = mem && fin;
+      const bool f = mem && fin;
       Entry t;
       t.lox = t.loy = t.loz = inf;
       t.hix = t.hiy = t.hiz = -inf;
-      if (__ballot_sync(gmask, f)) {
-        t.lox = key_float(__reduce_min_sync(gmask, f ? kx : 0xffffffffu));
-        t.loy = key_float(__reduce_min_sync(gmask, f ? ky : 0xffffffffu));
-        t.loz = key_float(__reduce_min_sync(gmask, f ? kz : 0xffffffffu));
-        t.hix = key_float(__reduce_max_sync(gmask, f ? kx : 0u));
-        t.hiy = key_float(__reduce_max_sync(gmask, f ? ky : 0u));
-        t.hiz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
+      // warp-wide test: both half-warp groups reduce, or neither does
+      if (__ballot_sync(kFull, f)) {
+        const bool any = __ballot_sync(gmask, f) != 0;
+        const float lx = key_float(__reduce_min_sync(gmask, f ? kx : 0xffffffffu));
+        const float ly = key_float(__reduce_min_sync(gmask, f ? ky : 0xffffffffu));
+        const float lz = key_float(__reduce_min_sync(gmask, f ? kz : 0xffffffffu));
+        const float hx = key_float(__reduce_max_sync(gmask, f ? kx : 0u));
+        const float hy = key_float(__reduce_max_sync(gmask, f ? ky : 0u));
+        const float hz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
+        if (any) {
+          t.lox = lx; t.loy = ly; t.loz = lz;
+          t.hix = hx; t.hiy = hy; t.hiz = hz;
+        }
       }
       t.minid = minid;
       t.ref = level_leaf_ref(start, members);
-      if (gl == 0) {
+      if (gl == 0 && r < total) {
         if (own)
           store_entry(own + (size_t)l * (d.n - 1) * 2, t);
         else
           a.root[b * a.levels + l] = t;
       }
+    }
+    if (on) {
+      if (a.levels == kMaxLevels)
+        reinterpret_cast<int4*>(a.wrank)[d.p0 + id] = make_int4(w[0], w[1], w[2], w[3]);
+      else
+        for (int l = 0; l < a.levels; ++l)
+          a.wrank[(size_t)(d.p0 + id) * a.levels + l] = w[l];
     }
   }
 }
