@@ -58,18 +58,37 @@ __global__ void upload_desc(TreeDesc* dst, DescChunk c, unsigned* bounds) {
 
 // Bounds over points whose three coordinates are finite (non-finite points
 // can never qualify: their squared distance is inf or NaN).
+constexpr int kUnroll = 4;  // points per thread and step (bounds, Morton)
+
 __global__ void bounds_kernel(const TreeDesc* desc, const float* x,
                               unsigned* bounds) {
   TreeDesc d = desc[blockIdx.y];
   float lo[3] = {INFINITY, INFINITY, INFINITY};
   float hi[3] = {-INFINITY, -INFINITY, -INFINITY};
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
-       i += gridDim.x * blockDim.x) {
-    const float* p = x + 3ll * (d.p0 + i);
-    float a = p[0], b = p[1], c = p[2];
-    if (finite3(a, b, c)) {
-      lo[0] = fminf(lo[0], a); lo[1] = fminf(lo[1], b); lo[2] = fminf(lo[2], c);
-      hi[0] = fmaxf(hi[0], a); hi[1] = fmaxf(hi[1], b); hi[2] = fmaxf(hi[2], c);
+  const int stride = gridDim.x * blockDim.x;
+  // kUnroll points per thread and step, all loaded before any is used
+  for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < d.n;
+       i0 += kUnroll * stride) {
+    float v[kUnroll][3];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * stride;
+      v[u][0] = v[u][1] = v[u][2] = NAN;
+      if (i < d.n) {
+        const float* p = x + 3ll * (d.p0 + i);
+        v[u][0] = p[0];
+        v[u][1] = p[1];
+        v[u][2] = p[2];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (finite3(v[u][0], v[u][1], v[u][2])) {
+        for (int k = 0; k < 3; ++k) {
+          lo[k] = fminf(lo[k], v[u][k]);
+          hi[k] = fmaxf(hi[k], v[u][k]);
+        }
+      }
     }
   }
   for (int k = 0; k < 3; ++k) {
@@ -131,14 +150,30 @@ __global__ void morton_kernel(const TreeDesc* desc, const float* x,
     ext = fmaxf(ext, h - lo[k]);
   }
   float scale = (ext > 0.f && isfinite(ext)) ? (float)top / ext : 0.f;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.n;
-       i += gridDim.x * blockDim.x) {
-    const float* p = x + 3ll * (d.p0 + i);
-    uint64_t key = (spread3(quantize(p[0], lo[0], scale, top)) << 2) |
-                   (spread3(quantize(p[1], lo[1], scale, top)) << 1) |
-                   spread3(quantize(p[2], lo[2], scale, top));
-    keys[d.p0 + i] = key;
-    vals[d.p0 + i] = i;
+  const int stride = gridDim.x * blockDim.x;
+  for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < d.n;
+       i0 += kUnroll * stride) {
+    float v[kUnroll][3];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * stride;
+      if (i < d.n) {
+        const float* p = x + 3ll * (d.p0 + i);
+        v[u][0] = p[0];
+        v[u][1] = p[1];
+        v[u][2] = p[2];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * stride;
+      if (i < d.n) {
+        keys[d.p0 + i] = (spread3(quantize(v[u][0], lo[0], scale, top)) << 2) |
+                         (spread3(quantize(v[u][1], lo[1], scale, top)) << 1) |
+                         spread3(quantize(v[u][2], lo[2], scale, top));
+        vals[d.p0 + i] = i;
+      }
+    }
   }
 }
 
@@ -874,7 +909,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   if (!e) {
     dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
     bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
-    dim3 gm(std::min(blocks_for(max_n, 256), 1024), B);
+    dim3 gm(std::min(blocks_for(max_n, 256 * kUnroll), 1024), B);
     const int bits = morton_bits(max_n);
     const int passes = (3 * bits + 7) / 8;
     morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, bits, keys, vals);
