@@ -536,35 +536,26 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
 // flight; no arrivals here -- the counters were initialised with the
 // leaf-child counts.
 template <int G>
-__global__ void __launch_bounds__(256, 5) leaf_kernel(RefitArgs a) {
-  constexpr int kPer = 32 / G;  // leaves per warp step
-  const int lane = threadIdx.x & 31;
-  const int gl = lane & (G - 1);
-  const unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
-  // the warp takes kPer consecutive records per step; the loop bound is the
-  // same for the whole warp, so warp-wide votes stay legal
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int warps = (gridDim.x * blockDim.x) >> 5;
+__global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
+  int lane = threadIdx.x & 31;
+  int gl = lane & (G - 1);
+  unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
+  int group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
+  int groups = (gridDim.x * blockDim.x) / G;
   const int b = blockIdx.y;
   const TreeDesc d = a.desc[b];
-  const int total = a.leaf_count[b];
+  int total = a.leaf_count[b];
   const float inf = __int_as_float(0x7f800000);
-  for (int r0 = warp * kPer; r0 < total; r0 += warps * kPer) {
-    const int r = r0 + lane / G;
-    int cf = 0, c = 0, code = -1;
-    if (r < total) {
-      int4 rec = a.leaves[d.p0 + r];
-      cf = rec.y;
-      c = rec.z - rec.y + 1;
-      code = rec.w;
-    }
-    const bool on = gl < c;
+  for (int r = group; r < total; r += groups) {
+    int4 rec = a.leaves[d.p0 + r];
+    int cf = rec.y, c = rec.z - rec.y + 1, code = rec.w;
+    bool on = gl < c;
     // the leaf's member offset on level l (lane l loads it; level 0: cf),
     // issued together with the point loads
     int st = cf;
-    if (r < total && gl >= 1 && gl < a.levels)
+    if (gl >= 1 && gl < a.levels)
       st = __ldcg(a.pref + (size_t)(gl - 1) * a.N + d.p0 + cf);
-    const int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
+    int id = on ? a.perm[d.p0 + cf + gl] : INT_MAX;
     float px = 0.f, py = 0.f, pz = 0.f;
     if (on) {
       const float* p = a.x + 3ll * (d.p0 + id);
@@ -578,61 +569,47 @@ __global__ void __launch_bounds__(256, 5) leaf_kernel(RefitArgs a) {
 #pragma unroll
     for (int j = 0; j < G; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
     if (on) a.pts[d.p0 + cf + rank] = make_float4(px, py, pz, __int_as_float(id));
-    const int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
-    const bool fin = on && finite3(px, py, pz);
-    const unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
+    int minid = (int)__reduce_min_sync(gmask, (unsigned)id);
+    bool fin = on && finite3(px, py, pz);
+    unsigned kx = float_key(px), ky = float_key(py), kz = float_key(pz);
     Entry* own = code < 0 ? nullptr : node_entry(a.nodes, d, 0, code >> 1, code & 1);
     int* qo = a.qorder + d.q0;           // level 0 of this tree's query order
     float4* lp = a.lpts + (d.q0 - d.p0);  // level 1 of its member arrays
-    int w[kMaxLevels];
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
-      w[l] = 0;
       if (l >= a.levels) break;
-      const bool mem = on && id < level_size(d.n, l);
-      const int members = __popc(__ballot_sync(gmask, mem));
-      const int start = __shfl_sync(gmask, st, l, G);
+      bool mem = on && id < level_size(d.n, l);
+      int members = __popc(__ballot_sync(gmask, mem));
+      int start = __shfl_sync(gmask, st, l, G);
       if (mem) {
         qo[start + rank] = id;
         if (l) lp[start + rank] = make_float4(px, py, pz, __int_as_float(id));
       }
       // members before this point in leaf order (the leaf's members first)
-      w[l] = start + min(rank, members);
+      if (on)
+        a.wrank[(size_t)(d.p0 + id) * a.levels + l] = start + min(rank, members);
       qo += level_size(d.n, l);
       if (l) lp += level_size(d.n, l);
-      const bool f = mem && fin;
+      bool f = mem && fin;
       Entry t;
       t.lox = t.loy = t.loz = inf;
       t.hix = t.hiy = t.hiz = -inf;
-      // warp-wide test: both half-warp groups reduce, or neither does
-      if (__ballot_sync(kFull, f)) {
-        const bool any = __ballot_sync(gmask, f) != 0;
-        const float lx = key_float(__reduce_min_sync(gmask, f ? kx : 0xffffffffu));
-        const float ly = key_float(__reduce_min_sync(gmask, f ? ky : 0xffffffffu));
-        const float lz = key_float(__reduce_min_sync(gmask, f ? kz : 0xffffffffu));
-        const float hx = key_float(__reduce_max_sync(gmask, f ? kx : 0u));
-        const float hy = key_float(__reduce_max_sync(gmask, f ? ky : 0u));
-        const float hz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
-        if (any) {
-          t.lox = lx; t.loy = ly; t.loz = lz;
-          t.hix = hx; t.hiy = hy; t.hiz = hz;
-        }
+      if (__ballot_sync(gmask, f)) {
+        t.lox = key_float(__reduce_min_sync(gmask, f ? kx : 0xffffffffu));
+        t.loy = key_float(__reduce_min_sync(gmask, f ? ky : 0xffffffffu));
+        t.loz = key_float(__reduce_min_sync(gmask, f ? kz : 0xffffffffu));
+        t.hix = key_float(__reduce_max_sync(gmask, f ? kx : 0u));
+        t.hiy = key_float(__reduce_max_sync(gmask, f ? ky : 0u));
+        t.hiz = key_float(__reduce_max_sync(gmask, f ? kz : 0u));
       }
       t.minid = minid;
       t.ref = level_leaf_ref(start, members);
-      if (gl == 0 && r < total) {
+      if (gl == 0) {
         if (own)
           store_entry(own + (size_t)l * (d.n - 1) * 2, t);
         else
           a.root[b * a.levels + l] = t;
       }
-    }
-    if (on) {
-      if (a.levels == kMaxLevels)
-        reinterpret_cast<int4*>(a.wrank)[d.p0 + id] = make_int4(w[0], w[1], w[2], w[3]);
-      else
-        for (int l = 0; l < a.levels; ++l)
-          a.wrank[(size_t)(d.p0 + id) * a.levels + l] = w[l];
     }
   }
 }
