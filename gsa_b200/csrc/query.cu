@@ -25,6 +25,7 @@
 // A walk's stack overflow (impossible for STACK >= 97 on a Karras tree of
 // 64-bit keys) falls back to the exact original-order scan and is counted,
 // as in the reference.
+#include <atomic>
 #include <algorithm>
 #include "forest.cuh"
 
@@ -1090,15 +1091,18 @@ QArgs make_args(const Forest& f, const QuerySet& qs) {
 namespace {
 
 int sm_count() {
-  static int cached[64] = {0};
+  // per device, filled on first use; host threads may race to fill an entry
+  // and all store the same value
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    int n = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (!n) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 // Queries per warp of a frontier launch.  A packet of 32 queries shares one
