@@ -14,6 +14,8 @@ import math
 
 import torch
 
+# _stream: the current raw stream, also used as runtime._stream by the
+# forest and hierarchy modules
 from ._library import current_stream, load, stream as _stream
 
 lib = load("gsa_bvh")
