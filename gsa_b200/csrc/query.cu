@@ -7,13 +7,15 @@
 // none); the three smallest finite squared distances in (d2, id) order,
 // missing entries (inf, 0).  Results do not depend on traversal order.
 //
-// Execution model (B200): one warp serves 32 queries at once.  Queries are
+// Execution model (B200): one warp serves a packet of 32 queries at once (16
+// or 8 when a launch would not fill the SMs, see packet_width).  Queries are
 // visited in the tree's leaf order (for a query array that is a prefix of the
-// support, neighbouring lanes hold neighbouring points), so the 32 lanes need
+// support, neighbouring lanes hold neighbouring points), so the lanes need
 // nearly the same part of the tree.  Three forms:
 //   * packet-frontier kernels (default for the tree): the tree is culled once
-//     against the box of the warp's queries, 32 child entries per step, and
-//     the surviving leaves are processed as dense (query x point) pairs;
+//     against the box of the warp's queries, starting from the level's cut of
+//     up to 32 entries, 32 child entries per step, and the surviving leaves
+//     are processed as dense (query x point) pairs;
 //   * per-query packet walks (walk_ordered, walk_knn3): one query per lane,
 //     a node entered when any lane needs it, node entries and leaf points
 //     loaded once per warp as 16-byte broadcast loads; the radius walk visits
