@@ -53,3 +53,17 @@ def current_stream():
 def stream():
     """Raw handle of the current CUDA stream."""
     return current_stream()[1]
+
+
+def launch_counter():
+    """Kernel launches the native libraries have enqueued in this process
+    (both libraries' counters added; a replayed CUDA graph adds nothing)."""
+    total = 0
+    for name in ("gsa_bvh", "reference_queries"):
+        lib = load(name)
+        v = ctypes.c_ulonglong()
+        lib.launch_counter.argtypes = [ctypes.POINTER(ctypes.c_ulonglong)]
+        lib.launch_counter.restype = ctypes.c_int
+        lib.launch_counter(ctypes.byref(v))
+        total += v.value
+    return total

@@ -801,6 +801,158 @@ int leaf_grid(bool half_warps, long long max_points) {
 
 }  // namespace
 
+// Build temporaries.  A forest made by build_forest frees them when the
+// build is enqueued; rebuild_forest keeps them with the forest, so that later
+// rebuilds of the same shape allocate nothing (and can be captured in a CUDA
+// graph).
+struct BuildScratch {
+  uint64_t* keys = nullptr;
+  uint64_t* keys2 = nullptr;
+  int* vals = nullptr;
+  int* vals2 = nullptr;
+  int* hist = nullptr;
+  unsigned* bounds = nullptr;
+  int4* leaves = nullptr;  // leaf records; at most one per point
+  int* parent = nullptr;
+  int* counter = nullptr;  // arrival counters + leaf-record and climb-start counts
+  int* pref = nullptr;
+  int* starts = nullptr;
+};
+
+namespace {
+
+int max_tiles_of(const Forest* f) { return blocks_for(f->max_n, kSortTile); }
+
+long long inner_nodes(const Forest* f) { return std::max<long long>(1, (long long)f->N - f->B); }
+
+cudaError_t alloc_scratch(const Forest* f, BuildScratch* sc, cudaStream_t s) {
+  const long long N = f->N, B = f->B, inner = inner_nodes(f);
+  cudaError_t e = cudaSuccess;
+  auto alloc = [&](void** p, size_t bytes) {
+    if (!e) e = pool_alloc(p, bytes, s);
+  };
+  alloc((void**)&sc->pref, sizeof(int) * std::max<long long>(1, (f->levels - 1) * N));
+  alloc((void**)&sc->starts, sizeof(int) * inner);
+  alloc((void**)&sc->vals, sizeof(int) * N);
+  alloc((void**)&sc->keys, sizeof(uint64_t) * N);
+  alloc((void**)&sc->keys2, sizeof(uint64_t) * N);
+  alloc((void**)&sc->vals2, sizeof(int) * N);
+  alloc((void**)&sc->hist, sizeof(int) * 256ll * B * max_tiles_of(f));
+  alloc((void**)&sc->bounds, sizeof(unsigned) * 6 * B);
+  alloc((void**)&sc->leaves, sizeof(int4) * N);
+  alloc((void**)&sc->parent, sizeof(int) * inner);
+  alloc((void**)&sc->counter, sizeof(int) * (inner + 2 * B));
+  return e;
+}
+
+cudaError_t free_scratch(BuildScratch* sc, cudaStream_t s) {
+  cudaError_t e = cudaSuccess;
+  void* bufs[] = {sc->keys,    sc->keys2,  sc->vals,   sc->vals2,
+                  sc->hist,    sc->bounds, sc->leaves, sc->parent,
+                  sc->counter, sc->pref,   sc->starts};
+  for (void* p : bufs) {
+    cudaError_t fe = pool_free(p, s);
+    if (!e) e = fe;
+  }
+  *sc = BuildScratch();
+  return e;
+}
+
+// Enqueues every build kernel of `f` over points `x` (the layout in f->hdesc)
+// using the temporaries in `sc`.  Allocates nothing.
+cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
+                          cudaStream_t s) {
+  const int B = f->B, max_n = f->max_n;
+  const long long N = f->N, inner = inner_nodes(f);
+  const int max_tiles = max_tiles_of(f);
+  uint64_t *keys = sc.keys, *keys2 = sc.keys2;
+  int *vals = sc.vals, *vals2 = sc.vals2, *hist = sc.hist;
+  int* counter = sc.counter;
+  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 2 * B), s);
+  if (e) return e;
+  int* leaf_count = counter + inner;
+  int* start_count = leaf_count + B;
+
+  for (int b0 = 0; b0 < B; b0 += 256) {
+    DescChunk c;
+    c.first = b0;
+    c.count = std::min(256, B - b0);
+    for (int i = 0; i < c.count; ++i) c.d[i] = f->hdesc[b0 + i];
+    upload_desc<<<1, 256, 0, s>>>(f->desc, c, sc.bounds);
+  }
+  int launches = (B + 255) / 256;
+  dim3 gs(max_tiles, B);
+  dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
+  {
+    dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
+    bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, sc.bounds);
+    dim3 gm(std::min(blocks_for(max_n, 256 * kUnroll), 1024), B);
+    const int bits = morton_bits(max_n);
+    const int passes = (3 * bits + 7) / 8;
+    morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, sc.bounds, bits, keys, vals);
+    for (int pass = 0; pass < passes; ++pass) {
+      int shift = 8 * pass;
+      sort_upsweep<<<gs, kSortThreads, 0, s>>>(f->desc, keys, shift, hist,
+                                               max_tiles);
+      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, 256, max_tiles,
+                                          kSortTile);
+      sort_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, keys, vals, keys2,
+                                               vals2, hist, shift, max_tiles);
+      std::swap(keys, keys2);
+      std::swap(vals, vals2);
+    }
+    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, sc.parent, counter,
+                                     f->leaf, sc.leaves, leaf_count, sc.starts,
+                                     start_count);
+    launches += 2 + 3 * passes + 1;
+    if (f->levels > 1) {
+      // members of each prefix level before every sorted position
+      member_count<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
+                                               max_tiles);
+      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels - 1,
+                                          max_tiles, kSortTile);
+      member_prefix<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
+                                                max_tiles, sc.pref, (int)N);
+      launches += 3;
+    }
+  }
+  RefitArgs ra;
+  ra.desc = f->desc;
+  ra.x = x;
+  ra.perm = vals;
+  ra.parent = sc.parent;
+  ra.counter = counter;
+  ra.pref = sc.pref;
+  ra.leaves = sc.leaves;
+  ra.leaf_count = leaf_count;
+  ra.starts = sc.starts;
+  ra.start_count = start_count;
+  ra.pts = f->pts;
+  ra.lpts = f->lpts;
+  ra.qorder = f->qorder;
+  ra.wrank = f->wrank;
+  ra.nodes = f->nodes;
+  ra.root = f->root;
+  ra.levels = f->levels;
+  ra.leaf = f->leaf;
+  ra.N = (int)N;
+  // lane groups of each tree loop over its leaf records (their count is
+  // only known on the device)
+  dim3 gl(leaf_grid(f->leaf <= 16, max_n), B);
+  if (f->leaf <= 16)
+    leaf_kernel<16><<<gl, 256, 0, s>>>(ra);
+  else
+    leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
+  climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
+  cut_kernel<<<dim3(f->levels, B), 32, 0, s>>>(f->desc, f->nodes, f->root,
+                                               f->levels, f->cut);
+  launches += 3;
+  count_launches(launches);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
                          int leaf, cudaStream_t s, Forest** out) {
   *out = nullptr;
@@ -850,118 +1002,34 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->lpts, sizeof(float4) * std::max<long long>(1, q_total - N));
   alloc((void**)&f->wrank, sizeof(int) * N * f->levels);
   alloc((void**)&f->cut, sizeof(int) * kCutStride * B * f->levels);
-  int max_tiles = blocks_for(max_n, kSortTile);
-  uint64_t *keys = nullptr, *keys2 = nullptr;
-  int *vals = nullptr, *vals2 = nullptr, *hist = nullptr, *parent = nullptr,
-      *counter = nullptr, *pref = nullptr, *starts = nullptr;
-  unsigned* bounds = nullptr;
-  int4* leaves = nullptr;  // leaf records; at most one per point
-  long long inner = std::max<long long>(1, N - B);
-  alloc((void**)&pref, sizeof(int) * std::max<long long>(1, (f->levels - 1) * N));
-  alloc((void**)&starts, sizeof(int) * inner);
-  alloc((void**)&vals, sizeof(int) * N);
-  alloc((void**)&keys, sizeof(uint64_t) * N);
-  alloc((void**)&keys2, sizeof(uint64_t) * N);
-  alloc((void**)&vals2, sizeof(int) * N);
-  alloc((void**)&hist, sizeof(int) * 256ll * B * max_tiles);
-  alloc((void**)&bounds, sizeof(unsigned) * 6 * B);
-  alloc((void**)&leaves, sizeof(int4) * N);
-  alloc((void**)&parent, sizeof(int) * inner);
-  // arrival counters + one leaf-record and one climb-start count per tree
-  alloc((void**)&counter, sizeof(int) * (inner + 2 * B));
-  if (!e) e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 2 * B), s);
-  int* leaf_count = counter + inner;
-  int* start_count = leaf_count + B;
-
-  for (int b0 = 0; !e && b0 < B; b0 += 256) {
-    DescChunk c;
-    c.first = b0;
-    c.count = std::min(256, B - b0);
-    for (int i = 0; i < c.count; ++i) c.d[i] = f->hdesc[b0 + i];
-    upload_desc<<<1, 256, 0, s>>>(f->desc, c, bounds);
-  }
-  int launches = (B + 255) / 256;
-  dim3 gs(max_tiles, B);
-  dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-  if (!e) {
-    dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
-    bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, bounds);
-    dim3 gm(std::min(blocks_for(max_n, 256 * kUnroll), 1024), B);
-    const int bits = morton_bits(max_n);
-    const int passes = (3 * bits + 7) / 8;
-    morton_kernel<<<gm, 256, 0, s>>>(f->desc, x, bounds, bits, keys, vals);
-    for (int pass = 0; pass < passes; ++pass) {
-      int shift = 8 * pass;
-      sort_upsweep<<<gs, kSortThreads, 0, s>>>(f->desc, keys, shift, hist,
-                                               max_tiles);
-      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, 256, max_tiles,
-                                          kSortTile);
-      sort_scatter<<<gs, kSortThreads, 0, s>>>(f->desc, keys, vals, keys2,
-                                               vals2, hist, shift, max_tiles);
-      std::swap(keys, keys2);
-      std::swap(vals, vals2);
-    }
-    karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, parent, counter, f->leaf,
-                                     leaves, leaf_count, starts, start_count);
-    launches += 2 + 3 * passes + 1;
-    if (f->levels > 1) {
-      // members of each prefix level before every sorted position
-      member_count<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
-                                               max_tiles);
-      seg_scan<<<B, kScanThreads, 0, s>>>(f->desc, hist, f->levels - 1,
-                                          max_tiles, kSortTile);
-      member_prefix<<<gs, kSortThreads, 0, s>>>(f->desc, vals, f->levels, hist,
-                                                max_tiles, pref, (int)N);
-      launches += 3;
-    }
-  }
-  if (!e) {
-    RefitArgs ra;
-    ra.desc = f->desc;
-    ra.x = x;
-    ra.perm = vals;
-    ra.parent = parent;
-    ra.counter = counter;
-    ra.pref = pref;
-    ra.leaves = leaves;
-    ra.leaf_count = leaf_count;
-    ra.starts = starts;
-    ra.start_count = start_count;
-    ra.pts = f->pts;
-    ra.lpts = f->lpts;
-    ra.qorder = f->qorder;
-    ra.wrank = f->wrank;
-    ra.nodes = f->nodes;
-    ra.root = f->root;
-    ra.levels = f->levels;
-    ra.leaf = f->leaf;
-    ra.N = (int)N;
-    // lane groups of each tree loop over its leaf records (their count is
-    // only known on the device)
-    dim3 gl(leaf_grid(f->leaf <= 16, max_n), B);
-    if (f->leaf <= 16)
-      leaf_kernel<16><<<gl, 256, 0, s>>>(ra);
-    else
-      leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
-    climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
-    cut_kernel<<<dim3(f->levels, B), 32, 0, s>>>(f->desc, f->nodes, f->root,
-                                                 f->levels, f->cut);
-    launches += 3;
-    count_launches(launches);
-    e = cudaGetLastError();
-  }
-  void* scratch[] = {keys, keys2, vals, vals2, hist,   bounds,
-                     leaves, parent, counter, pref, starts};
-  for (void* p : scratch) {
-    cudaError_t fe = pool_free(p, s);
-    if (!e) e = fe;
-  }
+  BuildScratch sc;
+  if (!e) e = alloc_scratch(f, &sc, s);
+  if (!e) e = enqueue_build(f, x, sc, s);
+  cudaError_t fe = free_scratch(&sc, s);
+  if (!e) e = fe;
   if (e) {
     free_forest(f, s);
     return e;
   }
   *out = f;
   return cudaSuccess;
+}
+
+cudaError_t rebuild_forest(Forest* f, const float* x, cudaStream_t s) {
+  if (!f || !x) return cudaErrorInvalidValue;
+  if (!f->scratch) {
+    BuildScratch* sc = new (std::nothrow) BuildScratch();
+    if (!sc) return cudaErrorMemoryAllocation;
+    cudaError_t e = alloc_scratch(f, sc, s);
+    if (e) {
+      free_scratch(sc, s);
+      delete sc;
+      return e;
+    }
+    f->scratch = sc;
+  }
+  f->x = x;
+  return enqueue_build(f, x, *f->scratch, s);
 }
 
 cudaError_t free_forest(Forest* f, cudaStream_t s) {
@@ -972,6 +1040,11 @@ cudaError_t free_forest(Forest* f, cudaStream_t s) {
   for (void* p : bufs) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;
+  }
+  if (f->scratch) {
+    cudaError_t fe = free_scratch(f->scratch, s);
+    if (!e) e = fe;
+    delete f->scratch;
   }
   delete f;
   return e;

@@ -7,6 +7,8 @@
 
 namespace gsa {
 
+struct BuildScratch;
+
 struct Forest {
   int B = 0;        // trees
   int N = 0;        // total support points
@@ -24,6 +26,7 @@ struct Forest {
   int* wrank = nullptr;
   int* cut = nullptr;
   const float* x = nullptr;  // borrowed
+  BuildScratch* scratch = nullptr;  // kept build temporaries (rebuild_forest)
 
   ForestView view() const {
     ForestView v;
@@ -47,6 +50,11 @@ struct Forest {
 cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
                          int leaf, cudaStream_t s, Forest** out);
 cudaError_t free_forest(Forest* f, cudaStream_t s);
+// Rebuilds `f` in place from points `x` with the same layout (scene sizes,
+// levels, leaf size).  The first call allocates the build temporaries and
+// keeps them with the forest; later calls allocate nothing, so a rebuild can
+// be captured in a CUDA graph.  Stream-ordered; no host synchronisation.
+cudaError_t rebuild_forest(Forest* f, const float* x, cudaStream_t s);
 
 // Queries of one launch.  Single tree: qseg == qseg_host == qstart == null,
 // `nq` queries at q[0..nq).  Forest: tree b answers qseg[b+1]-qseg[b] queries

@@ -105,6 +105,12 @@ GSA_API int build_bvh_batch(const float* x, const int* seg, int b, int prefix,
   return 0;
 }
 
+GSA_API int rebuild_bvh_batch(void* handle, const float* x, void* stream) {
+  Forest* f = (Forest*)handle;
+  if (!f || !x) return -1;
+  return as_code(rebuild_forest(f, x, (cudaStream_t)stream));
+}
+
 namespace {
 // Every tree with queries must have a support prefix of at least min_m
 // points that its level's bounds cover.

@@ -20,6 +20,13 @@ def world():
     return 0, 1
 
 
+def shard_seeds(rank, world_size, total):
+    """Scenes of a rank when ``total`` scenes are split over ``world_size``
+    GPUs: scene i goes to rank i mod world_size (strong scaling: the job is
+    fixed, each rank gets about total / world_size scenes)."""
+    return list(range(rank, total, world_size))
+
+
 def rank_seeds(rank, scenes_per_rank):
     """Scene seeds of a rank: rank * scenes_per_rank + i (weak scaling)."""
     return [rank * scenes_per_rank + i for i in range(scenes_per_rank)]

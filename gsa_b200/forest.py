@@ -30,6 +30,8 @@ lib.query_ball_bvh_batch.argtypes = [_ptr, _ptr, _ptr, _ptr, _ptr, _int, _int, c
 lib.query_ball_bvh_batch.restype = _int
 lib.query_bvh_batch.argtypes = [_ptr, _ptr, _ptr, _ptr, _ptr, _int, _int, _ptr, _ptr, _ptr, _ptr]
 lib.query_bvh_batch.restype = _int
+lib.rebuild_bvh_batch.argtypes = [_ptr, _ptr, _ptr]
+lib.rebuild_bvh_batch.restype = _int
 
 _INT_CACHE = {}
 
@@ -158,6 +160,22 @@ class Forest:
         if any(count > n for n in self.sizes):
             raise ValueError("prefix longer than a scene")
         return self._query(self.x, self._starts.data_ptr(), count, level, d, idx, m)
+
+    def rebuild(self, x):
+        """Rebuild every tree in place from ``x``, new coordinates with the
+        shape the forest was created with (``x`` is borrowed from then on).
+        The first call keeps the build temporaries with the forest; later
+        calls allocate nothing, so a rebuild and the queries after it can be
+        captured in a CUDA graph."""
+        if not (
+            self.ptr
+            and er._is_points(x)
+            and len(x) == len(self.x)
+            and x.device == self.x.device
+        ):
+            raise ValueError("rebuild requires contiguous CUDA FP32 points shaped like the forest's")
+        self.x = x
+        er.check(lib.rebuild_bvh_batch(self.ptr, x.data_ptr(), er._stream()))
 
     def close(self):
         if self.ptr:

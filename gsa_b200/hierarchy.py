@@ -127,6 +127,11 @@ class Batch:
             streams = self._streams[device] = [torch.cuda.Stream(device) for _ in range(8)]
         return streams
 
+    def _check_input(self, X):
+        if not (X.is_cuda and X.is_contiguous() and X.dtype == torch.float32 and X.ndim == 3
+                and X.shape[2] == 3 and X.shape[1] == self.sizes[0]):
+            raise ValueError("Batch needs contiguous CUDA FP32 (B, sizes[0], 3)")
+
     def run(self, X, out=None, timer=None, concurrent=True):
         """X: CUDA float32 (B, N, 3), N == sizes[0], each scene FPS-ordered.
 
@@ -136,16 +141,33 @@ class Batch:
         stages overlap the large ones; the caller's stream waits for all of
         them.  ``timer.span(name)``, if given, brackets each stage on the
         stream it runs on (build, ball<s>, reuse<s>, nn<s>)."""
+        self._check_input(X)
         B, N = X.shape[0], X.shape[1]
-        if not (X.is_cuda and X.is_contiguous() and X.dtype == torch.float32 and N == self.sizes[0]):
-            raise ValueError("Batch.run needs contiguous CUDA FP32 (B, sizes[0], 3)")
         out = out if out is not None else self.allocate(B, X.device)
+        timer = timer or _NoTimer()
+        with timer.span("build"):
+            out["snapshot"].copy_(X)  # retained snapshot of every support, as the session keeps
+            forest = Forest(X.view(-1, 3), [i * N for i in range(B + 1)], prefix=True, leaf=self.leaf)
+        self._stages(X, out, forest, timer, concurrent)
+        forest.close()
+        return out
+
+    def capture(self, X, out=None):
+        """The whole step over fixed buffers ``X`` and ``out`` as one CUDA
+        graph (``CapturedStep``): snapshot copy, in-place forest rebuild and
+        all eight query stages on their streams.  Replaying it answers the
+        hierarchy for whatever coordinates ``X`` holds at replay time, with
+        one host call per step instead of ~40 library calls."""
+        self._check_input(X)
+        out = out if out is not None else self.allocate(X.shape[0], X.device)
+        return CapturedStep(self, X, out)
+
+    def _stages(self, X, out, forest, timer=None, concurrent=True):
+        """Enqueue the eight query stages on ``forest`` (built over X)."""
+        B, N = X.shape[0], X.shape[1]
         timer = timer or _NoTimer()
         main = torch.cuda.current_stream()
         snap = out["snapshot"]
-        with timer.span("build"):
-            snap.copy_(X)  # retained snapshot of every support, as the session keeps
-            forest = Forest(X.view(-1, 3), [i * N for i in range(B + 1)], prefix=True, leaf=self.leaf)
 
         def radius_stage(s):
             n_s, n_q = self.sizes[s], self.sizes[s + 1]
@@ -191,8 +213,52 @@ class Batch:
         else:
             for job in stages:
                 job()
-        forest.close()
-        return out
+
+
+class CapturedStep:
+    """One hierarchy step over fixed input and output buffers, captured as a
+    CUDA graph.
+
+    The forest is created once and rebuilt in place inside the graph (its
+    build temporaries stay allocated with it), so a replay allocates nothing
+    and enqueues the snapshot copy, every build kernel, the eight query
+    stages on their side streams and the reuse checks with one
+    ``cudaGraphLaunch``.  ``launches`` is the number of library kernel
+    launches one replay runs (counted while capturing).  Outputs equal
+    ``Batch.run`` on the same coordinates."""
+
+    def __init__(self, batch, X, out):
+        from ._library import launch_counter
+
+        B, N = X.shape[0], X.shape[1]
+        self.X, self.out = X, out
+        flat = X.view(-1, 3)
+        self.forest = Forest(flat, [i * N for i in range(B + 1)], prefix=True, leaf=batch.leaf)
+        # eager pass: keeps the build temporaries, fills the host-side caches
+        out["snapshot"].copy_(X)
+        self.forest.rebuild(flat)
+        batch._stages(X, out, self.forest)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        before = launch_counter()
+        with torch.cuda.graph(self.graph):
+            out["snapshot"].copy_(X)
+            self.forest.rebuild(flat)
+            batch._stages(X, out, self.forest)
+        self.launches = launch_counter() - before
+        torch.cuda.synchronize()
+
+    def replay(self):
+        """Enqueue one step on the current stream; returns the outputs."""
+        self.graph.replay()
+        return self.out
+
+    def close(self):
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+            self.forest.close()
 
 
 class _NoTimer:

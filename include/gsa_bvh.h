@@ -80,6 +80,17 @@ int pool_reset_peak(void);
 int build_bvh_batch(const float* x, const int* seg, int b, int prefix,
                     int leaf, void** out, void* stream);
 
+/* Rebuilds a forest (from build_bvh_batch or build_bvh) in place from points
+ * x laid out as at its creation (same scene sizes; x may be a new address,
+ * and is borrowed like build_bvh's).  The first call on a forest allocates
+ * the build temporaries from the library pool and keeps them until free_bvh;
+ * every later call enqueues the build kernels only, so a rebuild followed by
+ * queries can be captured in a CUDA graph and replayed for new coordinate
+ * values.  Returns 0 or a cudaError_t; -1 for a null handle or x.  No
+ * counterpart in the reference, which builds a new tree per call
+ * (csrc/gsa_bvh.cu:217). */
+int rebuild_bvh_batch(void* h, const float* x, void* stream);
+
 /* Radius query on every tree of a forest in one launch.  Tree i answers
  * qseg[i+1]-qseg[i] queries read from rows q[qstart[i]..) (qstart null: from
  * row qseg[i]) and writes output rows qseg[i].. of out (ns ints per row).

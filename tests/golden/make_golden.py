@@ -2,7 +2,7 @@
 """Extract the reference's committed query-session golden records.
 
 Reads ``data/query_session/correctness.json`` of the GSA reference checkout
-(default ``/root/reference``) and writes ``query_session_correctness.json``
+(the argument, else the ``GSA_REFERENCE`` environment variable) and writes ``query_session_correctness.json``
 beside this script: for each of the 94 calls of the reference test
 ``tests/check_queries.py`` its op, label, sizes, radius, K, the SHA-256 of
 the int32 output rows (radius calls) and the session statistics after the
@@ -13,10 +13,16 @@ Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
 """
 
 import json
+import os
 import sys
 from pathlib import Path
 
-root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) > 1:
+    root = Path(sys.argv[1])
+elif os.environ.get("GSA_REFERENCE"):
+    root = Path(os.environ["GSA_REFERENCE"])
+else:
+    sys.exit("usage: make_golden.py REFERENCE_ROOT (or set GSA_REFERENCE)")
 src = json.loads((root / "data/query_session/correctness.json").read_text())
 keep = ("op", "label", "n", "q", "r", "k", "ids_sha256", "stats")
 records = [{k: r[k] for k in keep if k in r} for r in src["records"]]

@@ -1,7 +1,8 @@
 # SPDX-License-Identifier: Apache-2.0
 """CPU: the multi-rank path with two gloo ranks.
 
-Each rank answers the radius + 3NN hierarchy of its own scenes with the CPU
+Five scenes are split over two ranks (scene i to rank i mod 2); each rank
+answers the radius + 3NN hierarchy of its own scenes with the CPU
 oracle standing in for the GPU engine (the host logic is what is tested:
 scene sharding, max-over-ranks timing, the final gather of row counts and
 checksums), and every rank must see the same gathered table.
@@ -31,7 +32,7 @@ def _worker(rank, world, port, q):
         from oracle import numpy_oracle as orc
 
         assert gd.world() == (rank, world)
-        seeds = gd.rank_seeds(rank, 2)
+        seeds = gd.shard_seeds(rank, world, 5)
         rows, checksum = 0, 0
         sizes, radii = (400, 100, 25, 6, 1), (0.3, 0.5, 0.9, 1.5)
         for s in seeds:
@@ -60,7 +61,7 @@ def test_two_gloo_ranks_shard_and_gather():
         assert p.exitcode == 0
     results.sort()
     (r0, seeds0, slow0, table0), (r1, seeds1, slow1, table1) = results
-    assert seeds0 == [0, 1] and seeds1 == [2, 3]
+    assert seeds0 == [0, 2, 4] and seeds1 == [1, 3]
     assert slow0 == slow1 == 11.0
     assert table0 == table1 and len(table0) == 2
     assert table0[0] != table0[1]  # different scenes, different checksums
@@ -72,6 +73,9 @@ def test_single_process_defaults():
 
     assert gd.world() == (0, 1)
     assert gd.rank_seeds(3, 4) == [12, 13, 14, 15]
+    assert gd.shard_seeds(0, 1, 3) == [0, 1, 2]
+    assert gd.shard_seeds(3, 8, 64) == list(range(3, 64, 8))
+    assert sorted(s for r in range(8) for s in gd.shard_seeds(r, 8, 64)) == list(range(64))
     assert gd.max_over_ranks(2.5) == 2.5
     assert gd.gather_counts(7, 9) == [(7, 9)]
     out = {"ball0": torch.tensor([[1, 2]]), "nnd0": torch.tensor([[0.5]]), "nni0": torch.tensor([[3]])}

@@ -1,0 +1,257 @@
+# SPDX-License-Identifier: Apache-2.0
+"""GPU: every output row equals the reference's own GPU path, at full size.
+
+The checker is the unmodified reference package (qmkkk/GSA ``gsa/``) with its
+``csrc/gsa_bvh.cu`` (cuBQL build, prefix refit, ``radius_ordered``,
+``query3``) and ``csrc/reference_queries.cu`` (``ball``, ``nn3``) compiled
+from source for sm_100a (``oracle/reference_gpu.py``, installed by
+``make -C oracle install``).  Each test runs the same call sequence through
+``gsa.QuerySession`` (``gsa/session.py:83-151``) and through this
+repository's engine, then requires every row -- computed radius rows, reuse
+rows, 3NN squared distances and IDs -- and the session statistics to be
+identical.  Workloads:
+
+* the 94-call sequence of the reference's ``tests/check_queries.py``;
+* the 64 room scenes of the benchmark (24,000 FPS-ordered points each,
+  seeds 0..63), batched engine and its captured CUDA-graph step against the
+  reference session per scene;
+* the 1,000,000-point room (20 x 20 x 3 m), session and batched engine, with
+  the generator output and the FPS order pinned by SHA-256;
+* the 200,000-point clustered stress scene (all 50,000 radius rows, all
+  200,000 3NN rows, the exact-r anchors, a 1-ulp support change);
+* the fixed-graph adapter, ``prefix`` and ``scale`` policies at threshold 32
+  and 1024, against the reference's ``gsa.fixed_graph.forward``.
+
+The NumPy oracle checks samples of the same outputs as a second witness.
+"""
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import numpy_oracle as orc
+from oracle import reference_gpu
+
+pytestmark = pytest.mark.gpu
+
+LARGE = json.loads((Path(__file__).parent / "golden" / "large_room.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def gsa():
+    why = reference_gpu.available()
+    if why:
+        pytest.skip(why)
+    return reference_gpu.load()
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def _session_rows(make_session, P, sizes, radii):
+    from gsa_b200 import hierarchy as hz
+
+    with make_session() as s:
+        out = hz.run_session(s, P, sizes, radii)
+        torch.cuda.synchronize()
+        stats = dict(s.stats)
+    return out, stats
+
+
+def _assert_rows_equal(got, want, where):
+    for key, t in want.items():
+        assert torch.equal(got[key], t), (where, key)
+
+
+def test_check_queries_sequence_equals_reference_session(gsa):
+    from gsa_b200 import QuerySession
+    from tests import sequence
+
+    ours = sequence.run(lambda t: QuerySession(threshold=t), "cuda")
+    ref = sequence.run(lambda t: gsa.QuerySession(threshold=t), "cuda")
+    assert len(ours) == len(ref) == 94
+    for a, b in zip(ours, ref):
+        assert a["stats"] == b["stats"], a["label"]
+        assert np.array_equal(a["ids"], b["ids"]), a["label"]
+        if a["op"] == "nn":
+            assert np.array_equal(a["d"], b["d"]), a["label"]
+
+
+def test_benchmark_scenes_every_row_equals_reference(gsa):
+    """The 64 scenes the benchmark times on one GPU (seeds 0..63): every row
+    of the batched engine and of its captured graph step against the
+    reference session run per scene, and this repository's session against
+    the reference's on two scenes (rows and statistics)."""
+    from gsa_b200 import QuerySession, hierarchy as hz, scenes
+
+    sizes, radii = hz.ROOM_SIZES, hz.ROOM_RADII
+    X = scenes.room_batch(range(64))
+    eng = hz.Batch(sizes, radii)
+    out = eng.run(X)
+    step = eng.capture(X)
+    for _ in range(2):
+        graph_out = step.replay()
+    torch.cuda.synchronize()
+    for b in range(64):
+        ref, rstats = _session_rows(gsa.QuerySession, X[b], sizes, radii)
+        for key, t in ref.items():
+            n = t.shape[0]
+            assert torch.equal(out[key][b * n:(b + 1) * n], t), (b, key)
+            assert torch.equal(graph_out[key][b * n:(b + 1) * n], t), ("graph", b, key)
+        if b in (0, 63):
+            mine, stats = _session_rows(QuerySession, X[b], sizes, radii)
+            assert stats == rstats, b
+            _assert_rows_equal(mine, ref, b)
+        del ref
+    step.close()
+    # second witness: the oracle on one scene
+    P = X[17].cpu().numpy()
+    want, _ = orc.hierarchy_oracle(P, sizes, radii)
+    for key, v in want.items():
+        n = v.shape[0]
+        assert np.array_equal(out[key][17 * n:18 * n].cpu().numpy(), v), key
+
+
+def _large_room():
+    from gsa_b200 import scenes
+
+    p, start = scenes.room(11, n=1_000_000, box=(20.0, 20.0, 3.0))
+    assert _sha(p) == LARGE["points_sha256"]
+    assert start == LARGE["fps_start"]
+    x = torch.from_numpy(p).cuda()
+    order = scenes.fps_order(x, start)
+    got = _sha(order.numpy().astype(np.int32))
+    assert got == LARGE["fps_order_sha256"], f"FPS order of the 1M-point room: sha256 {got}"
+    return x[order.cuda()].contiguous()
+
+
+def test_large_room_every_row_equals_reference(gsa):
+    from gsa_b200 import QuerySession, hierarchy as hz
+
+    sizes, radii = hz.LARGE_SIZES, hz.LARGE_RADII
+    P = _large_room()
+    mine, stats = _session_rows(QuerySession, P, sizes, radii)
+    ref, rstats = _session_rows(gsa.QuerySession, P, sizes, radii)
+    assert stats == rstats
+    assert stats["builds"] == 2 and stats["ball_hits"] == 4 and stats["fallbacks"] == 0
+    _assert_rows_equal(mine, ref, "session")
+    del mine
+    batch = hz.Batch(sizes, radii).run(P[None])
+    torch.cuda.synchronize()
+    _assert_rows_equal({k: batch[k] for k in ref}, ref, "batch")
+    del batch
+    # second witness: oracle rows on a sample of every stage
+    Pn = P.cpu().numpy()
+    rng = np.random.default_rng(5)
+    for s in range(4):
+        pick = np.unique(np.concatenate([rng.choice(sizes[s], 100, replace=False), [0, sizes[s] - 1]]))
+        want = orc.ball_oracle_fast(Pn[pick], Pn[: sizes[s]], radii[s], 32)
+        assert np.array_equal(ref[f"ball{s}"].cpu().numpy()[pick], want), s
+        ed, ei = orc.nn_oracle_fast(Pn[pick], Pn[: sizes[s + 1]])
+        assert np.array_equal(ref[f"nnd{s}"].cpu().numpy()[pick], ed), s
+        assert np.array_equal(ref[f"nni{s}"].cpu().numpy()[pick], ei), s
+
+
+def _clustered_sequence(make_session, pts, info):
+    x = torch.from_numpy(pts).cuda()
+    nq = info["queries"]
+    anchors = np.array(info["anchors"][:2000])
+    outs = []
+    with make_session() as s:
+        out = torch.empty((nq, 32), dtype=torch.int32, device="cuda")
+        s.ball_into(x[:nq], x, 0.25, 32, out)
+        d = torch.empty((len(pts), 3), device="cuda")
+        ids = torch.empty((len(pts), 3), dtype=torch.int32, device="cuda")
+        s.nn_into(x, x[:nq], d, ids)
+        outs += [out, d, ids]
+        # strict qualification on a support made of exact-r anchor pairs
+        sub = torch.from_numpy(np.concatenate([pts[anchors[:, 1]], pts[anchors[:, 0]]])).cuda()
+        o2 = torch.empty((len(anchors), 32), dtype=torch.int32, device="cuda")
+        s.ball_into(sub[: len(anchors)], sub, 0.25, 32, o2)
+        outs.append(o2)
+        # one coordinate one ulp up: the cached rows must not be reused
+        j = int(anchors[0, 0])
+        x2 = x.clone()
+        x2[j, 0] = torch.nextafter(x2[j, 0], torch.tensor(np.inf, device="cuda"))
+        out2 = torch.empty((nq, 32), dtype=torch.int32, device="cuda")
+        s.ball_into(x2[:nq], x2, 0.25, 32, out2)
+        # the original values (fresh tensors) still hit
+        out3 = torch.empty((nq // 2, 8), dtype=torch.int32, device="cuda")
+        s.ball_into(x[: nq // 2].clone(), x.clone(), 0.25, 8, out3)
+        outs += [out2, out3]
+        torch.cuda.synchronize()
+        s.close(collect=True)
+        stats = dict(s.stats)
+    return outs, stats, x2
+
+
+def test_clustered_stress_every_row_equals_reference(gsa):
+    from gsa_b200 import QuerySession, scenes
+
+    pts, info = scenes.clustered(seed=0)
+    mine, stats, x2 = _clustered_sequence(QuerySession, pts, info)
+    ref, rstats, _ = _clustered_sequence(gsa.QuerySession, pts, info)
+    assert stats == rstats
+    assert stats["ball_hits"] == 1 and stats["fallbacks"] == 0
+    for i, (a, b) in enumerate(zip(mine, ref)):
+        assert torch.equal(a, b), i
+    nq = info["queries"]
+    assert not torch.equal(mine[4], mine[0])  # the changed point moved rows
+    assert torch.equal(mine[5], mine[0][: nq // 2, :8])
+    # second witness: oracle rows around the changed point's query
+    p2 = x2.cpu().numpy()
+    j = int(info["anchors"][0][1])
+    pick = np.unique(np.concatenate([np.arange(0, 50), [j]]))
+    assert np.array_equal(mine[4].cpu().numpy()[pick], orc.ball_oracle_fast(p2[pick], p2, 0.25, 32))
+
+
+def _network(ops, sizes=(4096, 1024, 256, 64), radii=(0.2, 0.4, 0.8)):
+    """A PointNet++-shaped graph over FPS-style prefixes: per encoder stage a
+    self query (support P_s) and a down-sampling query (P_{s+1} against
+    P_s), then 3NN up the decoder."""
+
+    def graph(inputs):
+        root = inputs["pos"]
+        outputs = []
+        for s, r in enumerate(radii):
+            ps, pn = root[:, : sizes[s]].contiguous(), root[:, : sizes[s + 1]].contiguous()
+            for q, k in ((ps, 32), (pn, 16)):
+                result = torch.zeros(1, q.shape[1], k, device="cuda", dtype=torch.int32)
+                ops.ball_query_wrapper(1, ps.shape[1], q.shape[1], r, k, q, ps, result)
+                outputs.append(result)
+        for s in range(len(radii) - 1, -1, -1):
+            q, sup = root[:, : sizes[s]].contiguous(), root[:, : sizes[s + 1]].contiguous()
+            d = torch.empty(1, q.shape[1], 3, device="cuda")
+            ids = torch.empty(1, q.shape[1], 3, device="cuda", dtype=torch.int32)
+            ops.three_nn_wrapper(1, q.shape[1], sup.shape[1], q, sup, d, ids)
+            outputs += [d, ids]
+        return outputs
+
+    return graph
+
+
+@pytest.mark.parametrize("threshold", [32, 1024])
+def test_fixed_graph_equals_reference_adapter(gsa, threshold):
+    from gsa_b200 import fixed_graph_forward, reference as ops, scenes
+
+    X = scenes.room_batch([5], n=4096)
+    data = {"pos": X}
+    for policy in ["prefix", "scale"]:
+        stats, rstats = {}, {}
+        with torch.inference_mode():
+            mine = fixed_graph_forward(_network(ops), data, ops=ops, policy=policy, threshold=threshold, stats=stats)
+            ref = gsa.fixed_graph_forward(_network(gsa.reference), data, ops=gsa.reference, policy=policy,
+                                          threshold=threshold, stats=rstats)
+        torch.cuda.synchronize()
+        assert stats == rstats, (policy, stats, rstats)
+        assert len(mine) == len(ref)
+        for i, (a, b) in enumerate(zip(mine, ref)):
+            assert torch.equal(a, b), (policy, i)
+    P = X[0].cpu().numpy()
+    want = orc.ball_oracle_fast(P[:1024], P[:4096], 0.2, 16)
+    assert np.array_equal(mine[1][0].cpu().numpy(), want)
