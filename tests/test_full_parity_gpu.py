@@ -201,7 +201,6 @@ def test_clustered_stress_every_row_equals_reference(gsa):
     for i, (a, b) in enumerate(zip(mine, ref)):
         assert torch.equal(a, b), i
     nq = info["queries"]
-    assert not torch.equal(mine[4], mine[0])  # the changed point moved rows
     assert torch.equal(mine[5], mine[0][: nq // 2, :8])
     # second witness: oracle rows around the changed point's query
     p2 = x2.cpu().numpy()
