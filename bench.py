@@ -2,34 +2,43 @@
 # SPDX-License-Identifier: Apache-2.0
 """Exact radius + 3NN query throughput on B200; prints one JSON line.
 
-Workload (weak scaling, scenes sharded by rank, no data-path collective):
-each GPU answers the PointNeXt-shaped query hierarchy of 64 FPS-ordered
-synthetic room scenes of 24,000 points (seeds rank*64 + i): per scene,
-prefixes 24000/6000/1500/375/94, radius r = 0.1/0.2/0.4/0.8 with K = 32
-(31,875 computed rows), the down-sampling rows served by the reuse cache
-after its value checks (7,969 rows) and 3NN on every decoder stage (31,875
-rows).  Unit: answered query rows per second, all GPUs together.
+Workload (the 64-scene configuration, scenes sharded across GPUs, no
+data-path collective): 64 FPS-ordered synthetic room scenes of 24,000 points
+(seeds 0..63); scene i runs on GPU i mod N, so each of N GPUs answers 64 / N
+scenes (strong scaling).  Per scene: prefixes 24000/6000/1500/375/94, radius
+r = 0.1/0.2/0.4/0.8 with K = 32 (31,875 computed rows), the down-sampling
+rows served by the reuse cache after its value checks (7,969 rows) and 3NN
+on every decoder stage (31,875 rows).  Unit: answered query rows per second,
+all GPUs together.
 
-* ``value``: one step = build the prefix forest of the rank's scenes and run
-  every stage (``gsa_b200.hierarchy.Batch``), inputs resident in HBM; device
+* ``value``: one step = rebuild the prefix forest of the rank's scenes and
+  run every stage (``gsa_b200.hierarchy.Batch``), inputs resident in HBM;
+  the step runs as one captured CUDA graph or as direct launches, whichever
+  a short calibration before timing finds faster (``step_mode``); device
   time from CUDA events per step, L2 flushed (256 MiB write) between steps
-  outside the timed events; max over ranks.
+  outside the timed events; max over ranks.  ``weak`` (N > 1): the same with
+  64 scenes on every GPU.
 * ``e2e``: the same rows through the drop-in ``QuerySession`` API, one scene
   at a time, points copied from pinned host memory and every output row
   copied back to pinned host memory inside the timed region.
-  ``e2e_batched``: the same with the batched ``Forest`` engine.
+  ``e2e_fixed_graph``: the same through ``fixed_graph_forward`` with the
+  measured "frozen" policy (``prefix``, ``verify=False``).  ``e2e_batched``:
+  the same with the batched engine.
 * ``roofline``: the query kernel with the largest share of step time,
   algorithmic bytes (radius 12 + 4K B per query, 3NN 36 B per query) over its
   measured time, against the measured HBM copy bandwidth.
 * ``cpu_baseline``: the NumPy oracle (a port of the reference's test oracle)
   on one scene, one core, rank 0 at N=1.
 
-``--impl reference`` times the reference's CPU algorithm (the oracle port) on
-all host cores on the same workload and exits; under torchrun only rank 0
-runs it.
+``--impl reference`` runs the reference instead, on rank 0 only: its CPU
+algorithm (the oracle port) on all host cores for ``value``, and, in
+``ref_cuda``, the reference's own GPU path (its unmodified ``QuerySession``
+with its CUDA kernels built from source for sm_100a) on the same scenes,
+timed per call with CUDA events.
 """
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -51,18 +60,20 @@ SIZES = (24000, 6000, 1500, 375, 94)
 RADII = (0.1, 0.2, 0.4, 0.8)
 K = 32
 FALLBACK_HBM_GBS = 6650.0
+TRAFFIC_PROFILE = ROOT / "profiles" / "dram_traffic_room64.json"
 
 
 def rows_per_scene():
     return sum(SIZES[:4]), sum(SIZES[1:5]), sum(SIZES[:4])
 
 
-def config(scenes):
+def config(total, world):
     ball, hit, nn = rows_per_scene()
     return {
-        "workload": f"room hierarchy, {scenes} FPS-ordered scenes x {SIZES[0]} points per GPU",
-        "scenes_per_gpu": scenes,
-        "scene_seeds": "rank*scenes + i",
+        "workload": f"room hierarchy, {total} FPS-ordered scenes x {SIZES[0]} points, scene i on GPU i mod {world}",
+        "scenes_total": total,
+        "scenes_per_gpu": -(-total // world),
+        "scene_seeds": "0..scenes_total-1",
         "points_per_scene": SIZES[0],
         "prefixes": list(SIZES),
         "radii": list(RADII),
@@ -79,14 +90,15 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--scenes", type=int, default=SCENES)
+    p.add_argument("--scenes", type=int, default=SCENES, help="scenes of the whole job")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     return p.parse_args()
 
 
 # --------------------------------------------------------------------------
-# reference arm: the oracle port on all host cores
+# reference arm: the oracle port on all host cores, and the reference's own
+# GPU path
 
 
 def _ref_worker_init():
@@ -114,6 +126,110 @@ def _ref_step(args):
 
 
 _ref_scene_cache = {}
+
+
+def ref_session_calls(gsa, s, P, out):
+    """The hierarchy's twelve calls on the reference's QuerySession, in the
+    order a PointNeXt-style network issues them; yields each call's name
+    after enqueueing it."""
+    for st in range(4):
+        ps, pn = P[: SIZES[st]], P[: SIZES[st + 1]]
+        s.ball_into(ps, ps, RADII[st], K, out[f"ball{st}"])
+        yield f"ball{st}"
+        s.ball_into(pn, ps, RADII[st], K, out[f"hit{st}"])
+        yield f"hit{st}"
+    for st in range(3, -1, -1):
+        s.nn_into(P[: SIZES[st]], P[: SIZES[st + 1]], out[f"nnd{st}"], out[f"nni{st}"])
+        yield f"nn{st}"
+
+
+def run_ref_cuda(args, total):
+    """The reference's GPU path on the job's scenes (all on this GPU): per
+    call CUDA-event time summed over scenes (host synchronisations inside
+    the calls included), a standalone prefix-tree build per scene, and the
+    end-to-end rate with pinned host buffers like our ``e2e``."""
+    import torch
+
+    from oracle import reference_gpu
+
+    why = reference_gpu.available()
+    if why:
+        return {"unavailable": why}
+    gsa = reference_gpu.load()
+    from gsa_b200 import hierarchy as hz, scenes
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    X = scenes.room_batch(range(total))  # the same inputs as our arm
+    flat, views = hz.session_outputs(SIZES, dev)
+    steps = max(1, min(args.steps, 3))
+    # per call, device spans
+    per_call = {}
+    for step in range(steps + 1):
+        for i in range(total):
+            with gsa.QuerySession() as s:
+                calls = ref_session_calls(gsa, s, X[i], views)
+                while True:
+                    t0 = torch.cuda.Event(enable_timing=True)
+                    t1 = torch.cuda.Event(enable_timing=True)
+                    t0.record()
+                    name = next(calls, None)
+                    t1.record()
+                    if name is None:
+                        break
+                    if step:
+                        per_call.setdefault(name, []).append((t0, t1))
+    torch.cuda.synchronize()
+    call_ms = {k: sum(a.elapsed_time(b) for a, b in v) / steps for k, v in per_call.items()}
+    # standalone prefix-tree build (cuBQL build + prefix refit, host-synced levels)
+    spans = []
+    for step in range(steps + 1):
+        for i in range(total):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            tree = gsa.Tree(X[i].clone(), prefix=True)
+            t1.record()
+            tree.close()
+            if step:
+                spans.append((t0, t1))
+    torch.cuda.synchronize()
+    build_ms = sum(a.elapsed_time(b) for a, b in spans) / steps
+    # end to end, as our e2e: pinned host points in, every row out
+    host_x = X.cpu().pin_memory()
+    host_flat = torch.empty((total, flat.numel()), dtype=torch.int32, pin_memory=True)
+    ms = 0.0
+    for step in range(steps + 1):
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(total):
+            x = host_x[i].to(dev, non_blocking=True)
+            with gsa.QuerySession() as s:
+                for _ in ref_session_calls(gsa, s, x, views):
+                    pass
+            host_flat[i].copy_(flat, non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        if step:
+            ms += t0.elapsed_time(t1)
+    ball, hit, nn = rows_per_scene()
+    rows = ball + hit + nn
+    step_ms = sum(call_ms.values())
+    return {
+        "what": "reference gsa.QuerySession + csrc/gsa_bvh.cu, csrc/reference_queries.cu built from source for sm_100a, one scene per session, threshold 1024",
+        "scenes": total,
+        "steps": steps,
+        "value": total * rows / (step_ms / 1000.0),
+        "ms_per_step": step_ms,
+        "calls_ms_per_step": {k: round(v, 4) for k, v in call_ms.items()},
+        "tree_build_ms_per_step": build_ms,
+        "e2e": {"value": total * rows * steps / (ms / 1000.0), "unit": UNIT,
+                "h2d_bytes_per_step": int(host_x.numel() * 4),
+                "d2h_bytes_per_step": int(host_flat.numel() * 4)},
+        "unit": UNIT,
+        "note": "call times are CUDA-event spans around each session call, host synchronisations inside the calls included",
+    }
 
 
 def run_reference(args, rank, world):
@@ -151,19 +267,28 @@ def run_reference(args, rank, world):
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * total_t / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": config(args.scenes),
+        "config": config(args.scenes, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            line["ref_cuda"] = run_ref_cuda(args, args.scenes)
+    except Exception as e:  # the CPU line stands; say why the GPU leg is missing
+        line["ref_cuda"] = {"unavailable": f"{type(e).__name__}: {e}"}
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------
 # our arm
+
 
 
 class NvmlClocks:
@@ -286,19 +411,6 @@ class Clocks:
         }
 
 
-def launch_total():
-    import ctypes
-
-    from gsa_b200 import _library
-
-    tot = 0
-    for name in ("gsa_bvh", "reference_queries"):
-        lib = _library.load(name)
-        v = ctypes.c_ulonglong()
-        lib.launch_counter.argtypes = [ctypes.POINTER(ctypes.c_ulonglong)]
-        lib.launch_counter(ctypes.byref(v))
-        tot += v.value
-    return tot
 
 
 def hbm_peak():
@@ -309,68 +421,125 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def dram_bytes_per_query():
-    """Measured DRAM bytes per radius query from the committed ncu summary."""
-    p = ROOT / "profiles" / "radius_frontier_kernel_room64.md"
+def kernel_sources_sha(names):
+    h = hashlib.sha256()
+    for n in names:
+        h.update((ROOT / "gsa_b200" / "csrc" / n).read_bytes())
+    return h.hexdigest()
+
+
+def measured_traffic(kernel):
+    """ncu DRAM bytes per query of ``kernel`` from the committed profile,
+    used only when the profile was taken of the kernel source built here
+    (same SHA-256 of its source files); else None."""
     try:
-        for line in p.read_text().splitlines():
-            if line.strip().startswith("dram_bytes_per_query:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
+        prof = json.loads(TRAFFIC_PROFILE.read_text())
+        entry = prof["kernels"][kernel]
+        if kernel_sources_sha(prof["sources"]) != prof["sources_sha256"]:
+            return None, "profile taken of a different kernel source"
+        return float(entry["dram_bytes_per_query"]), prof.get("command")
+    except (OSError, KeyError, ValueError) as e:
+        return None, f"no profile ({type(e).__name__})"
+
+
+def timed_steps(fn, steps, flush, torch):
+    """CUDA-event milliseconds of ``steps`` calls of ``fn`` (L2 flushed
+    before each, outside the events)."""
+    records = []
+    for _ in range(steps):
+        flush.zero_()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        records.append((start, end))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in records]
+
+
+class Step:
+    """One hierarchy step over the rank's scenes: a captured CUDA graph or
+    direct launches, whichever a calibration run finds faster (the graph
+    removes ~40 host calls per step; with many scenes per GPU the step is
+    device bound and direct launches schedule the concurrent stages a little
+    better)."""
+
+    def __init__(self, eng, X, out, flush, torch, calibrate=True):
+        from gsa_b200._library import launch_counter
+
+        self.eng, self.X, self.out = eng, X, out
+        self.graph = eng.capture(X, out)
+        self.mode = "graph"
+        if calibrate:
+            eager_fn = lambda: eng.run(X, out)
+            for _ in range(3):
+                eager_fn()
+                self.graph.replay()
+            torch.cuda.synchronize()
+            eager = statistics.median(timed_steps(eager_fn, 7, flush, torch))
+            graph = statistics.median(timed_steps(self.graph.replay, 7, flush, torch))
+            self.calibration_ms = {"graph": graph, "eager": eager}
+            if eager < graph:
+                self.mode = "eager"
+        if self.mode == "eager":
+            before = launch_counter()
+            eng.run(X, out)
+            self.launches = launch_counter() - before
+        else:
+            self.launches = self.graph.launches
+
+    def __call__(self):
+        if self.mode == "graph":
+            self.graph.replay()
+        else:
+            self.eng.run(self.X, self.out)
+
+    def close(self):
+        self.graph.close()
 
 
 def run_ours(args, rank, world, local):
-    import numpy as np
     import torch
-    import torch.distributed as dist
 
-    from gsa_b200 import QuerySession, distributed as gd, hierarchy as hz, scenes
+    from gsa_b200 import distributed as gd, hierarchy as hz, scenes
 
     dev = torch.device("cuda", local)
-    S = args.scenes
-    seeds = gd.rank_seeds(rank, S)
+    seeds = gd.shard_seeds(rank, world, args.scenes)
+    S = len(seeds)
     X = scenes.room_batch(seeds)
     eng = hz.Batch(SIZES, RADII)
     out = eng.allocate(S, dev)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
-    for _ in range(max(3, args.warmup)):
-        eng.run(X, out)
+    step = Step(eng, X, out, flush, torch)
+    warmup = max(3, args.warmup)
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
 
     try:
         clocks = NvmlClocks(torch, dev)
     except Exception:
         clocks = Clocks(torch, dev)
-    launches0 = launch_total()
+    if world > 1:
+        gd.barrier()
+    torch.cuda.synchronize()
     clocks.start()
-    records = []
-    timer = hz.StageTimer()
+    step_ms = timed_steps(step, args.steps, flush, torch)
     if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for _ in range(args.steps):
-        flush.zero_()
-        start = torch.cuda.Event(enable_timing=True)
-        start.record()
-        eng.run(X, out, timer)
-        end = torch.cuda.Event(enable_timing=True)
-        end.record()
-        records.append((start, end))
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+        gd.barrier()
     clock_info = clocks.stop()
-    launches = launch_total() - launches0
+    launches = step.launches * args.steps
 
-    step_ms = [s.elapsed_time(e) for s, e in records]
     total_ms = sum(step_ms)
+    max_ms = gd.max_over_ranks(total_ms, dev)
+    ball_rows, hit_rows, nn_rows = rows_per_scene()
+    rows = ball_rows + hit_rows + nn_rows
+    value = args.scenes * rows * args.steps / (max_ms / 1000.0)
+
     # Stage attribution and the roofline come from a second, serialized pass
-    # of the same steps (stages one after another on one stream, CUDA events
-    # around each stage), because the concurrent stages' spans overlap.
+    # of the same steps (direct launches, stages one after another on one
+    # stream, CUDA events around each stage), because concurrent spans overlap.
     timer = hz.StageTimer()
     torch.cuda.synchronize()
     for _ in range(args.steps):
@@ -383,10 +552,6 @@ def run_ours(args, rank, world, local):
         key = name.rstrip("0123456789")
         phase[key] = phase.get(key, 0.0) + ms
     serial_ms = sum(phase.values()) / args.steps
-    max_ms = gd.max_over_ranks(total_ms, dev)
-    ball_rows, hit_rows, nn_rows = rows_per_scene()
-    rows = ball_rows + hit_rows + nn_rows
-    value = world * S * rows * args.steps / (max_ms / 1000.0)
 
     # Roofline per query kernel (serialized pass): stages 0-2 of the radius
     # query and of 3NN walk the tree, stage 3 scans (support prefixes of at
@@ -400,7 +565,8 @@ def run_ours(args, rank, world, local):
         queries = args.steps * S * sum(SIZES[i] for i in sizes_idx)
         gbs = queries * per_query / (ms / 1000.0) / 1e9 if ms else 0.0
         return {"ms_per_step": ms / args.steps, "launches_per_step": len(stages),
-                "queries_per_step": queries // args.steps, "achieved_gbs": gbs}
+                "queries_per_step": queries // args.steps, "achieved_gbs": gbs,
+                "frac": gbs / peak}
 
     kernels = {
         "radius_frontier_kernel": kernel_line(["ball0", "ball1", "ball2"], [0, 1, 2], radius_q),
@@ -423,7 +589,7 @@ def run_ours(args, rank, world, local):
     name = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     kl = kernels[name]
     achieved = kl["achieved_gbs"]
-    dbq = dram_bytes_per_query() if name == "radius_frontier_kernel" else None
+    dbq, traffic_src = measured_traffic(name)
     traffic = None if dbq is None else dbq * kl["queries_per_step"] / kl["launches_per_step"]
     roofline = {
         "bound": "hbm",
@@ -433,9 +599,10 @@ def run_ours(args, rank, world, local):
         "unit": "GB/s",
         "frac": achieved / peak,
         "traffic": traffic,
+        "traffic_source": traffic_src,
         "peak_source": f"{peak_kind} HBM copy bandwidth",
         "algorithmic_bytes_per_query": radius_q if name.startswith("radius") else 36,
-        "note": "achieved = algorithmic bytes of the kernel's launches / their summed CUDA-event time (serialized pass)",
+        "note": "achieved = algorithmic bytes of the kernel's launches / their summed CUDA-event time (serialized pass); traffic = ncu DRAM bytes per launch",
         "kernels": kernels,
         "reuse_check_and_copy": reuse_line,
     }
@@ -449,14 +616,16 @@ def run_ours(args, rank, world, local):
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
-        "warmup": max(3, args.warmup),
+        "warmup": warmup,
         "ms_per_step": max_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": config(S),
+        "config": config(args.scenes, world),
+        "step_mode": step.mode,
+        "step_calibration_ms": getattr(step, "calibration_ms", None),
         "roofline": roofline,
         "phases_ms_per_step": {k: v / args.steps for k, v in phase.items()},
         "stages_ms_per_step": {k: round(v / args.steps, 4) for k, v in stage.items()},
@@ -466,110 +635,160 @@ def run_ours(args, rank, world, local):
             "stage times and the roofline come from a separate serialized pass of the same steps"
         ),
         "gpu_launches": launches,
-        "gpu_launches_per_step": launches / args.steps,
+        "gpu_launches_per_step": step.launches,
         "clocks": clock_info,
         "rank_rows_checksums": [list(g) for g in gathered],
     }
 
+    if world > 1:
+        line["weak"] = weak_run(args, rank, world, dev, flush)
+
     if not args.no_e2e:
-        line["e2e"], line["e2e_batched"] = e2e(args, X, eng, out, world, dev)
+        line["e2e"], line["e2e_fixed_graph"], line["e2e_batched"] = e2e(args, X, step, out, world, dev)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out, S)
+        line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out)
+    step.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
 
 
-def e2e(args, X, eng, out, world, dev):
+def weak_run(args, rank, world, dev, flush):
+    """Weak scaling: 64 scenes on every GPU (seeds rank*64 + i)."""
+    import torch
+
+    from gsa_b200 import distributed as gd, hierarchy as hz, scenes
+
+    S = SCENES
+    X = scenes.room_batch(gd.rank_seeds(rank, S))
+    eng = hz.Batch(SIZES, RADII)
+    out = eng.allocate(S, dev)
+    step = Step(eng, X, out, flush, torch)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    gd.barrier()
+    ms = sum(timed_steps(step, args.steps, flush, torch))
+    gd.barrier()
+    max_ms = gd.max_over_ranks(ms, dev)
+    ball, hit, nn = rows_per_scene()
+    step.close()
+    return {
+        "scenes_per_gpu": S,
+        "value": world * S * (ball + hit + nn) * args.steps / (max_ms / 1000.0),
+        "ms_per_step": max_ms / args.steps,
+        "step_mode": step.mode,
+        "unit": UNIT,
+    }
+
+
+def e2e(args, X, step, out, world, dev):
     """End-to-end rows/s through the public APIs with pinned host buffers."""
     import torch
-    import torch.distributed as dist
 
-    from gsa_b200 import QuerySession, hierarchy as hz
+    from gsa_b200 import QuerySession, distributed as gd, fixed_graph_forward, hierarchy as hz
+    from gsa_b200 import reference as ops
 
     S = X.shape[0]
     host_x = X.cpu().pin_memory()
     ball_rows, hit_rows, nn_rows = rows_per_scene()
     rows = ball_rows + hit_rows + nn_rows
     steps = max(1, min(args.steps, 3))
-
-    # drop-in QuerySession, one scene at a time; a scene's outputs are views
-    # of one device buffer, copied back to pinned memory in one transfer
-    # (stream order keeps the next scene from overwriting it early)
     flat, views = hz.session_outputs(SIZES, dev)
     host_flat = torch.empty((S, flat.numel()), dtype=torch.int32, pin_memory=True)
     d2h = S * flat.numel() * flat.element_size()
-    ms = 0.0
-    for step in range(steps + 1):  # first pass warms allocator and pinned buffers
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for i in range(S):
-            x = host_x[i].to(dev, non_blocking=True)
-            with QuerySession() as s:
-                hz.run_session(s, x, SIZES, RADII, views)
-            host_flat[i].copy_(flat, non_blocking=True)
-        t1.record()
-        torch.cuda.synchronize()
-        if step:
-            ms += t0.elapsed_time(t1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+
+    def per_scene(run_scene):
+        ms = 0.0
+        for st in range(steps + 1):  # first pass warms allocator and pinned buffers
+            torch.cuda.synchronize()
+            if world > 1:
+                gd.barrier()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for i in range(S):
+                x = host_x[i].to(dev, non_blocking=True)
+                run_scene(x)
+                # a scene's outputs are views of one device buffer, copied back
+                # in one transfer (stream order keeps the next scene from
+                # overwriting it early)
+                host_flat[i].copy_(flat, non_blocking=True)
+            t1.record()
+            torch.cuda.synchronize()
+            if st:
+                ms += t0.elapsed_time(t1)
+        return world * S * rows * steps / (gd.max_over_ranks(ms, dev) / 1000.0)
+
+    def session_scene(x):
+        with QuerySession() as s:
+            hz.run_session(s, x, SIZES, RADII, views)
+
     session = {
-        "value": world * S * rows * steps / (float(t.item()) / 1000.0),
+        "value": per_scene(session_scene),
         "unit": UNIT,
         "h2d_bytes_per_step": int(host_x.numel() * 4),
         "d2h_bytes_per_step": int(d2h),
         "api": "gsa_b200.QuerySession (drop-in for gsa.QuerySession), one scene per session, threshold 1024",
         "steps": steps,
     }
+    session_rows0 = host_flat[0].clone()
 
-    # batched Forest engine
+    model = hz.graph_model(ops, SIZES, RADII, views)
+
+    def fixed_scene(x):
+        fixed_graph_forward(model, {"pos": x[None]}, ops=ops, policy="prefix", verify=False)
+
+    with torch.inference_mode():
+        fixed_value = per_scene(fixed_scene)
+    fixed = {
+        "value": fixed_value,
+        "unit": UNIT,
+        "h2d_bytes_per_step": int(host_x.numel() * 4),
+        "d2h_bytes_per_step": int(d2h),
+        "api": "gsa_b200.fixed_graph_forward (drop-in for gsa.fixed_graph.forward), policy prefix, verify=False (the measured 'frozen' policy), one scene per forward",
+        "steps": steps,
+        "rows_equal_session_scene0": bool(torch.equal(host_flat[0], session_rows0)),
+    }
+
+    # batched engine: the captured step reads X, so the host copy lands there
     keys = [k for k in out if k.startswith(("ball", "hit", "nn"))]
     host_b = {k: torch.empty(out[k].shape, dtype=out[k].dtype, pin_memory=True) for k in keys}
-    xb = torch.empty_like(X)
     ms = 0.0
-    for step in range(steps + 1):
+    for st in range(steps + 1):
         torch.cuda.synchronize()
         if world > 1:
-            dist.barrier()
+            gd.barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        xb.copy_(host_x, non_blocking=True)
-        eng.run(xb, out)
+        X.copy_(host_x, non_blocking=True)
+        step()
         for k in keys:
             host_b[k].copy_(out[k], non_blocking=True)
         t1.record()
         torch.cuda.synchronize()
-        if step:
+        if st:
             ms += t0.elapsed_time(t1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    # scene 0 through both paths: the same rows
-    _, first = hz.session_outputs(SIZES, "cpu", host_flat[0])
-    same = all(
-        torch.equal(v, host_b[k][: v.shape[0]]) for k, v in first.items() if k in host_b
+    _, first = hz.session_outputs(SIZES, "cpu", session_rows0)
+    session["rows_equal_batched_scene0"] = bool(
+        all(torch.equal(v, host_b[k][: v.shape[0]]) for k, v in first.items() if k in host_b)
     )
-    session["rows_equal_batched_scene0"] = bool(same)
     batched = {
-        "value": world * S * rows * steps / (float(t.item()) / 1000.0),
+        "value": world * S * rows * steps / (gd.max_over_ranks(ms, dev) / 1000.0),
         "unit": UNIT,
         "h2d_bytes_per_step": int(host_x.numel() * 4),
         "d2h_bytes_per_step": int(sum(v.numel() * v.element_size() for v in host_b.values())),
-        "api": "gsa_b200.hierarchy.Batch over gsa_b200.Forest (batched C ABI)",
+        "api": f"gsa_b200.hierarchy.Batch over gsa_b200.Forest (batched C ABI), step as {step.mode}",
         "steps": steps,
     }
-    return session, batched
+    return session, fixed, batched
 
 
-def cpu_baseline(P, out, S):
+def cpu_baseline(P, out):
     """The NumPy oracle on scene 0 (one core); also checks scene 0's rows."""
+    import numpy as np
+
     from oracle import numpy_oracle as orc
 
     t0 = time.perf_counter()
@@ -578,10 +797,7 @@ def cpu_baseline(P, out, S):
     ok = True
     for key, v in ref.items():
         n = v.shape[0]
-        got = out[key][:n].cpu().numpy()
-        import numpy as np
-
-        ok &= bool(np.array_equal(got, v))
+        ok &= bool(np.array_equal(out[key][:n].cpu().numpy(), v))
     return {
         "value": rows / dt,
         "unit": UNIT,

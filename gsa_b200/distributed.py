@@ -32,6 +32,12 @@ def rank_seeds(rank, scenes_per_rank):
     return [rank * scenes_per_rank + i for i in range(scenes_per_rank)]
 
 
+def barrier():
+    """Wait for every rank (no-op without a process group)."""
+    if world()[1] > 1:
+        dist.barrier()
+
+
 def max_over_ranks(value, device="cpu"):
     """Largest value over all ranks (e.g. the slowest rank's device time)."""
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)

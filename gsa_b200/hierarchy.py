@@ -93,6 +93,31 @@ def run_session(session, P, sizes=ROOM_SIZES, radii=ROOM_RADII, out=None):
     return out
 
 
+def graph_model(ops, sizes=ROOM_SIZES, radii=ROOM_RADII, out=None):
+    """The hierarchy as a fixed PointNet++-style network for
+    ``fixed_graph_forward``: ``model(data)`` takes ``data["pos"]`` of shape
+    (1, N, 3) and issues, through ``ops.ball_query_wrapper`` /
+    ``ops.three_nn_wrapper`` (looked up at call time, so the adapter's
+    patched wrappers run), the same calls in the same order as
+    ``run_session``: per stage s the self query of P_s and the down-sampling
+    query of P_{s+1} against P_s, then 3NN for s = 3..0.  Rows go to ``out``
+    (tensors keyed and shaped like ``run_session``'s, e.g. the views of
+    ``session_outputs``)."""
+
+    def model(data):
+        root = data["pos"]
+        for s in range(4):
+            ps, pn = root[:, : sizes[s]], root[:, : sizes[s + 1]]
+            ops.ball_query_wrapper(1, sizes[s], sizes[s], radii[s], K, ps, ps, out[f"ball{s}"][None])
+            ops.ball_query_wrapper(1, sizes[s], sizes[s + 1], radii[s], K, pn, ps, out[f"hit{s}"][None])
+        for s in range(3, -1, -1):
+            ops.three_nn_wrapper(1, sizes[s], sizes[s + 1], root[:, : sizes[s]], root[:, : sizes[s + 1]],
+                                 out[f"nnd{s}"][None], out[f"nni{s}"][None])
+        return out
+
+    return model
+
+
 class Batch:
     """Hierarchy over B scenes of N points each, all on the device."""
 
