@@ -23,21 +23,23 @@ __device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
   }
 }
 
+// The first m points of the order of each scene (m <= n); start[b] null
+// starts every scene at index 0.
 __global__ void __launch_bounds__(kFpsThreads)
-    fps_kernel(int n, const float* x, const int* start, int* order) {
+    fps_kernel(int n, int m, const float* x, const int* start, int* order) {
   extern __shared__ float mind[];
   __shared__ float wv[32];
   __shared__ int wi[32];
   __shared__ int cur_s;
   int b = blockIdx.x;
   const float* xb = x + 3ll * n * b;
-  int* ob = order + (long long)n * b;
+  int* ob = order + (long long)m * b;
   for (int i = threadIdx.x; i < n; i += kFpsThreads)
     mind[i] = __int_as_float(0x7f800000);
-  if (threadIdx.x == 0) cur_s = start[b];
+  if (threadIdx.x == 0) cur_s = start ? start[b] : 0;
   __syncthreads();
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int it = 0; it < n; ++it) {
+  for (int it = 0; it < m; ++it) {
     int cur = cur_s;
     if (threadIdx.x == 0) ob[it] = cur;
     float cx = __ldg(xb + 3ll * cur), cy = __ldg(xb + 3ll * cur + 1),
@@ -121,7 +123,7 @@ __device__ void grid_barrier(unsigned* count, unsigned* gen, int* err) {
 
 template <int PER>
 __global__ void __launch_bounds__(kFpsThreads)
-    fps_grid_kernel(int n, const float* x, int start, int* order,
+    fps_grid_kernel(int n, int m, const float* x, int start, int* order,
                     unsigned long long* best, unsigned* bar, int* err) {
   __shared__ unsigned long long wbest[32];
   const int threads = gridDim.x * kFpsThreads;
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(kFpsThreads)
   }
   int cur = start;
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int it = 0; it < n; ++it) {
+  for (int it = 0; it < m; ++it) {
     if (tid == 0) order[it] = cur;
     float cx = __ldg(x + 3ll * cur), cy = __ldg(x + 3ll * cur + 1),
           cz = __ldg(x + 3ll * cur + 2);
@@ -179,10 +181,11 @@ __global__ void __launch_bounds__(kFpsThreads)
 }
 
 template <int PER>
-cudaError_t launch_fps_grid(int n, const float* x, int start, int* order,
-                            unsigned long long* best, unsigned* bar, int* err,
-                            int blocks, cudaStream_t s) {
-  void* args[] = {&n, &x, &start, &order, &best, &bar, &err};
+cudaError_t launch_fps_grid(int n, int m, const float* x, int start,
+                            int* order, unsigned long long* best,
+                            unsigned* bar, int* err, int blocks,
+                            cudaStream_t s) {
+  void* args[] = {&n, &m, &x, &start, &order, &best, &bar, &err};
   return cudaLaunchCooperativeKernel((const void*)fps_grid_kernel<PER>,
                                      dim3(blocks), dim3(kFpsThreads), args, 0,
                                      s);
@@ -193,12 +196,13 @@ cudaError_t launch_fps_grid(int n, const float* x, int start, int* order,
 
 using namespace gsa;
 
-// See include/gsa_bvh.h.
-GSA_API int fps_order_large(int n, const float* x, int start, int* order,
-                            void* scratch, int* err, void* stream) {
-  if (n < 1 || !x || !order || !scratch || !err || start < 0 || start >= n)
-    return -2;
-  cudaStream_t s = (cudaStream_t)stream;
+namespace {
+
+constexpr size_t kFpsSmemMax = 200 * 1024;  // running minima in shared memory
+
+cudaError_t fps_large(int n, int m, const float* x, int start, int* order,
+                      void* scratch, int* err, cudaStream_t s, int* code) {
+  *code = 0;
   int device = 0, sms = 0, per_sm = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (!e) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -208,18 +212,45 @@ GSA_API int fps_order_large(int n, const float* x, int start, int* order,
   if (e) return e;
   int blocks = sms * std::min(per_sm, 1);
   long long threads = (long long)blocks * kFpsThreads;
+  if (n > threads * 8) {  // at most 8 points per thread
+    *code = -2;
+    return cudaSuccess;
+  }
   unsigned long long* best = static_cast<unsigned long long*>(scratch);
   unsigned* bar = reinterpret_cast<unsigned*>(best + 3);
   e = cudaMemsetAsync(scratch, 0, 64, s);
   if (!e) e = cudaMemsetAsync(err, 0, sizeof(int), s);
   if (e) return e;
-  if (n > threads * 8) return -2;  // at most 8 points per thread
   count_launches();
   if (n <= threads * 2)
-    e = launch_fps_grid<2>(n, x, start, order, best, bar, err, blocks, s);
+    e = launch_fps_grid<2>(n, m, x, start, order, best, bar, err, blocks, s);
   else
-    e = launch_fps_grid<8>(n, x, start, order, best, bar, err, blocks, s);
-  return e ? (int)e : (int)cudaGetLastError();
+    e = launch_fps_grid<8>(n, m, x, start, order, best, bar, err, blocks, s);
+  return e ? e : cudaGetLastError();
+}
+
+cudaError_t fps_small(int b, int n, int m, const float* x, const int* start,
+                      int* order, cudaStream_t s) {
+  size_t smem = sizeof(float) * (size_t)n;
+  cudaError_t e = cudaFuncSetAttribute(
+      fps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e) return e;
+  count_launches();
+  fps_kernel<<<b, kFpsThreads, smem, s>>>(n, m, x, start, order);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// See include/gsa_bvh.h.
+GSA_API int fps_order_large(int n, const float* x, int start, int* order,
+                            void* scratch, int* err, void* stream) {
+  if (n < 1 || !x || !order || !scratch || !err || start < 0 || start >= n)
+    return -2;
+  int code = 0;
+  cudaError_t e = fps_large(n, n, x, start, order, scratch, err,
+                            (cudaStream_t)stream, &code);
+  return e ? (int)e : code;
 }
 
 // See include/gsa_bvh.h.
@@ -227,14 +258,30 @@ GSA_API int fps_order(int b, int n, const float* x, const int* start,
                       int* order, void* stream) {
   if (b < 0 || n < 0) return -2;
   if (!b || !n) return 0;
-  size_t smem = sizeof(float) * (size_t)n;
-  if (smem > 200 * 1024) return -2;
+  if (sizeof(float) * (size_t)n > kFpsSmemMax) return -2;
   if (!x || !start || !order) return -2;
-  cudaError_t e = cudaFuncSetAttribute(
-      fps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e) return e;
-  count_launches();
-  fps_kernel<<<b, kFpsThreads, smem, (cudaStream_t)stream>>>(n, x, start,
-                                                              order);
-  return cudaGetLastError();
+  return (int)fps_small(b, n, n, x, start, order, (cudaStream_t)stream);
+}
+
+// See include/gsa_bvh.h.
+GSA_API int furthest_point_sample(int b, int n, int m, const float* x,
+                                  float* temp, int* idx, void* stream) {
+  if (b < 0 || n < 0 || m < 0 || m > n) return -2;
+  if (!b || !m) return 0;
+  if (!x || !idx) return -2;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (sizeof(float) * (size_t)n <= kFpsSmemMax)
+    return (int)fps_small(b, n, m, x, nullptr, idx, s);
+  // one scene per cooperative grid; temp (b*n floats) holds its barrier
+  // words and the error flag
+  if (!temp) return -2;
+  for (int i = 0; i < b; ++i) {
+    float* t = temp + (long long)n * i;
+    int code = 0;
+    cudaError_t e = fps_large(n, m, x + 3ll * n * i, 0, idx + (long long)m * i,
+                              t, reinterpret_cast<int*>(t + 16), s, &code);
+    if (e) return (int)e;
+    if (code) return code;
+  }
+  return 0;
 }

@@ -197,6 +197,27 @@ int fps_order(int b, int n, const float* x, const int* start, int* order,
 int fps_order_large(int n, const float* x, int start, int* order,
                     void* scratch, int* err, void* stream);
 
+/* Furthest point sampling with the PointNet++ operator's arguments
+ * (furthest_point_sampling_wrapper(b, n, m, points, temp, idx), the op that
+ * samples the query levels GSA's networks search): for each of b scenes of n
+ * points (x is [b][n][3]) the first m indices of the farthest-point order
+ * starting at index 0, into idx ([b][m] device ints).  Rule: the next point
+ * is the one with the largest running minimum of the FP32 squared distance
+ * ((dx*dx + dy*dy) + dz*dz) (round to nearest, no FMA) to the points chosen
+ * so far, ties to the LOWEST index, chosen points never repeat; a NaN
+ * distance never lowers a running minimum, so points with a non-finite
+ * coordinate stay at +inf and are chosen first, lowest index first.  Scenes of up to 51,200 points keep the running minima in shared
+ * memory (one block per scene; temp may be null).  Larger scenes use one
+ * cooperative grid each (up to ~1.2 M points) and need temp (device floats,
+ * b*n): its first 17 words of each scene's row are the grid's barrier words
+ * and error flag, and ((int*)temp)[n*i + 16] != 0 after the stream reaches
+ * it means scene i's order is incomplete (a grid barrier wait ran out).
+ * Returns 0, a cudaError_t, or -2 for bad arguments.  The reference has no
+ * FPS of its own (it sits upstream, in FlashFPS); the rule is the one its
+ * FPS-ordered prefixes assume. */
+int furthest_point_sample(int b, int n, int m, const float* x, float* temp,
+                          int* idx, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,7 @@ def bvh_lib(name="gsa_bvh"):
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]
     lib.fps_order.argtypes = [I, I, P, P, P, P]
+    lib.furthest_point_sample.argtypes = [I, I, I, P, P, P, P]
     lib.bvh_info.argtypes = [P] + [ctypes.POINTER(I)] * 4
     lib.pool_memory.argtypes = [ctypes.POINTER(ctypes.c_uint64)] * 2
     return lib

@@ -254,3 +254,35 @@ def test_fixed_graph_equals_reference_adapter(gsa, threshold):
     P = X[0].cpu().numpy()
     want = orc.ball_oracle_fast(P[:1024], P[:4096], 0.2, 16)
     assert np.array_equal(mine[1][0].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("workload", ["room", "large_room"])
+def test_pool_memory_next_to_reference(gsa, workload):
+    """Native-pool high-water marks of one scene's hierarchy through each
+    session (``pool_memory`` after ``pool_reset_peak``, both libraries'
+    own pools, ``gsa/runtime.py:33-40``): the figures the reference's
+    memory-overhead comparison reads.  The forest stores two 32-byte child
+    entries per level for every one of the n-1 radix-tree nodes (about a
+    tenth are used), so it holds more than the reference's cuBQL tree; the
+    test pins that ratio so it cannot grow unnoticed."""
+    from gsa_b200 import QuerySession, hierarchy as hz, runtime, scenes
+
+    if workload == "room":
+        sizes, radii = hz.ROOM_SIZES, hz.ROOM_RADII
+        P = scenes.room_batch([3])[0]
+    else:
+        sizes, radii = hz.LARGE_SIZES, hz.LARGE_RADII
+        P = _large_room()
+    peaks = {}
+    for name, mod, session in (("ours", runtime, QuerySession), ("reference", gsa.runtime, gsa.QuerySession)):
+        torch.cuda.synchronize()
+        assert mod.lib.pool_reset_peak() == 0
+        _session_rows(session, P, sizes, radii)
+        torch.cuda.synchronize()
+        peaks[name] = mod.pool_memory()
+    print(f"\npool peaks {workload} ({sizes[0]} points): {json.dumps(peaks)}")
+    ours = peaks["ours"]["native_pool_used_peak_bytes"]
+    ref = peaks["reference"]["native_pool_used_peak_bytes"]
+    assert 0 < ref and 0 < ours <= 16 * ref
+    for p in peaks.values():
+        assert p["native_pool_reserved_peak_bytes"] >= p["native_pool_used_peak_bytes"]

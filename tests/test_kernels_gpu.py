@@ -344,6 +344,39 @@ def test_fps_cooperative_grid_matches_single_block():
     assert torch.equal(small, large)
 
 
+def test_furthest_point_sample_op_matches_sequential_rule():
+    """The PointNet++-style FPS op: first m indices from index 0, exact FP32
+    distances, ties to the lowest index (a lattice makes many exact ties),
+    NaN points chosen first; small scenes in shared memory, a 60,000-point
+    scene on the cooperative grid."""
+    from gsa_b200 import sampling
+    from oracle import fps as fps_cpu
+
+    rng = np.random.default_rng(4)
+    lat = np.stack(np.meshgrid(*[np.arange(12, dtype=np.float32)] * 3, indexing="ij"), -1).reshape(-1, 3)
+    pts = np.stack([
+        rng.normal(size=(1728, 3)).astype(np.float32),
+        lat * np.float32(0.25),
+        rng.random((1728, 3)).astype(np.float32),
+    ])
+    pts[2, 5] = pts[2, 9]
+    pts[2, 40, 1] = np.nan
+    x = torch.from_numpy(pts).cuda()
+    for m in (1, 432, 1728):
+        idx = sampling.furthest_point_sample(x, m).cpu().numpy()
+        for i in range(3):
+            assert np.array_equal(idx[i], fps_cpu.fps_order(pts[i], 0, m)), (i, m)
+    assert sampling.furthest_point_sample(x, 0).shape == (3, 0)
+    big = rng.normal(size=(1, 60000, 3)).astype(np.float32)
+    idx = sampling.furthest_point_sample(torch.from_numpy(big).cuda(), 300).cpu().numpy()
+    assert np.array_equal(idx[0], fps_cpu.fps_order(big[0], 0, 300))
+    with pytest.raises(ValueError):
+        sampling.furthest_point_sample(x, 1729)
+    lib = abi.bvh_lib()
+    assert lib.furthest_point_sample(1, 10, 11, None, None, None, None) == -2
+    assert lib.furthest_point_sample(1, 60000, 5, x.data_ptr(), None, x.data_ptr(), None) == -2  # temp needed
+
+
 def test_pool_reports_usage():
     from gsa_b200 import runtime
 
