@@ -26,10 +26,20 @@
 //      every subtree with <= `leaf` members is a leaf over the level's member
 //      array, so coarse levels keep full leaves      (climb_kernel: one
 //      thread per climb from each node with two leaves)
+#include <cooperative_groups.h>
 #include <algorithm>
+#include <atomic>
 #include <new>
 #include "forest.cuh"
 #include "pool.cuh"
+
+namespace cg = cooperative_groups;
+
+// Trees of up to 32,768 points are keyed and sorted by one cluster launch
+// (cluster_sort_kernel); 0 keeps every tree on the multi-launch path.
+#ifndef GSA_CLUSTER_SORT
+#define GSA_CLUSTER_SORT 1
+#endif
 
 namespace gsa {
 namespace {
@@ -302,6 +312,249 @@ __global__ void __launch_bounds__(kSortThreads)
     cnt[tid] += s;
     __syncthreads();
   }
+}
+
+// ---------------------------------------------------------------------------
+// Trees of up to kClusterMaxPoints points: bounds, Morton keys, the four
+// radix passes and the per-level member offsets in ONE launch.  A thread-block
+// cluster owns one tree, each CTA a tile of kCTile consecutive positions held
+// in its shared memory; the CTAs exchange bounds, digit histograms and member
+// counts through distributed shared memory and scatter keys straight into the
+// destination CTA's next buffer, with a cluster barrier between steps.  The
+// multi-launch path (bounds_kernel ... member_prefix, 14 launches) does the
+// same work for larger trees.  Keys are at most 30 bits here (morton_bits of
+// n <= 32768 is 10), so they live in shared memory as 32-bit words; the output
+// (64-bit keys, local indices, member offsets) equals the multi-launch path's.
+constexpr int kCThreads = 512;
+constexpr int kCItems = 8;
+constexpr int kCTile = kCThreads * kCItems;  // 4096 positions per CTA
+constexpr int kClusterMax = 8;               // portable cluster size
+constexpr int kClusterMaxPoints = kClusterMax * kCTile;
+constexpr int kCWarps = kCThreads / 32;
+
+struct ClusterSmem {
+  unsigned keys[2][kCTile];
+  int vals[2][kCTile];
+  int wcnt[kCWarps][256];  // per-warp digit counts of one item row
+  int hist[256];           // this tile's digit counts (read by the cluster)
+  int goff[256];
+  int cnt[256];
+  unsigned bnd[6];         // this tile's bounds keys (read by the cluster)
+  int lcnt[kMaxLevels];    // this tile's member counts (read by the cluster)
+  int wsum[kCWarps][kMaxLevels];
+  int grp[kCItems][kCWarps][kMaxLevels];  // member counts per (row, warp)
+};
+
+__global__ void __launch_bounds__(kCThreads)
+    cluster_sort_kernel(const TreeDesc* desc, const float* x, int bits,
+                        int levels, uint64_t* keys_out, int* vals_out,
+                        int* pref, int N) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  ClusterSmem& S = *reinterpret_cast<ClusterSmem*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int cs = (int)cluster.num_blocks();
+  const TreeDesc d = desc[blockIdx.y];
+  const int n = d.n;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int base = rank * kCTile;
+
+  // 1. bounds of the finite points (order-preserving keys, as bounds_kernel)
+  float px[kCItems], py[kCItems], pz[kCItems];
+  unsigned lo[3] = {~0u, ~0u, ~0u}, hi[3] = {0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < kCItems; ++j) {
+    const int i = base + j * kCThreads + tid;
+    px[j] = py[j] = pz[j] = NAN;
+    if (i < n) {
+      const float* q = x + 3ll * (d.p0 + i);
+      px[j] = q[0];
+      py[j] = q[1];
+      pz[j] = q[2];
+    }
+    if (finite3(px[j], py[j], pz[j])) {
+      lo[0] = min(lo[0], float_key(px[j]));
+      lo[1] = min(lo[1], float_key(py[j]));
+      lo[2] = min(lo[2], float_key(pz[j]));
+      hi[0] = max(hi[0], float_key(px[j]));
+      hi[1] = max(hi[1], float_key(py[j]));
+      hi[2] = max(hi[2], float_key(pz[j]));
+    }
+  }
+  if (tid < 6) S.bnd[tid] = tid < 3 ? ~0u : 0u;
+  __syncthreads();
+  for (int k = 0; k < 3; ++k) {
+    lo[k] = __reduce_min_sync(kFull, lo[k]);
+    hi[k] = __reduce_max_sync(kFull, hi[k]);
+  }
+  if (lane == 0) {
+    for (int k = 0; k < 3; ++k) {
+      atomicMin(&S.bnd[k], lo[k]);
+      atomicMax(&S.bnd[3 + k], hi[k]);
+    }
+  }
+  cluster.sync();
+  unsigned bk[6] = {~0u, ~0u, ~0u, 0u, 0u, 0u};
+  for (int c = 0; c < cs; ++c) {
+    const unsigned* rb = cluster.map_shared_rank(S.bnd, c);
+    for (int k = 0; k < 3; ++k) {
+      bk[k] = min(bk[k], rb[k]);
+      bk[3 + k] = max(bk[3 + k], rb[3 + k]);
+    }
+  }
+
+  // 2. Morton keys (as morton_kernel) and local indices, in tile order
+  {
+    const unsigned top = (1u << bits) - 1u;
+    const bool any = bk[0] != 0xffffffffu;
+    float l3[3], ext = 0.f;
+    for (int k = 0; k < 3; ++k) {
+      l3[k] = any ? key_float(bk[k]) : 0.f;
+      const float h = any ? key_float(bk[3 + k]) : 0.f;
+      ext = fmaxf(ext, h - l3[k]);
+    }
+    const float scale = (ext > 0.f && isfinite(ext)) ? (float)top / ext : 0.f;
+#pragma unroll
+    for (int j = 0; j < kCItems; ++j) {
+      const int li = j * kCThreads + tid;
+      S.keys[0][li] =
+          (unsigned)((spread3(quantize(px[j], l3[0], scale, top)) << 2) |
+                     (spread3(quantize(py[j], l3[1], scale, top)) << 1) |
+                     spread3(quantize(pz[j], l3[2], scale, top)));
+      S.vals[0][li] = base + li;
+    }
+  }
+
+  // 3. stable LSD radix passes over 8-bit digits
+  const int passes = (3 * bits + 7) / 8;
+  int cur = 0;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = 8 * pass;
+    if (tid < 256) {
+      S.hist[tid] = 0;
+      S.cnt[tid] = 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kCItems; ++j) {
+      const int li = j * kCThreads + tid;
+      if (base + li < n) atomicAdd(&S.hist[(S.keys[cur][li] >> shift) & 255], 1);
+    }
+    cluster.sync();  // every tile's histogram complete
+    if (tid < 256) {
+      // digits below tid over the whole tree, plus digit tid in lower tiles
+      int below = 0, total = 0;
+      for (int c = 0; c < cs; ++c) {
+        const int v = cluster.map_shared_rank(S.hist, c)[tid];
+        total += v;
+        if (c < rank) below += v;
+      }
+      int incl = total;  // inclusive scan of totals over digits (8 warps)
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (lane == 31) S.wsum[warp][0] = incl;
+      S.goff[tid] = incl - total + below;
+    }
+    __syncthreads();
+    if (tid < 256) {
+      int add = 0;
+      for (int w = 0; w < warp; ++w) add += S.wsum[w][0];
+      S.goff[tid] += add;
+    }
+    __syncthreads();
+    const int nxt = cur ^ 1;
+    for (int j = 0; j < kCItems; ++j) {
+      const int li = j * kCThreads + tid;
+      const bool valid = base + li < n;
+      const unsigned key = S.keys[cur][li];
+      const int val = S.vals[cur][li];
+      const int digit = valid ? (int)((key >> shift) & 255) : 256 + lane;
+      const unsigned peers = __match_any_sync(kFull, digit);
+      const int lower = __popc(peers & ((1u << lane) - 1u));
+      if (valid && lower == 0) S.wcnt[warp][digit] = __popc(peers);
+      __syncthreads();
+      if (valid) {
+        int r = S.goff[digit] + S.cnt[digit] + lower;
+        for (int w = 0; w < warp; ++w) r += S.wcnt[w][digit];
+        ClusterSmem* dst = cluster.map_shared_rank(&S, r / kCTile);
+        dst->keys[nxt][r % kCTile] = key;
+        dst->vals[nxt][r % kCTile] = val;
+      }
+      __syncthreads();
+      if (tid < 256) {
+        int sum = 0;
+        for (int w = 0; w < kCWarps; ++w) {
+          sum += S.wcnt[w][tid];
+          S.wcnt[w][tid] = 0;
+        }
+        S.cnt[tid] += sum;
+      }
+      __syncthreads();
+    }
+    cluster.sync();  // every scatter landed; hist/goff free again
+    cur = nxt;
+  }
+
+  // 4. sorted keys and indices out; per level the members before each
+  // position (member_count + member_prefix of the multi-launch path)
+  int ids[kCItems];
+#pragma unroll
+  for (int j = 0; j < kCItems; ++j) {
+    const int li = j * kCThreads + tid;
+    ids[j] = S.vals[cur][li];
+    if (base + li < n) {
+      keys_out[d.p0 + base + li] = S.keys[cur][li];
+      vals_out[d.p0 + base + li] = ids[j];
+    }
+  }
+  if (levels > 1) {
+    // tile order is row-major (position j*512 + tid): a member's offset is
+    // the members of the lower tiles, of the earlier (row, warp) groups of
+    // this tile, and of the lower lanes of its warp
+    int inwarp[kCItems][kMaxLevels];
+#pragma unroll
+    for (int j = 0; j < kCItems; ++j) {
+      const int li = j * kCThreads + tid;
+#pragma unroll
+      for (int l = 1; l < kMaxLevels; ++l) {
+        const bool m = l < levels && base + li < n && ids[j] < level_size(n, l);
+        const unsigned bal = __ballot_sync(kFull, m);
+        inwarp[j][l] = __popc(bal & ((1u << lane) - 1u));
+        if (lane == 0) S.grp[j][warp][l] = __popc(bal);
+      }
+    }
+    __syncthreads();
+    if (tid >= 1 && tid < levels) {  // exclusive scan over (row, warp) groups
+      int run = 0;
+      for (int j = 0; j < kCItems; ++j)
+        for (int w = 0; w < kCWarps; ++w) {
+          const int c = S.grp[j][w][tid];
+          S.grp[j][w][tid] = run;
+          run += c;
+        }
+      S.lcnt[tid] = run;
+    }
+    cluster.sync();  // tile totals visible to the cluster
+    int below[kMaxLevels] = {0, 0, 0, 0};
+    for (int c = 0; c < rank; ++c) {
+      const int* rl = cluster.map_shared_rank(S.lcnt, c);
+      for (int l = 1; l < kMaxLevels; ++l) below[l] += rl[l];
+    }
+#pragma unroll
+    for (int j = 0; j < kCItems; ++j) {
+      const int li = j * kCThreads + tid;
+      if (base + li >= n) continue;
+#pragma unroll
+      for (int l = 1; l < kMaxLevels; ++l) {
+        if (l >= levels) break;
+        pref[(size_t)(l - 1) * N + d.p0 + base + li] =
+            below[l] + S.grp[j][warp][l] + inwarp[j][l];
+      }
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may read its shared memory
 }
 
 // ---------------------------------------------------------------------------
@@ -858,6 +1111,38 @@ cudaError_t free_scratch(BuildScratch* sc, cudaStream_t s) {
   return e;
 }
 
+cudaError_t launch_cluster_sort(const Forest* f, const float* x,
+                                const BuildScratch& sc, cudaStream_t s) {
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e) return e;
+  const unsigned long long bit = 1ull << (device & 63);
+  if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(cluster_sort_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(ClusterSmem));
+    if (e) return e;
+    attr_set.fetch_or(bit, std::memory_order_relaxed);
+  }
+  const int cs = blocks_for(f->max_n, kCTile);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs, f->B);
+  cfg.blockDim = dim3(kCThreads);
+  cfg.dynamicSmemBytes = sizeof(ClusterSmem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, cluster_sort_kernel, f->desc, x,
+                            morton_bits(f->max_n), f->levels, sc.keys,
+                            sc.vals, sc.pref, f->N);
+}
+
 // Enqueues every build kernel of `f` over points `x` (the layout in f->hdesc)
 // using the temporaries in `sc`.  Allocates nothing.
 cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
@@ -883,7 +1168,15 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
   int launches = (B + 255) / 256;
   dim3 gs(max_tiles, B);
   dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-  {
+  if (GSA_CLUSTER_SORT && max_n <= kClusterMaxPoints) {
+    // one cluster per tree: bounds, keys, sort and member offsets
+    e = launch_cluster_sort(f, x, sc, s);
+    if (e) return e;
+    karras_kernel<<<gk, 256, 0, s>>>(f->desc, sc.keys, sc.parent, counter,
+                                     f->leaf, sc.leaves, leaf_count, sc.starts,
+                                     start_count);
+    launches += 2;
+  } else {
     dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
     bounds_kernel<<<g, 256, 0, s>>>(f->desc, x, sc.bounds);
     dim3 gm(std::min(blocks_for(max_n, 256 * kUnroll), 1024), B);
