@@ -382,6 +382,8 @@ __global__ void __launch_bounds__(kCThreads)
     }
   }
   if (tid < 6) S.bnd[tid] = tid < 3 ? ~0u : 0u;
+  // per-warp digit counters start at zero (each item row clears them after)
+  for (int e = tid; e < kCWarps * 256; e += kCThreads) (&S.wcnt[0][0])[e] = 0;
   __syncthreads();
   for (int k = 0; k < 3; ++k) {
     lo[k] = __reduce_min_sync(kFull, lo[k]);
@@ -475,9 +477,14 @@ __global__ void __launch_bounds__(kCThreads)
       const int lower = __popc(peers & ((1u << lane) - 1u));
       if (valid && lower == 0) S.wcnt[warp][digit] = __popc(peers);
       __syncthreads();
+      int r = 0;
       if (valid) {
-        int r = S.goff[digit] + S.cnt[digit] + lower;
+        r = S.goff[digit] + S.cnt[digit] + lower;
         for (int w = 0; w < warp; ++w) r += S.wcnt[w][digit];
+      }
+      // r < n by construction; the check keeps a corrupted count from
+      // addressing a CTA outside the cluster
+      if (valid && r >= 0 && r < n) {
         ClusterSmem* dst = cluster.map_shared_rank(&S, r / kCTile);
         dst->keys[nxt][r % kCTile] = key;
         dst->vals[nxt][r % kCTile] = val;
