@@ -317,10 +317,13 @@ __global__ void __launch_bounds__(kSortThreads)
 // ---------------------------------------------------------------------------
 // Trees of up to kClusterMaxPoints points: bounds, Morton keys, the four
 // radix passes and the per-level member offsets in ONE launch.  A thread-block
-// cluster owns one tree, each CTA a tile of kCTile consecutive positions held
-// in its shared memory; the CTAs exchange bounds, digit histograms and member
-// counts through distributed shared memory and scatter keys straight into the
-// destination CTA's next buffer, with a cluster barrier between steps.  The
+// cluster owns one tree, each CTA a tile of kCTile consecutive positions; the
+// CTAs exchange bounds, digit histograms and member counts through
+// distributed shared memory and scatter keys straight into the destination
+// CTA's buffer, with cluster barriers between the steps.  Inside a tile each
+// warp owns kCItems * 32 consecutive positions, so a warp ranks its items
+// against its own running digit counts (match_any, no block barrier per
+// item row) and one scan over the warps per digit places them.  The
 // multi-launch path (bounds_kernel ... member_prefix, 14 launches) does the
 // same work for larger trees.  Keys are at most 30 bits here (morton_bits of
 // n <= 32768 is 10), so they live in shared memory as 32-bit words; the output
@@ -333,17 +336,21 @@ constexpr int kClusterMaxPoints = kClusterMax * kCTile;
 constexpr int kCWarps = kCThreads / 32;
 
 struct ClusterSmem {
-  unsigned keys[2][kCTile];
-  int vals[2][kCTile];
-  int wcnt[kCWarps][256];  // per-warp digit counts of one item row
+  unsigned keys[kCTile];   // the tile's keys in position order (scatter target)
+  int vals[kCTile];
+  int wcnt[kCWarps][256];  // per-warp digit counts, then their exclusive scan
   int hist[256];           // this tile's digit counts (read by the cluster)
   int goff[256];
-  int cnt[256];
   unsigned bnd[6];         // this tile's bounds keys (read by the cluster)
   int lcnt[kMaxLevels];    // this tile's member counts (read by the cluster)
-  int wsum[kCWarps][kMaxLevels];
-  int grp[kCItems][kCWarps][kMaxLevels];  // member counts per (row, warp)
+  int wsum[kCWarps];
+  int wmem[kCWarps][kMaxLevels];  // members per warp, then their exclusive scan
 };
+
+// Position of item j of a lane inside its CTA's tile (warp-major).
+__device__ __forceinline__ int cpos(int warp, int j, int lane) {
+  return warp * (kCItems * 32) + j * 32 + lane;
+}
 
 __global__ void __launch_bounds__(kCThreads)
     cluster_sort_kernel(const TreeDesc* desc, const float* x, int bits,
@@ -357,6 +364,7 @@ __global__ void __launch_bounds__(kCThreads)
   const TreeDesc d = desc[blockIdx.y];
   const int n = d.n;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned lt = (1u << lane) - 1u;
   const int base = rank * kCTile;
 
   // 1. bounds of the finite points (order-preserving keys, as bounds_kernel)
@@ -364,7 +372,7 @@ __global__ void __launch_bounds__(kCThreads)
   unsigned lo[3] = {~0u, ~0u, ~0u}, hi[3] = {0u, 0u, 0u};
 #pragma unroll
   for (int j = 0; j < kCItems; ++j) {
-    const int i = base + j * kCThreads + tid;
+    const int i = base + cpos(warp, j, lane);
     px[j] = py[j] = pz[j] = NAN;
     if (i < n) {
       const float* q = x + 3ll * (d.p0 + i);
@@ -382,8 +390,6 @@ __global__ void __launch_bounds__(kCThreads)
     }
   }
   if (tid < 6) S.bnd[tid] = tid < 3 ? ~0u : 0u;
-  // per-warp digit counters start at zero (each item row clears them after)
-  for (int e = tid; e < kCWarps * 256; e += kCThreads) (&S.wcnt[0][0])[e] = 0;
   __syncthreads();
   for (int k = 0; k < 3; ++k) {
     lo[k] = __reduce_min_sync(kFull, lo[k]);
@@ -405,7 +411,9 @@ __global__ void __launch_bounds__(kCThreads)
     }
   }
 
-  // 2. Morton keys (as morton_kernel) and local indices, in tile order
+  // 2. Morton keys (as morton_kernel) and local indices, in registers
+  unsigned key[kCItems];
+  int val[kCItems];
   {
     const unsigned top = (1u << bits) - 1u;
     const bool any = bk[0] != 0xffffffffu;
@@ -418,31 +426,44 @@ __global__ void __launch_bounds__(kCThreads)
     const float scale = (ext > 0.f && isfinite(ext)) ? (float)top / ext : 0.f;
 #pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      const int li = j * kCThreads + tid;
-      S.keys[0][li] =
-          (unsigned)((spread3(quantize(px[j], l3[0], scale, top)) << 2) |
-                     (spread3(quantize(py[j], l3[1], scale, top)) << 1) |
-                     spread3(quantize(pz[j], l3[2], scale, top)));
-      S.vals[0][li] = base + li;
+      key[j] = (unsigned)((spread3(quantize(px[j], l3[0], scale, top)) << 2) |
+                          (spread3(quantize(py[j], l3[1], scale, top)) << 1) |
+                          spread3(quantize(pz[j], l3[2], scale, top)));
+      val[j] = base + cpos(warp, j, lane);
     }
   }
 
-  // 3. stable LSD radix passes over 8-bit digits
+  // 3. stable LSD radix passes over 8-bit digits.  Item j of a lane sits at
+  // tile position cpos(warp, j, lane) at the start of every pass.
   const int passes = (3 * bits + 7) / 8;
-  int cur = 0;
   for (int pass = 0; pass < passes; ++pass) {
     const int shift = 8 * pass;
-    if (tid < 256) {
-      S.hist[tid] = 0;
-      S.cnt[tid] = 0;
-    }
-    __syncthreads();
+    int* wc = S.wcnt[warp];
+    for (int e = lane; e < 256; e += 32) wc[e] = 0;
+    __syncwarp();
+    int rk[kCItems];
 #pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      const int li = j * kCThreads + tid;
-      if (base + li < n) atomicAdd(&S.hist[(S.keys[cur][li] >> shift) & 255], 1);
+      const bool valid = base + cpos(warp, j, lane) < n;
+      const int digit = valid ? (int)((key[j] >> shift) & 255) : 256 + lane;
+      const unsigned peers = __match_any_sync(kFull, digit);
+      const int lower = __popc(peers & lt);
+      rk[j] = valid ? wc[digit] + lower : 0;
+      __syncwarp();
+      if (valid && lower == 0) wc[digit] += __popc(peers);
+      __syncwarp();
     }
-    cluster.sync();  // every tile's histogram complete
+    __syncthreads();
+    if (tid < 256) {  // tile histogram; per digit, warps' exclusive offsets
+      int run = 0;
+      for (int w = 0; w < kCWarps; ++w) {
+        const int c = S.wcnt[w][tid];
+        S.wcnt[w][tid] = run;
+        run += c;
+      }
+      S.hist[tid] = run;
+    }
+    cluster.sync();  // every tile's histogram complete, every buffer read
     if (tid < 256) {
       // digits below tid over the whole tree, plus digit tid in lower tiles
       int below = 0, total = 0;
@@ -456,108 +477,81 @@ __global__ void __launch_bounds__(kCThreads)
         const int u = __shfl_up_sync(kFull, incl, o);
         if (lane >= o) incl += u;
       }
-      if (lane == 31) S.wsum[warp][0] = incl;
+      if (lane == 31) S.wsum[warp] = incl;
       S.goff[tid] = incl - total + below;
     }
     __syncthreads();
     if (tid < 256) {
       int add = 0;
-      for (int w = 0; w < warp; ++w) add += S.wsum[w][0];
+      for (int w = 0; w < warp; ++w) add += S.wsum[w];
       S.goff[tid] += add;
     }
     __syncthreads();
-    const int nxt = cur ^ 1;
+#pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      const int li = j * kCThreads + tid;
-      const bool valid = base + li < n;
-      const unsigned key = S.keys[cur][li];
-      const int val = S.vals[cur][li];
-      const int digit = valid ? (int)((key >> shift) & 255) : 256 + lane;
-      const unsigned peers = __match_any_sync(kFull, digit);
-      const int lower = __popc(peers & ((1u << lane) - 1u));
-      if (valid && lower == 0) S.wcnt[warp][digit] = __popc(peers);
-      __syncthreads();
-      int r = 0;
-      if (valid) {
-        r = S.goff[digit] + S.cnt[digit] + lower;
-        for (int w = 0; w < warp; ++w) r += S.wcnt[w][digit];
-      }
+      const bool valid = base + cpos(warp, j, lane) < n;
+      if (!valid) continue;
+      const int digit = (int)((key[j] >> shift) & 255);
+      const int r = S.goff[digit] + wc[digit] + rk[j];
       // r < n by construction; the check keeps a corrupted count from
       // addressing a CTA outside the cluster
-      if (valid && r >= 0 && r < n) {
+      if (r >= 0 && r < n) {
         ClusterSmem* dst = cluster.map_shared_rank(&S, r / kCTile);
-        dst->keys[nxt][r % kCTile] = key;
-        dst->vals[nxt][r % kCTile] = val;
+        dst->keys[r % kCTile] = key[j];
+        dst->vals[r % kCTile] = val[j];
       }
-      __syncthreads();
-      if (tid < 256) {
-        int sum = 0;
-        for (int w = 0; w < kCWarps; ++w) {
-          sum += S.wcnt[w][tid];
-          S.wcnt[w][tid] = 0;
-        }
-        S.cnt[tid] += sum;
-      }
-      __syncthreads();
     }
-    cluster.sync();  // every scatter landed; hist/goff free again
-    cur = nxt;
+    cluster.sync();  // every scatter landed
+#pragma unroll
+    for (int j = 0; j < kCItems; ++j) {
+      key[j] = S.keys[cpos(warp, j, lane)];
+      val[j] = S.vals[cpos(warp, j, lane)];
+    }
   }
 
   // 4. sorted keys and indices out; per level the members before each
   // position (member_count + member_prefix of the multi-launch path)
-  int ids[kCItems];
 #pragma unroll
   for (int j = 0; j < kCItems; ++j) {
-    const int li = j * kCThreads + tid;
-    ids[j] = S.vals[cur][li];
-    if (base + li < n) {
-      keys_out[d.p0 + base + li] = S.keys[cur][li];
-      vals_out[d.p0 + base + li] = ids[j];
+    const int i = base + cpos(warp, j, lane);
+    if (i < n) {
+      keys_out[d.p0 + i] = key[j];
+      vals_out[d.p0 + i] = val[j];
     }
   }
   if (levels > 1) {
-    // tile order is row-major (position j*512 + tid): a member's offset is
-    // the members of the lower tiles, of the earlier (row, warp) groups of
-    // this tile, and of the lower lanes of its warp
-    int inwarp[kCItems][kMaxLevels];
+    for (int l = 1; l < kMaxLevels; ++l) {
+      int run = 0;
 #pragma unroll
-    for (int j = 0; j < kCItems; ++j) {
-      const int li = j * kCThreads + tid;
-#pragma unroll
-      for (int l = 1; l < kMaxLevels; ++l) {
-        const bool m = l < levels && base + li < n && ids[j] < level_size(n, l);
-        const unsigned bal = __ballot_sync(kFull, m);
-        inwarp[j][l] = __popc(bal & ((1u << lane) - 1u));
-        if (lane == 0) S.grp[j][warp][l] = __popc(bal);
+      for (int j = 0; j < kCItems; ++j) {
+        const bool m = l < levels && base + cpos(warp, j, lane) < n &&
+                       val[j] < level_size(n, l);
+        run += __popc(__ballot_sync(kFull, m));
       }
+      if (lane == 0) S.wmem[warp][l] = run;
     }
     __syncthreads();
-    if (tid >= 1 && tid < levels) {  // exclusive scan over (row, warp) groups
+    if (tid >= 1 && tid < kMaxLevels) {  // exclusive scan over the warps
       int run = 0;
-      for (int j = 0; j < kCItems; ++j)
-        for (int w = 0; w < kCWarps; ++w) {
-          const int c = S.grp[j][w][tid];
-          S.grp[j][w][tid] = run;
-          run += c;
-        }
+      for (int w = 0; w < kCWarps; ++w) {
+        const int c = S.wmem[w][tid];
+        S.wmem[w][tid] = run;
+        run += c;
+      }
       S.lcnt[tid] = run;
     }
     cluster.sync();  // tile totals visible to the cluster
-    int below[kMaxLevels] = {0, 0, 0, 0};
-    for (int c = 0; c < rank; ++c) {
-      const int* rl = cluster.map_shared_rank(S.lcnt, c);
-      for (int l = 1; l < kMaxLevels; ++l) below[l] += rl[l];
-    }
+    for (int l = 1; l < kMaxLevels; ++l) {
+      if (l >= levels) break;
+      int run = S.wmem[warp][l];
+      for (int c = 0; c < rank; ++c) run += cluster.map_shared_rank(S.lcnt, c)[l];
 #pragma unroll
-    for (int j = 0; j < kCItems; ++j) {
-      const int li = j * kCThreads + tid;
-      if (base + li >= n) continue;
-#pragma unroll
-      for (int l = 1; l < kMaxLevels; ++l) {
-        if (l >= levels) break;
-        pref[(size_t)(l - 1) * N + d.p0 + base + li] =
-            below[l] + S.grp[j][warp][l] + inwarp[j][l];
+      for (int j = 0; j < kCItems; ++j) {
+        const int i = base + cpos(warp, j, lane);
+        const bool m = i < n && val[j] < level_size(n, l);
+        const unsigned bal = __ballot_sync(kFull, m);
+        if (i < n) pref[(size_t)(l - 1) * N + d.p0 + i] = run + __popc(bal & lt);
+        run += __popc(bal);
       }
     }
   }
