@@ -235,3 +235,26 @@ GSA_API int reuse_rows_batch(int count, const int* src, long long src_stride,
       src, src_stride, src_ld, flags, rows, cols, dst, dst_stride, hits);
   return cudaGetLastError();
 }
+
+// See include/gsa_bvh.h.
+GSA_API int session_lookup(int count, const float* const* a,
+                           const float* const* b, const long long* nfloat,
+                           int nmemo, const int* const* cached, int src_ld,
+                           int rows, int cols, int* dst, int* flags,
+                           int* flags_host, void* stream) {
+  if (count < 1 || nmemo < 0 || 2 * nmemo > count || nmemo > kMaxPairs ||
+      !flags || !flags_host)
+    return -2;
+  int code = coords_mismatch(count, a, b, nfloat, flags, stream);
+  if (code) return code;
+  if (nmemo) {
+    code = reuse_rows(nmemo, cached, flags, src_ld, rows, cols, dst, nullptr,
+                      stream);
+    if (code) return code;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(flags_host, flags, sizeof(int) * count,
+                                  cudaMemcpyDeviceToHost, s);
+  if (!e) e = cudaStreamSynchronize(s);
+  return (int)e;
+}

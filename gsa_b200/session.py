@@ -11,10 +11,11 @@ equals a stored root prefix of length ``N, N/4, N/16, N/64``
 (``gsa/session.py:65-71``).
 
 B200 difference: the reference tests each candidate with ``torch.equal`` (a
-kernel and a host synchronisation per comparison).  Here one call evaluates
-all of its candidate comparisons in a single launch, gathers the hit rows on
-the device in the same stream, and synchronises once to read the flags; the
-statistics replay the reference's short-circuit order over those flags, so
+kernel and a host synchronisation per comparison).  Here one native call
+(``session_lookup``) evaluates all of a call's candidate comparisons in a
+single launch, gathers the hit rows on the device in the same stream and
+returns the flags after one synchronisation; the statistics replay the
+reference's short-circuit order over those flags, so
 ``coordinate_comparisons`` and the other counters stay identical.
 """
 
@@ -37,12 +38,50 @@ er.lib.reuse_rows.argtypes = [_I, _P, _P, _I, _I, _I, _P, _P, _P]
 er.lib.reuse_rows.restype = _I
 er.lib.gather_rows.argtypes = [_P, _I, _I, _I, _P, _P]
 er.lib.gather_rows.restype = _I
+er.lib.session_lookup.argtypes = [_I, _P, _P, _P, _I, _P, _I, _I, _I, _P, _P, _P, _P]
+er.lib.session_lookup.restype = _I
+_LOOKUP_MAX = 128  # pairs per session_lookup call (device flag buffer size)
+
+
 class _CudaOps:
     """Device side of the session: comparisons, row gathers, trees."""
 
     lib = er.lib
 
     current = staticmethod(current_stream)
+
+    def __init__(self):
+        self._dflags = None
+        self._hflags = (ctypes.c_int * _LOOKUP_MAX)()
+
+    def lookup(self, pairs, cached, rows, cols, out, device):
+        """Compare every pair (a, b): a against the first a.numel() values
+        of b; when ``cached`` is given (memo rows, pairs 2c / 2c+1 belonging
+        to candidate c), copy the first fully matching candidate's rows into
+        ``out`` on the device; return the host flags (1 = differs).  One
+        native call and one synchronisation (session_lookup)."""
+        n = len(pairs)
+        if n > _LOOKUP_MAX or len(cached) > _MAX_DEVICE_CANDIDATES:
+            flags = self.fetch(self.mismatch([(a, b[: a.shape[0]]) for a, b in pairs], device))
+            for c, rows_c in enumerate(cached):
+                if not (flags[2 * c] or flags[2 * c + 1]):
+                    self.copy_cols(out, rows_c, cols)
+                    break
+            return flags
+        if self._dflags is None:
+            self._dflags = torch.empty(_LOOKUP_MAX, dtype=torch.int32, device=device)
+        a = (ctypes.c_void_p * n)(*[p[0].data_ptr() for p in pairs])
+        b = (ctypes.c_void_p * n)(*[p[1].data_ptr() for p in pairs])
+        c = (ctypes.c_longlong * n)(*[p[0].numel() for p in pairs])
+        m = len(cached)
+        src = (ctypes.c_void_p * max(1, m))(*[t.data_ptr() for t in cached])
+        er.check(
+            self.lib.session_lookup(
+                n, a, b, c, m, src, 32, rows, cols, out.data_ptr() if m else None,
+                self._dflags.data_ptr(), self._hflags, _stream(),
+            )
+        )
+        return self._hflags[:n]
 
     @staticmethod
     def on_device(x, device):
@@ -186,8 +225,8 @@ class QuerySession:
         candidates = self._tree_candidates(x)
         flags = []
         if candidates:
-            pairs = [(x, root[: x.shape[0]]) for root, _ in candidates]
-            flags = self._ops.fetch(self._ops.mismatch(pairs, x.device))
+            pairs = [(x, root) for root, _ in candidates]
+            flags = self._ops.lookup(pairs, [], 0, 1, None, x.device)
         return self._pick_tree(x, candidates, flags)
 
     # -- public API ------------------------------------------------------
@@ -214,18 +253,14 @@ class QuerySession:
             return
         memo = [e for e in self.memo if e[2] == r and n == e[0].shape[0] and nq <= e[1].shape[0]]
         trees = self._tree_candidates(x) if n > self.threshold else []
+        # pairs (a, b): a against the first a.numel() values of b
         pairs = []
         for saved_x, saved_q, _, _ in memo:
-            pairs += [(x, saved_x), (q, saved_q[:nq])]
-        pairs += [(x, root[:n]) for root, _ in trees]
+            pairs += [(x, saved_x), (q, saved_q)]
+        pairs += [(x, root) for root, _ in trees]
         flags = []
-        device_reuse = False
         if pairs:
-            dflags = self._ops.mismatch(pairs, q.device)
-            device_reuse = 0 < len(memo) <= _MAX_DEVICE_CANDIDATES
-            if device_reuse:
-                self._ops.reuse([e[3] for e in memo], dflags, nq, k, out)
-            flags = self._ops.fetch(dflags)
+            flags = self._ops.lookup(pairs, [e[3] for e in memo], nq, k, out, q.device)
         # Replay of the reference memo scan (gsa/session.py:104-114).
         for i, entry in enumerate(memo):
             self.stats["coordinate_comparisons"] += 1
@@ -234,8 +269,7 @@ class QuerySession:
             self.stats["coordinate_comparisons"] += 1
             if flags[2 * i + 1]:
                 continue
-            if not device_reuse:
-                self._ops.copy_cols(out, entry[3], k)
+            # the lookup copied this entry's rows into out on the device
             self.stats["ball_hits"] += 1
             return
         cap = 32

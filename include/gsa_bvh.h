@@ -182,6 +182,19 @@ int reuse_lookup_static(int count, const float* x, long long nx,
                         int src_ld, int rows, int cols, int* dst, int* hit,
                         void* stream);
 
+/* One QuerySession admission step in one call (the comparisons and row copy
+ * of gsa/session.py:65-71 and :104-114, which the reference runs as one
+ * torch.equal plus host synchronisation per candidate): compares every pair
+ * as coords_mismatch does (flags: count device ints, 1 = differs), then,
+ * when nmemo > 0, copies the rows of the first memo candidate c whose pairs
+ * 2c and 2c+1 both match, as reuse_rows does (nmemo <= 64, pairs 0..2*nmemo-1
+ * are the memo pairs), then copies the flags to flags_host (count host
+ * ints) and waits for the stream.  Returns 0, a cudaError_t, or -2. */
+int session_lookup(int count, const float* const* a, const float* const* b,
+                   const long long* nfloat, int nmemo,
+                   const int* const* cached, int src_ld, int rows, int cols,
+                   int* dst, int* flags, int* flags_host, void* stream);
+
 /* Farthest-point order of b scenes of n points each (x is [b][n][3]),
  * starting at start[b] (device int[b]); order is device int[b][n].  Ties pick
  * the lowest index; chosen points are never repeated.  Input generator for

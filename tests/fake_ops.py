@@ -55,6 +55,14 @@ class OracleOps:
     def on_device(x, device):
         return not x.is_cuda
 
+    def lookup(self, pairs, cached, rows, cols, out, device):
+        flags = [0 if torch.equal(a, b[: a.shape[0]]) else 1 for a, b in pairs]
+        for c, rows_c in enumerate(cached):
+            if not (flags[2 * c] or flags[2 * c + 1]):
+                out.copy_(rows_c[:rows, :cols])
+                break
+        return flags
+
     def mismatch(self, pairs, device):
         return torch.tensor([0 if torch.equal(a, b) else 1 for a, b in pairs], dtype=torch.int32)
 
