@@ -132,6 +132,37 @@ class _CudaOps:
             )
         )
 
+    # Direct native calls for the session's own default paths: the session
+    # has already validated every argument, so these skip the public
+    # wrappers' re-validation and the (1, N, 3) views.
+    _ref_lib = rt.lib
+
+    def scan_ball(self, n, nq, r, cap, q, x, out):
+        code = self._ref_lib.ball(1, n, nq, r, cap, q.data_ptr(), x.data_ptr(), out.data_ptr(), _stream())
+        if code:
+            raise RuntimeError(f"ball: CUDA error {code}")
+
+    def scan_nn(self, nq, n, q, x, d, ids):
+        code = self._ref_lib.nn3(1, nq, n, q.data_ptr(), x.data_ptr(), d.data_ptr(), ids.data_ptr(), _stream())
+        if code:
+            raise RuntimeError(f"nn3: CUDA error {code}")
+
+    def tree_ball(self, tree, q, m, r, cap, out):
+        er.check(
+            self.lib.query_ball_bvh(
+                tree.ptr, q.data_ptr(), q.shape[0], m, tree.level(m), r, cap,
+                out.data_ptr(), tree.fallback.data_ptr(), _stream(),
+            )
+        )
+
+    def tree_query(self, tree, q, m, d, ids):
+        er.check(
+            self.lib.query_bvh(
+                tree.ptr, q.data_ptr(), q.shape[0], m, tree.level(m), d.data_ptr(),
+                ids.data_ptr(), tree.fallback.data_ptr(), _stream(),
+            )
+        )
+
     @staticmethod
     def zeros(rows, device):
         return torch.zeros((rows, 32), device=device, dtype=torch.int32)
@@ -167,6 +198,8 @@ class QuerySession:
         self.device, self.stream = self._ops.current()
         self.ball_reference = ball_reference or self._ops.default_ball
         self.nn_reference = nn_reference or self._ops.default_nn
+        self._own_ball = ball_reference is None
+        self._own_nn = nn_reference is None
         self.threshold = threshold
         self.trees = []
         self.memo = []
@@ -189,15 +222,22 @@ class QuerySession:
         self.stats["snapshot_bytes"] += y.numel() * y.element_size()
         return y
 
-    def _check(self, x):
+    def _check2(self, x, q):
+        """_check of both tensors with one read of the current stream."""
+        ops = self._ops
         if not (
             not self.closed
             and x.ndim == 2
             and x.shape[1] == 3
             and x.is_contiguous()
             and x.dtype == torch.float32
-            and self._ops.on_device(x, self.device)
-            and self._ops.current() == (self.device, self.stream)
+            and q.ndim == 2
+            and q.shape[1] == 3
+            and q.is_contiguous()
+            and q.dtype == torch.float32
+            and ops.on_device(x, self.device)
+            and ops.on_device(q, self.device)
+            and ops.current() == (self.device, self.stream)
         ):
             raise ValueError(
                 "Use an open session with contiguous FP32 (N,3) tensors on its original CUDA device and stream"
@@ -221,7 +261,6 @@ class QuerySession:
         return tree
 
     def _tree(self, x):
-        self._check(x)
         candidates = self._tree_candidates(x)
         flags = []
         if candidates:
@@ -231,8 +270,7 @@ class QuerySession:
 
     # -- public API ------------------------------------------------------
     def ball_into(self, q, x, r, k, out):
-        self._check(x)
-        self._check(q)
+        self._check2(x, q)
         n, nq = x.shape[0], q.shape[0]
         if not (
             n >= 1
@@ -240,7 +278,7 @@ class QuerySession:
             and 1 <= k <= 32
             and out.shape == (nq, k)
             and out.dtype == torch.int32
-            and out.device == q.device
+            and self._ops.on_device(out, self.device)
             and out.is_contiguous()
             and math.isfinite(r)
             and 0 <= r <= _FLT_MAX
@@ -277,12 +315,15 @@ class QuerySession:
             # the scan leaves rows without a hit untouched: start from zeros
             result = self._ops.zeros(nq, q.device)
             owned_x = self._snapshot(x)
-            self.ball_reference(1, n, nq, r, cap, q[None], owned_x[None], result[None])
+            if self._own_ball:
+                self._ops.scan_ball(n, nq, r, cap, q, owned_x, result)
+            else:
+                self.ball_reference(1, n, nq, r, cap, q[None], owned_x[None], result[None])
         else:
             result = self._ops.rows(nq, q.device)
             tree = self._pick_tree(x, trees, flags[2 * len(memo):])
             owned_x = tree.x[:n]
-            tree.ball(q, n, r, cap, result)
+            self._ops.tree_ball(tree, q, n, r, cap, result)
         if q.data_ptr() == x.data_ptr() and nq == n:
             # a self-query: the query snapshot would be a second copy of the
             # support snapshot's values, so the entry shares it (snapshots
@@ -296,15 +337,15 @@ class QuerySession:
         self._ops.copy_cols(out, result, k)
 
     def nn_into(self, q, x, d, ids):
-        self._check(x)
-        self._check(q)
+        self._check2(x, q)
         n, nq = x.shape[0], q.shape[0]
         if not (
             n >= 3
             and d.shape == ids.shape == (nq, 3)
             and d.dtype == torch.float32
             and ids.dtype == torch.int32
-            and d.device == ids.device == q.device
+            and self._ops.on_device(d, self.device)
+            and self._ops.on_device(ids, self.device)
             and d.is_contiguous()
             and ids.is_contiguous()
         ):
@@ -315,9 +356,12 @@ class QuerySession:
         if not nq:
             return
         if n <= self.threshold:
-            self.nn_reference(1, nq, n, q[None], x[None], d[None], ids[None])
+            if self._own_nn:
+                self._ops.scan_nn(nq, n, q, x, d, ids)
+            else:
+                self.nn_reference(1, nq, n, q[None], x[None], d[None], ids[None])
         else:
-            self._tree(x).query(q, n, d, ids)
+            self._ops.tree_query(self._tree(x), q, n, d, ids)
 
     def close(self, collect=False):
         if self.closed:

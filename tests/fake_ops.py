@@ -82,6 +82,22 @@ class OracleOps:
         out.copy_(result[: out.shape[0], :k])
 
     @staticmethod
+    def scan_ball(n, nq, r, cap, q, x, out):
+        _ball_scan(1, n, nq, r, cap, q[None], x[None], out[None])
+
+    @staticmethod
+    def scan_nn(nq, n, q, x, d, ids):
+        _nn_scan(1, nq, n, q[None], x[None], d[None], ids[None])
+
+    @staticmethod
+    def tree_ball(tree, q, m, r, cap, out):
+        tree.ball(q, m, r, cap, out)
+
+    @staticmethod
+    def tree_query(tree, q, m, d, ids):
+        tree.query(q, m, d, ids)
+
+    @staticmethod
     def zeros(rows, device):
         return torch.zeros((rows, 32), dtype=torch.int32)
 
