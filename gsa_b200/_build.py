@@ -7,8 +7,7 @@
 answers every support size with the tree walk (the default library scans
 small prefixes), ``gsa_bvh_ordered.so`` does so with the per-query walks
 (ordered radius, nearest-first 3NN) instead of the packet-frontier kernels
-and builds every tree with the multi-launch sort and the device-scope climb
-instead of the cluster sort and the block climb,
+and builds every tree with the multi-launch sort instead of the cluster sort,
 and ``gsa_bvh_stack4.so`` has a 4-entry traversal stack (8-entry frontier)
 so that the per-query-walk and exact full-scan fallbacks are exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
@@ -49,7 +48,7 @@ LIBS = {
     # test variants: tree walks for every support size (packet frontier;
     # per-query walks); and the frontier with a 4-entry stack
     "gsa_bvh_walk": (_BVH, _WALK_ONLY),
-    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_FRONTIER=0", "-DGSA_KNN_FRONTIER=0", "-DGSA_CLUSTER_SORT=0", "-DGSA_CLIMB_CTA=0"]),
+    "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_FRONTIER=0", "-DGSA_KNN_FRONTIER=0", "-DGSA_CLUSTER_SORT=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
 }
 

@@ -40,11 +40,6 @@ namespace cg = cooperative_groups;
 #ifndef GSA_CLUSTER_SORT
 #define GSA_CLUSTER_SORT 1
 #endif
-// Trees of up to 49,152 points climb in one CTA each with block-scope
-// arrivals (climb_block_kernel); 0 keeps every tree on climb_kernel.
-#ifndef GSA_CLIMB_CTA
-#define GSA_CLIMB_CTA 1
-#endif
 
 namespace gsa {
 namespace {
@@ -734,35 +729,9 @@ __device__ __forceinline__ int arrive(int* p) {
 // children are level leaves holding at most `leaf` members together: the
 // members of a subtree are contiguous in the level's member array, the left
 // child's (slot 0 until this node swaps) first.
-// Arrival at a CTA-local counter in shared memory (climb_block_kernel): the
-// same acquire-release pattern as arrive() at block scope.
-__device__ __forceinline__ int arrive_cta(int* p) {
-  int old;
-  asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
-               : "=r"(old)
-               : "r"((unsigned)__cvta_generic_to_shared(p))
-               : "memory");
-  return old;
-}
-
-// Entry written earlier in this kernel by a thread of the same CTA (plain
-// coherent loads; ordered by arrive_cta).
-__device__ __forceinline__ Entry load_entry_cta(const Entry* e) {
-  const float4* p = reinterpret_cast<const float4*>(e);
-  float4 u = p[0], v = p[1];
-  Entry r;
-  r.lox = u.x; r.loy = u.y; r.loz = u.z; r.minid = __float_as_int(u.w);
-  r.hix = v.x; r.hiy = v.y; r.hiz = v.z; r.ref = __float_as_int(v.w);
-  return r;
-}
-
-// CTA: the tree's climbs all run in one CTA with its arrival counters in
-// shared memory (`scnt`); else the counters are in global memory.
-template <bool CTA>
-__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
-                      int* scnt = nullptr) {
+__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
   const int* par = a.parent + (d.p0 - b);
-  int* cnt = CTA ? scnt : a.counter + (d.p0 - b);
+  int* cnt = a.counter + (d.p0 - b);
   // Karras depth is below 97 (64 key bits + 32 index bits); the bound only
   // guards against a corrupted topology.
   for (int step = 0; step < 128; ++step) {
@@ -771,13 +740,8 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
       if (l < a.levels) {
-        if (CTA) {
-          u[l] = load_entry_cta(node_entry(a.nodes, d, l, i, 0));
-          v[l] = load_entry_cta(node_entry(a.nodes, d, l, i, 1));
-        } else {
-          u[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 0));
-          v[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 1));
-        }
+        u[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 0));
+        v[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 1));
       }
     }
     int pc = i ? par[i] : 0;
@@ -809,9 +773,7 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
       else
         store_entry(node_entry(a.nodes, d, l, pc >> 1, pc & 1), e);
     }
-    if (i == 0) return;
-    if ((CTA ? arrive_cta(cnt + (pc >> 1)) : arrive(cnt + (pc >> 1))) == 0)
-      return;
+    if (i == 0 || arrive(cnt + (pc >> 1)) == 0) return;
     i = pc >> 1;
   }
 }
@@ -918,28 +880,7 @@ __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
   int total = a.start_count[b];
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < total;
        r += gridDim.x * blockDim.x)
-    climb<false>(a, d, b, st[r]);
-}
-
-// Trees of up to kClimbCtaMax points: one 512-thread CTA per tree runs all
-// of the tree's climbs with the arrival counters copied into shared memory,
-// so each level's hand-over is a block-scope atomic instead of a device-scope
-// one (the climb is a chain of ~depth dependent steps).
-constexpr int kClimbThreads = 512;
-constexpr int kClimbCtaMax = 49152;  // counters: (n - 1) ints of shared memory
-
-__global__ void __launch_bounds__(kClimbThreads)
-    climb_block_kernel(RefitArgs a) {
-  extern __shared__ int scnt[];
-  const int b = blockIdx.x;
-  const TreeDesc d = a.desc[b];
-  const int* gcnt = a.counter + (d.p0 - b);
-  for (int i = threadIdx.x; i < d.n - 1; i += kClimbThreads) scnt[i] = gcnt[i];
-  __syncthreads();
-  const int* st = a.starts + (d.p0 - b);
-  const int total = a.start_count[b];
-  for (int r = threadIdx.x; r < total; r += kClimbThreads)
-    climb<true>(a, d, b, st[r], scnt);
+    climb(a, d, b, st[r]);
 }
 
 // One warp per (level, tree): the top of the level's tree expanded breadth
@@ -1171,22 +1112,20 @@ cudaError_t free_scratch(BuildScratch* sc, cudaStream_t s) {
   return e;
 }
 
-// Raises a kernel's dynamic shared-memory limit to `bytes` (a host-side
-// attribute; set again only when a larger size is needed).
-cudaError_t set_smem_attr(const void* fn, size_t bytes) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
-  cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, fn);
-  if (e) return e;
-  if ((size_t)fa.maxDynamicSharedSizeBytes >= bytes) return cudaSuccess;
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)bytes);
-}
-
 cudaError_t launch_cluster_sort(const Forest* f, const float* x,
                                 const BuildScratch& sc, cudaStream_t s) {
-  cudaError_t e = set_smem_attr((const void*)cluster_sort_kernel, sizeof(ClusterSmem));
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
   if (e) return e;
+  const unsigned long long bit = 1ull << (device & 63);
+  if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(cluster_sort_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(ClusterSmem));
+    if (e) return e;
+    attr_set.fetch_or(bit, std::memory_order_relaxed);
+  }
   const int cs = blocks_for(f->max_n, kCTile);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, f->B);
@@ -1298,14 +1237,7 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
     leaf_kernel<16><<<gl, 256, 0, s>>>(ra);
   else
     leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
-  if (GSA_CLIMB_CTA && max_n <= kClimbCtaMax) {
-    const size_t smem = sizeof(int) * std::max(1, max_n - 1);
-    e = set_smem_attr((const void*)climb_block_kernel, smem);
-    if (e) return e;
-    climb_block_kernel<<<B, kClimbThreads, smem, s>>>(ra);
-  } else {
-    climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
-  }
+  climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
   cut_kernel<<<dim3(f->levels, B), 32, 0, s>>>(f->desc, f->nodes, f->root,
                                                f->levels, f->cut);
   launches += 3;
