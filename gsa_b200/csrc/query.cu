@@ -787,6 +787,34 @@ __device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
   return false;
 }
 
+// Sorts h[0..count) ascending (count <= W) with a bitonic network over W
+// registers, the slots past count padded with INT_MAX.
+template <int W>
+__device__ __forceinline__ void sort_hits(int* h, int count) {
+  int v[W];
+#pragma unroll
+  for (int i = 0; i < W; ++i) v[i] = i < count ? h[i] : INT_MAX;
+#pragma unroll
+  for (int k = 2; k <= W; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < W; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const int lo = min(v[i], v[l]), hi = max(v[i], v[l]);
+          const bool up = (i & k) == 0;
+          v[i] = up ? lo : hi;
+          v[l] = up ? hi : lo;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < W; ++i)
+    if (i < count) h[i] = v[i];
+}
+
 template <int STACK>
 __global__ void __launch_bounds__(kFWarps * 32)
     radius_frontier_kernel(QArgs a) {
@@ -827,17 +855,15 @@ __global__ void __launch_bounds__(kFWarps * 32)
   int count = 0;
   if (!overflow) {
     bool spill = active && hc > kPacketCap;
-    if (active && !spill) {
-      for (int i = 1; i < hc; ++i) {  // ascending IDs
-        int v = H[i], pos = i;
-        while (pos > 0 && H[pos - 1] > v) {
-          H[pos] = H[pos - 1];
-          --pos;
-        }
-        H[pos] = v;
-      }
-      count = min(hc, c.K);
+    // ascending IDs: a sorting network in registers (no data-dependent
+    // branches), 16 wide when no lane of the warp holds more hits
+    const bool sorted_here = active && !spill;
+    if (__any_sync(kFull, sorted_here && hc > 16)) {
+      if (sorted_here) sort_hits<32>(H, hc);
+    } else if (sorted_here) {
+      sort_hits<16>(H, hc);
     }
+    if (sorted_here) count = min(hc, c.K);
     if (__any_sync(kFull, spill)) {
       // The buffer holds kPacketCap >= K hits, so the first K IDs are all at
       // most its largest ID: the walk starts with that bound.
