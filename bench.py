@@ -93,6 +93,9 @@ def parse():
     p.add_argument("--scenes", type=int, default=SCENES, help="scenes of the whole job")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--write-traffic-profile", metavar="NCU_CSV",
+                   help="write the DRAM traffic profile from an ncu --csv capture of the frontier "
+                        "kernels' first hierarchy run (see TRAFFIC_SOURCES) and exit")
     return p.parse_args()
 
 
@@ -421,6 +424,61 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+# Sources whose change invalidates a traffic profile: the query kernels and
+# the tree layout they read.
+TRAFFIC_SOURCES = ["query.cu", "common.cuh", "forest.cuh", "build.cu"]
+TRAFFIC_COMMAND = (
+    "ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum,smsp__inst_executed.sum "
+    "--clock-control none -k regex:frontier_kernel -c 6 --csv --log-file gpurun_out/dram.csv "
+    "python bench.py --steps 1 --warmup 3 --no-e2e --no-cpu-baseline"
+)
+
+
+def write_traffic_profile(csv_path):
+    """Per-query DRAM bytes of the frontier kernels from an ncu --csv capture
+    of TRAFFIC_COMMAND (the first hierarchy run: each kernel's launches are
+    stages 0, 1, 2 in order, over 64 scenes of SIZES[0..2] queries), written
+    with the SHA-256 of TRAFFIC_SOURCES so that bench lines use it only for
+    the code it was taken of."""
+    import csv
+
+    rows = []
+    with open(csv_path, newline="") as fh:
+        lines = [ln for ln in fh if ln.startswith('"')]
+    for r in csv.DictReader(lines):
+        rows.append(r)
+    per = {}
+    for r in rows:
+        # "void <unnamed>::radius_frontier_kernel<128>(<unnamed>::QArgs)"
+        name = r["Kernel Name"].split("(")[0]
+        while name.endswith(">"):  # template arguments
+            name = name[: name.rindex("<")]
+        name = name.split("::")[-1].split()[-1]
+        launch = per.setdefault(name, {}).setdefault(r["ID"], {})
+        unit = r.get("Metric Unit", "")
+        val = float(r["Metric Value"].replace(",", ""))
+        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "nsecond": 1, "usecond": 1e3,
+                 "msecond": 1e6}.get(unit, 1)
+        launch[r["Metric Name"]] = val * scale
+    out = {"command": TRAFFIC_COMMAND, "sources": TRAFFIC_SOURCES,
+           "sources_sha256": kernel_sources_sha(TRAFFIC_SOURCES), "kernels": {}}
+    for name, launches in per.items():
+        stages = [launches[k] for k in sorted(launches, key=int)][:3]
+        queries = [SCENES * SIZES[i] for i in range(len(stages))]
+        dram = [st["dram__bytes_read.sum"] + st["dram__bytes_write.sum"] for st in stages]
+        out["kernels"][name] = {
+            "dram_bytes_per_query": sum(dram) / sum(queries),
+            "per_stage": [
+                {"stage": i, "queries": q, "dram_bytes": d, "dram_bytes_per_query": d / q,
+                 "ncu_ns": st.get("gpu__time_duration.sum"),
+                 "warp_inst_per_32_queries": st.get("smsp__inst_executed.sum", 0) * 32 / q}
+                for i, (q, d, st) in enumerate(zip(queries, dram, stages))
+            ],
+        }
+    TRAFFIC_PROFILE.write_text(json.dumps(out, indent=1) + "\n")
+    print(json.dumps(out, indent=1))
+
+
 def kernel_sources_sha(names):
     h = hashlib.sha256()
     for n in names:
@@ -574,15 +632,16 @@ def run_ours(args, rank, world, local):
         "knn3_frontier_kernel": kernel_line(["nn0", "nn1", "nn2"], [0, 1, 2], 36),
         "knn3_scan_kernel": kernel_line(["nn3"], [3], 36),
     }
-    # Reuse check + row copy (mismatch_strided_kernel, reuse_rows_batch_kernel):
-    # per scene and stage, both value checks read the support and query
-    # prefix twice (input and snapshot, 12 B per point each) and the hit rows
-    # are read and written once (4K B each).
+    # Reuse check + row copy (reuse_stage_kernel, one launch per stage): per
+    # scene and stage the support prefix is read twice (input and snapshot,
+    # 12 B per point each; the query prefix is its first rows, so one pass
+    # answers both checks) and the hit rows are read and written once (4K B
+    # each).
     reuse_ms = sum(stage.get(f"reuse{s}", 0.0) for s in range(4))
-    reuse_bytes = args.steps * S * sum(24 * (SIZES[s] + SIZES[s + 1]) + 8 * K * SIZES[s + 1] for s in range(4))
+    reuse_bytes = args.steps * S * sum(24 * SIZES[s] + 8 * K * SIZES[s + 1] for s in range(4))
     reuse_line = {
         "ms_per_step": reuse_ms / args.steps,
-        "launches_per_step": 12,
+        "launches_per_step": 4,
         "bytes_per_step": reuse_bytes // args.steps,
         "achieved_gbs": reuse_bytes / (reuse_ms / 1000.0) / 1e9 if reuse_ms else 0.0,
     }
@@ -811,6 +870,9 @@ def cpu_baseline(P, out):
 
 def main():
     args = parse()
+    if args.write_traffic_profile:
+        write_traffic_profile(args.write_traffic_profile)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -11,6 +11,7 @@
 //
 // Equality is IEEE value equality of float32 elements, the semantics of
 // torch.equal: NaN never equals, -0 equals +0.
+#include <cooperative_groups.h>
 #include <algorithm>
 #include "common.cuh"
 
@@ -137,6 +138,103 @@ inline unsigned copy_blocks(long long work) {
   return (unsigned)std::max<long long>(1, std::min<long long>(b, 148 * 8));
 }
 
+// One hierarchy stage's reuse admission and gather in one launch: a thread-
+// block cluster per scene.  Every CTA compares its share of the support
+// (ns floats; the query prefix is its first nq floats, so one pass yields
+// both flags), the cluster combines the CTAs' bits through distributed shared
+// memory, and on a hit every CTA copies its share of the rows.  The flags and
+// hits are written whole (no memset), the rows only on a hit.
+constexpr int kStageThreads = 256;
+constexpr int kStageClusterMax = 8;  // portable cluster size
+
+// Elements j..j+3 of a support pair: any difference sets ds, a difference
+// among the first nq elements sets dq (IEEE !=: NaN differs, -0 == +0).
+__device__ __forceinline__ void diff4(const float4 x, const float4 y,
+                                      long long j, long long nq, bool& ds,
+                                      bool& dq) {
+  const bool ex = x.x != y.x, ey = x.y != y.y, ez = x.z != y.z, ew = x.w != y.w;
+  ds |= ex | ey | ez | ew;
+  dq |= (ex & (j < nq)) | (ey & (j + 1 < nq)) | (ez & (j + 2 < nq)) |
+        (ew & (j + 3 < nq));
+}
+
+__global__ void __launch_bounds__(kStageThreads)
+    reuse_stage_kernel(const float* a, long long a_stride, const float* b,
+                       long long b_stride, long long ns, long long nq,
+                       const int* src, long long src_stride, int src_ld,
+                       int rows, int cols, int* dst, long long dst_stride,
+                       int* flags, int* hits) {
+  namespace cg = cooperative_groups;
+  __shared__ int bits;  // bit 0: support differs, bit 1: query prefix differs
+  cg::cluster_group cluster = cg::this_cluster();
+  const long long p = blockIdx.y;
+  const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+  const float* u = a + p * a_stride;
+  const float* v = b + p * b_stride;
+  const long long t = (long long)rank * kStageThreads + threadIdx.x;
+  const long long stride = (long long)cs * kStageThreads;
+  bool ds = false, dq = false;
+  if (((((uintptr_t)u) | ((uintptr_t)v)) & 15) == 0) {
+    const float4* u4 = reinterpret_cast<const float4*>(u);
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    const long long n4 = ns >> 2;
+    long long i = t;
+    // two independent 16-byte pairs in flight per thread
+    for (; i + stride < n4; i += 2 * stride) {
+      const float4 x0 = __ldcs(u4 + i), y0 = __ldcs(v4 + i);
+      const float4 x1 = __ldcs(u4 + i + stride), y1 = __ldcs(v4 + i + stride);
+      diff4(x0, y0, 4 * i, nq, ds, dq);
+      diff4(x1, y1, 4 * (i + stride), nq, ds, dq);
+    }
+    for (; i < n4; i += stride) diff4(__ldcs(u4 + i), __ldcs(v4 + i), 4 * i, nq, ds, dq);
+    for (long long k = (n4 << 2) + t; k < ns; k += stride) {
+      const bool e = u[k] != v[k];
+      ds |= e;
+      dq |= e && k < nq;
+    }
+  } else {
+    for (long long k = t; k < ns; k += stride) {
+      const bool e = u[k] != v[k];
+      ds |= e;
+      dq |= e && k < nq;
+    }
+  }
+  const int mine = __syncthreads_or(ds) | (__syncthreads_or(dq) << 1);
+  if (threadIdx.x == 0) bits = mine;
+  cluster.sync();  // every CTA's bits written
+  int all = 0;
+  for (int c = 0; c < cs; ++c) all |= *cluster.map_shared_rank(&bits, c);
+  cluster.sync();  // no CTA leaves while another may still read its bits
+  const bool hit = all == 0;
+  if (rank == 0 && threadIdx.x == 0) {
+    flags[2 * p] = all & 1;
+    flags[2 * p + 1] = (all >> 1) & 1;
+    if (hits) hits[p] = hit;
+  }
+  if (!hit || rows == 0) return;
+  const int* s = src + p * src_stride;
+  int* d = dst + p * dst_stride;
+  const long long total = (long long)rows * cols;
+  if (cols == src_ld && ((((uintptr_t)s) | ((uintptr_t)d)) & 15) == 0 &&
+      (total & 3) == 0) {
+    const int4* s4 = reinterpret_cast<const int4*>(s);
+    int4* d4 = reinterpret_cast<int4*>(d);
+    const long long n4 = total >> 2;
+    long long i = t;
+    for (; i + stride < n4; i += 2 * stride) {
+      const int4 r0 = __ldcs(s4 + i), r1 = __ldcs(s4 + i + stride);
+      d4[i] = r0;
+      d4[i + stride] = r1;
+    }
+    for (; i < n4; i += stride) d4[i] = __ldcs(s4 + i);
+    return;
+  }
+  for (long long i = t; i < total; i += stride) {
+    const long long row = i / cols, col = i - row * cols;
+    d[i] = s[row * src_ld + col];
+  }
+}
+
 }  // namespace
 }  // namespace gsa
 
@@ -257,4 +355,39 @@ GSA_API int session_lookup(int count, const float* const* a,
                                   cudaMemcpyDeviceToHost, s);
   if (!e) e = cudaStreamSynchronize(s);
   return (int)e;
+}
+
+// See include/gsa_bvh.h.
+GSA_API int reuse_prefix_batch(int count, const float* a, long long a_stride,
+                               const float* b, long long b_stride,
+                               long long ns, long long nq, const int* src,
+                               long long src_stride, int src_ld, int rows,
+                               int cols, int* dst, long long dst_stride,
+                               int* flags, int* hits, void* stream) {
+  if (count < 0 || count > 65535 || ns < 0 || nq < 0 || nq > ns || rows < 0 ||
+      cols < 1 || src_ld < cols)
+    return -2;
+  if (!count) return 0;
+  if (!a || !b || !flags || (rows && (!src || !dst))) return -2;
+  // one CTA per ~64 KB of compared and copied bytes, at most a portable
+  // cluster of 8
+  const long long bytes = 8 * ns + 8ll * rows * cols;
+  const int cs = (int)std::max<long long>(
+      1, std::min<long long>(kStageClusterMax, (bytes + (64 << 10) - 1) >> 16));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs, count);
+  cfg.blockDim = dim3(kStageThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launches();
+  return cudaLaunchKernelEx(&cfg, reuse_stage_kernel, a, a_stride, b, b_stride,
+                            ns, nq, src, src_stride, src_ld, rows, cols, dst,
+                            dst_stride, flags, hits);
 }

@@ -16,10 +16,11 @@
 // (kStaticCandidates * 2 ints, 512 bytes), which every GPU that loads this
 // library holds until the process exits.
 //
-// Set-up: the first call on a device, with that device current, looks up the
-// array's device address with cudaGetSymbolAddress (host code cannot use the
-// array's name as a device pointer) and caches it for that device; make that
-// first call before any stream capture.  All calls share the array and it
+// Set-up: a call outside stream capture, with the device current, looks up
+// the array's device address with cudaGetSymbolAddress (host code cannot use
+// the array's name as a device pointer) and caches it for that device; a
+// call during capture uses that cached address, so make one call on each
+// device before any stream capture.  All calls share the array and it
 // keeps the previous call's contents, so every call clears its flags first;
 // calls whose work overlaps on the GPU (different streams, no ordering)
 // race on the array.  No call allocates or frees memory.
@@ -37,18 +38,27 @@ static __device__ __align__(256) int g_lookup_flags[2 * kStaticCandidates];
 std::mutex g_setup_mutex;
 int* g_flag_ptr[kMaxDevices] = {};
 
-// Device address of g_lookup_flags on the current device (set-up once).
-cudaError_t flags_on_current_device(int** out) {
+// Device address of g_lookup_flags on the current device.  Outside stream
+// capture the address is looked up on every call (cudaGetSymbolAddress
+// allocates nothing), so a context re-created after cudaDeviceReset gets the
+// array's new address; during capture the address cached by the last call
+// outside capture on this device is used (none cached: an error).
+cudaError_t flags_on_current_device(cudaStream_t s, int** out) {
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e) return e;
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(s, &capture);
+  if (e) return e;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_flag_ptr[device]) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_lookup_flags);
     if (e) return e;
     g_flag_ptr[device] = static_cast<int*>(p);
+  } else if (!g_flag_ptr[device]) {
+    return cudaErrorStreamCaptureUnsupported;
   }
   *out = g_flag_ptr[device];
   return cudaSuccess;
@@ -62,7 +72,8 @@ struct LookupArgs {
   int count;
 };
 
-// Pair p: candidate p / 2, support (p even) or query prefix (p odd).
+// Pair p: candidate p / 2, support (p even) or query prefix (p odd).  16-byte
+// loads when both arrays are 16-byte aligned.
 __global__ void __launch_bounds__(256)
     lookup_compare_kernel(LookupArgs a, int* flags) {
   int p = blockIdx.y;
@@ -71,9 +82,20 @@ __global__ void __launch_bounds__(256)
   const float* v = a.saved[side][p >> 1];
   long long n = a.n[side];
   bool diff = false;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    diff |= u[i] != v[i];
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long tail = 0;
+  if (((((uintptr_t)u) | ((uintptr_t)v)) & 15) == 0) {
+    const float4* u4 = reinterpret_cast<const float4*>(u);
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    const long long n4 = n >> 2;
+    for (long long i = t; i < n4; i += stride) {
+      const float4 x = __ldcs(u4 + i), y = __ldcs(v4 + i);
+      diff |= (x.x != y.x) | (x.y != y.y) | (x.z != y.z) | (x.w != y.w);
+    }
+    tail = n4 << 2;
+  }
+  for (long long i = tail + t; i < n; i += stride) diff |= u[i] != v[i];
   if (__any_sync(kFull, diff) && (threadIdx.x & 31) == 0) flags[p] = 1;
 }
 
@@ -115,8 +137,9 @@ GSA_API int reuse_lookup_static(int count, const float* x, long long nx,
   if (count < 1 || nx < 0 || nq < 0 || rows < 0 || cols < 1 || src_ld < cols)
     return -2;
   if (!x || !q || !saved_x || !saved_q || !cached || (rows && !dst)) return -2;
+  cudaStream_t s = (cudaStream_t)stream;
   int* flags = nullptr;
-  cudaError_t e = flags_on_current_device(&flags);
+  cudaError_t e = flags_on_current_device(s, &flags);
   if (e) return e;
   LookupArgs a = {};
   a.cur[0] = x;
@@ -130,7 +153,6 @@ GSA_API int reuse_lookup_static(int count, const float* x, long long nx,
     a.saved[1][c] = saved_q[c];
     a.cached[c] = cached[c];
   }
-  cudaStream_t s = (cudaStream_t)stream;
   e = cudaMemsetAsync(flags, 0, sizeof(int) * 2 * count, s);
   if (e) return e;
   dim3 grid(blocks_for_work(nx > nq ? nx : nq), 2 * count);

@@ -14,8 +14,8 @@ and per decoder stage ``nn(P_s -> P_{s+1})`` for s = 3..0.
 ``run_session`` issues exactly these calls through the drop-in
 ``QuerySession``.  ``Batch`` runs the same hierarchy for B equally sized
 scenes with one launch per build step / query stage (forest build, radius
-and 3NN traversal of every scene, one batched value check and one batched
-row gather per stage); its outputs equal ``run_session``'s for every scene.
+and 3NN traversal of every scene, one launch per stage for the value checks
+and the row gather); its outputs equal ``run_session``'s for every scene.
 """
 
 import contextlib
@@ -37,6 +37,8 @@ er.lib.coords_mismatch_strided.argtypes = [_I, _P, _LL, _P, _LL, _LL, _P, _I, _P
 er.lib.coords_mismatch_strided.restype = _I
 er.lib.reuse_rows_batch.argtypes = [_I, _P, _LL, _I, _P, _I, _I, _P, _LL, _P, _P]
 er.lib.reuse_rows_batch.restype = _I
+er.lib.reuse_prefix_batch.argtypes = [_I, _P, _LL, _P, _LL, _LL, _LL, _P, _LL, _I, _I, _I, _P, _LL, _P, _P, _P]
+er.lib.reuse_prefix_batch.restype = _I
 
 
 def unit_counts(sizes):
@@ -202,14 +204,13 @@ class Batch:
                 forest.ball_prefix(n_s, s, self.radii[s], K, rows)
             # reuse admission: support P_s and query prefix P_{s+1} equal the
             # retained snapshot, then gather the first n_q rows of each scene
+            # (one launch: a thread-block cluster per scene)
             with timer.span(f"reuse{s}"):
-                stream = er._stream()
-                er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, flags.data_ptr(), 2, stream))
-                er.check(er.lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, flags.data_ptr() + 4, 2, stream))
                 er.check(
-                    er.lib.reuse_rows_batch(
-                        B, rows.data_ptr(), n_s * K, K, flags.data_ptr(), n_q, K,
-                        out[f"hit{s}"].data_ptr(), n_q * K, hitflags.data_ptr(), stream,
+                    er.lib.reuse_prefix_batch(
+                        B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, n_q * 3,
+                        rows.data_ptr(), n_s * K, K, n_q, K, out[f"hit{s}"].data_ptr(), n_q * K,
+                        flags.data_ptr(), hitflags.data_ptr(), er._stream(),
                     )
                 )
 

@@ -156,6 +156,24 @@ int reuse_rows_batch(int count, const int* src, long long src_stride,
                      int src_ld, const int* flags, int rows, int cols,
                      int* dst, long long dst_stride, int* hits, void* stream);
 
+/* One hierarchy stage's reuse admission and gather in one launch: for scene
+ * p < count, flags[2p] = 1 when the support a[p*a_stride + i] differs from
+ * the retained snapshot b[p*b_stride + i] for some i < ns (IEEE !=), and
+ * flags[2p+1] = 1 when it differs for some i < nq (the query prefix: the
+ * session's query is the support's first nq floats); else 0.  When both are
+ * 0 the rows src[p*src_stride + i*src_ld + j] go to dst[p*dst_stride +
+ * i*cols + j] (i < rows, j < cols) and hits[p] (may be null) is 1, else 0;
+ * rows of a miss are left untouched.  Fused, batched form of the two
+ * torch.equal checks and the cached-row copy of gsa/session.py:104-114 (one
+ * thread-block cluster per scene).  Returns 0, -2 (bad argument), or a
+ * cudaError_t. */
+int reuse_prefix_batch(int count, const float* a, long long a_stride,
+                       const float* b, long long b_stride, long long ns,
+                       long long nq, const int* src, long long src_stride,
+                       int src_ld, int rows, int cols, int* dst,
+                       long long dst_stride, int* flags, int* hits,
+                       void* stream);
+
 /* Total kernel launches this library has issued since it was loaded. */
 int launch_counter(unsigned long long* total);
 
@@ -171,9 +189,12 @@ int launch_counter(unsigned long long* total);
  * saved_x, saved_q, cached are HOST arrays of count device pointers.  The
  * per-candidate flags live in a fixed 512-byte device array inside the
  * library (held on every GPU that loads it), so count may not exceed 64:
- * larger counts return -4.  The first call on a device looks up that array's
- * address (make it before any stream capture).  Calls share the array:
- * calls whose GPU work overlaps race.  Returns 0, -2 (bad argument), -4, or
+ * larger counts return -4.  A call outside stream capture looks up that
+ * array's device address (again on every such call, so a device reset does
+ * not leave a stale address); a call during capture reuses the address of
+ * the last uncaptured call on that device, so make one call per device
+ * before any stream capture.  Calls share the array: calls whose GPU work
+ * overlaps race.  Returns 0, -2 (bad argument), -4, or
  * a cudaError_t. */
 int reuse_lookup_static(int count, const float* x, long long nx,
                         const float* q, long long nq,

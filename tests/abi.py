@@ -22,6 +22,8 @@ def bvh_lib(name="gsa_bvh"):
     lib.query_bvh_batch.argtypes = [P, P, P, P, P, I, I, P, P, P, P]
     lib.coords_mismatch_strided.argtypes = [I, P, ctypes.c_longlong, P, ctypes.c_longlong, ctypes.c_longlong, P, I, P]
     lib.reuse_rows_batch.argtypes = [I, P, ctypes.c_longlong, I, P, I, I, P, ctypes.c_longlong, P, P]
+    LL = ctypes.c_longlong
+    lib.reuse_prefix_batch.argtypes = [I, P, LL, P, LL, LL, LL, P, LL, I, I, I, P, LL, P, P, P]
     lib.coords_mismatch.argtypes = [I, P, P, P, P, P]
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]

@@ -157,6 +157,53 @@ def test_batched_reuse_admission_rejects_changed_scene():
             assert (got == -1).all()
 
 
+@pytest.mark.parametrize("N,n_q,shift", [(1000, 250, 0), (24000, 6000, 0), (1001, 333, 1), (94, 23, 0), (7, 7, 1)])
+def test_fused_stage_reuse_equals_two_step_path(N, n_q, shift):
+    """reuse_prefix_batch (one cluster launch) against coords_mismatch_strided
+    twice + reuse_rows_batch: same flags, hits and rows; rows of a miss stay
+    untouched.  shift=1 offsets every buffer by one element (scalar path)."""
+    from tests import abi
+
+    lib = abi.bvh_lib()
+    B, K = 6, 32
+    g = torch.Generator(device="cpu").manual_seed(N + n_q)
+    X = torch.randn(B * N * 3 + shift, generator=g).cuda()[shift:].view(B, N, 3)
+    snap = torch.empty(B * N * 3 + shift, device="cuda")[shift:].view(B, N, 3)
+    snap.copy_(X)
+    if N > n_q:
+        snap[1, N - 1, 2] += 1e-3  # support differs beyond the query prefix
+    snap[2, n_q - 1, 2] = torch.nextafter(snap[2, n_q - 1, 2], torch.tensor(float("inf"), device="cuda"))  # last query element
+    snap[3, 0, 0] = float("nan")  # NaN never compares equal
+    X[4, 0, 1] = 0.0
+    snap[4, 0, 1] = -0.0  # -0 == +0: still a hit
+    X[5, n_q // 2, 0] = float("nan")
+    snap[5, n_q // 2, 0] = float("nan")
+    st = abi.stream()
+    want_flags = torch.full((2 * B,), 7, dtype=torch.int32, device="cuda")
+    assert lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, N * 3, want_flags.data_ptr(), 2, st) == 0
+    assert lib.coords_mismatch_strided(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, want_flags.data_ptr() + 4, 2, st) == 0
+    rows = torch.randint(0, 999, (B * N * K + shift,), dtype=torch.int32, device="cuda")[shift:].view(B * N, K)
+    want = torch.full((B * n_q * K + shift,), -1, dtype=torch.int32, device="cuda")[shift:].view(B * n_q, K)
+    got = want.clone()
+    want_hits = torch.full((B,), 9, dtype=torch.int32, device="cuda")
+    assert lib.reuse_rows_batch(B, rows.data_ptr(), N * K, K, want_flags.data_ptr(), n_q, K, want.data_ptr(), n_q * K, want_hits.data_ptr(), st) == 0
+    flags = torch.full((2 * B,), 7, dtype=torch.int32, device="cuda")
+    hits = torch.full((B,), 9, dtype=torch.int32, device="cuda")
+    for _ in range(2):  # flags and hits are written whole on every call
+        assert lib.reuse_prefix_batch(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, N * 3, n_q * 3,
+                                      rows.data_ptr(), N * K, K, n_q, K, got.data_ptr(), n_q * K,
+                                      flags.data_ptr(), hits.data_ptr(), st) == 0
+        torch.cuda.synchronize()
+        assert flags.tolist() == want_flags.tolist()
+        assert hits.tolist() == want_hits.tolist()
+        assert torch.equal(got, want)
+    expect_hits = [1, 0 if N > n_q else 1, 0, 0, 1, 0]
+    assert hits.tolist() == expect_hits
+    assert lib.reuse_prefix_batch(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, N * 3,
+                                  rows.data_ptr(), N * K, K, n_q, K, got.data_ptr(), n_q * K,
+                                  flags.data_ptr(), hits.data_ptr(), st) == (-2 if N > n_q else 0)
+
+
 def test_clustered_exactness_stress():
     from gsa_b200 import QuerySession, scenes
 

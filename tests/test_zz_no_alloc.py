@@ -91,6 +91,36 @@ def test_static_lookup_equals_two_step_path_on_consecutive_calls():
     assert torch.equal(got[0], want[0])
 
 
+def test_static_lookup_allocates_no_device_memory():
+    """After one warm-up call (which looks up the array's address), further
+    calls change neither torch's allocated bytes nor the device's free bytes
+    as cudaMemGetInfo reports them: every buffer is passed in."""
+    lib = _lib()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    n, nq = 4096, 1024
+    x = torch.randn(n, 3, device="cuda", generator=g)
+    q = x[:nq]
+    sx = [x.clone(), x.clone()]
+    sq = [q.clone(), q.clone()]
+    sx[0][7, 1] += 1.0
+    cached = [torch.randint(0, n, (nq, 32), dtype=torch.int32, device="cuda", generator=g) for _ in range(2)]
+    dst = torch.full((nq, 32), -1, dtype=torch.int32, device="cuda")
+    hit = torch.full((1,), -9, dtype=torch.int32, device="cuda")
+    args = (2, x.data_ptr(), x.numel(), q.data_ptr(), q.numel(), _ptrs(sx), _ptrs(sq), _ptrs(cached),
+            32, nq, 32, dst.data_ptr(), hit.data_ptr(), abi.stream())
+    assert lib.reuse_lookup_static(*args) == 0
+    torch.cuda.synchronize()
+    torch_bytes = torch.cuda.memory_allocated()
+    free_bytes = torch.cuda.mem_get_info()[0]
+    for _ in range(8):
+        assert lib.reuse_lookup_static(*args) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == torch_bytes
+    assert torch.cuda.mem_get_info()[0] == free_bytes
+    assert int(hit.item()) == 1
+    assert torch.equal(dst, cached[1])
+
+
 def test_static_lookup_rejects_more_candidates_than_its_array():
     lib = _lib()
     x = torch.zeros(10, 3, device="cuda")
