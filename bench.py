@@ -20,10 +20,12 @@ all GPUs together.
   64 scenes on every GPU.
 * ``e2e``: the same rows through the drop-in ``QuerySession`` API, one scene
   at a time, points copied from pinned host memory and every output row
-  copied back to pinned host memory inside the timed region.
-  ``e2e_fixed_graph``: the same through ``fixed_graph_forward`` with the
-  measured "frozen" policy (``prefix``, ``verify=False``).  ``e2e_batched``:
-  the same with the batched engine.
+  copied back to pinned host memory inside the timed region (a scene's rows
+  on a copy stream while the next scene runs).  ``e2e_fixed_graph``: the
+  same through ``fixed_graph_forward`` with the measured "frozen" policy
+  (``prefix``, ``verify=False``).  ``e2e_concurrent_sessions``: the session
+  API from two host threads, each on its own stream.  ``e2e_batched``: the
+  same with the batched engine.
 * ``roofline``: the query kernel with the largest share of step time,
   algorithmic bytes (radius 12 + 4K B per query, 3NN 36 B per query) over its
   measured time, against the measured HBM copy bandwidth.
@@ -703,7 +705,8 @@ def run_ours(args, rank, world, local):
         line["weak"] = weak_run(args, rank, world, dev, flush)
 
     if not args.no_e2e:
-        line["e2e"], line["e2e_fixed_graph"], line["e2e_batched"] = e2e(args, X, step, out, world, dev)
+        line["e2e"], line["e2e_fixed_graph"], line["e2e_batched"], line["e2e_concurrent_sessions"] = e2e(
+            args, X, step, out, world, dev)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out)
@@ -753,12 +756,18 @@ def e2e(args, X, step, out, world, dev):
     ball_rows, hit_rows, nn_rows = rows_per_scene()
     rows = ball_rows + hit_rows + nn_rows
     steps = max(1, min(args.steps, 3))
-    flat, views = hz.session_outputs(SIZES, dev)
-    host_flat = torch.empty((S, flat.numel()), dtype=torch.int32, pin_memory=True)
-    d2h = S * flat.numel() * flat.element_size()
+    # two output buffers: scene i's rows leave the device on a copy stream
+    # while scene i+1 runs (a scene's outputs are views of one device buffer,
+    # copied back in one transfer)
+    bufs = [hz.session_outputs(SIZES, dev) for _ in range(2)]
+    words = bufs[0][0].numel()
+    host_flat = torch.empty((S, words), dtype=torch.int32, pin_memory=True)
+    d2h = S * words * 4
+    copy_stream = torch.cuda.Stream(dev)
 
     def per_scene(run_scene):
         ms = 0.0
+        main = torch.cuda.current_stream()
         for st in range(steps + 1):  # first pass warms allocator and pinned buffers
             torch.cuda.synchronize()
             if world > 1:
@@ -766,37 +775,45 @@ def e2e(args, X, step, out, world, dev):
             t0 = torch.cuda.Event(enable_timing=True)
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record()
+            free = [torch.cuda.Event(), torch.cuda.Event()]
+            for ev in free:
+                ev.record(main)
             for i in range(S):
+                k = i % 2
+                main.wait_event(free[k])  # scene i-2's copy out of this buffer done
                 x = host_x[i].to(dev, non_blocking=True)
-                run_scene(x)
-                # a scene's outputs are views of one device buffer, copied back
-                # in one transfer (stream order keeps the next scene from
-                # overwriting it early)
-                host_flat[i].copy_(flat, non_blocking=True)
+                run_scene(x, k)
+                done = torch.cuda.Event()
+                done.record(main)
+                copy_stream.wait_event(done)
+                with torch.cuda.stream(copy_stream):
+                    host_flat[i].copy_(bufs[k][0], non_blocking=True)
+                    free[k].record(copy_stream)
+            main.wait_stream(copy_stream)
             t1.record()
             torch.cuda.synchronize()
             if st:
                 ms += t0.elapsed_time(t1)
         return world * S * rows * steps / (gd.max_over_ranks(ms, dev) / 1000.0)
 
-    def session_scene(x):
+    def session_scene(x, k):
         with QuerySession() as s:
-            hz.run_session(s, x, SIZES, RADII, views)
+            hz.run_session(s, x, SIZES, RADII, bufs[k][1])
 
     session = {
         "value": per_scene(session_scene),
         "unit": UNIT,
         "h2d_bytes_per_step": int(host_x.numel() * 4),
         "d2h_bytes_per_step": int(d2h),
-        "api": "gsa_b200.QuerySession (drop-in for gsa.QuerySession), one scene per session, threshold 1024",
+        "api": "gsa_b200.QuerySession (drop-in for gsa.QuerySession), one scene per session, one session at a time, threshold 1024; each scene's rows copied out on a copy stream while the next scene runs",
         "steps": steps,
     }
-    session_rows0 = host_flat[0].clone()
+    session_rows = host_flat.clone()
 
-    model = hz.graph_model(ops, SIZES, RADII, views)
+    models = [hz.graph_model(ops, SIZES, RADII, bufs[k][1]) for k in range(2)]
 
-    def fixed_scene(x):
-        fixed_graph_forward(model, {"pos": x[None]}, ops=ops, policy="prefix", verify=False)
+    def fixed_scene(x, k):
+        fixed_graph_forward(models[k], {"pos": x[None]}, ops=ops, policy="prefix", verify=False)
 
     with torch.inference_mode():
         fixed_value = per_scene(fixed_scene)
@@ -807,8 +824,15 @@ def e2e(args, X, step, out, world, dev):
         "d2h_bytes_per_step": int(d2h),
         "api": "gsa_b200.fixed_graph_forward (drop-in for gsa.fixed_graph.forward), policy prefix, verify=False (the measured 'frozen' policy), one scene per forward",
         "steps": steps,
-        "rows_equal_session_scene0": bool(torch.equal(host_flat[0], session_rows0)),
+        "rows_equal_session": bool(torch.equal(host_flat, session_rows)),
     }
+    concurrent = concurrent_sessions(host_x, host_flat, steps, world, dev, threads=2)
+    concurrent.update({
+        "h2d_bytes_per_step": int(host_x.numel() * 4),
+        "d2h_bytes_per_step": int(d2h),
+        "rows_equal_session": bool(torch.equal(host_flat, session_rows)),
+    })
+    session_rows0 = session_rows[0]
 
     # batched engine: the captured step reads X, so the host copy lands there
     keys = [k for k in out if k.startswith(("ball", "hit", "nn"))]
@@ -841,7 +865,72 @@ def e2e(args, X, step, out, world, dev):
         "api": f"gsa_b200.hierarchy.Batch over gsa_b200.Forest (batched C ABI), step as {step.mode}",
         "steps": steps,
     }
-    return session, fixed, batched
+    return session, fixed, batched, concurrent
+
+
+def concurrent_sessions(host_x, host_flat, steps, world, dev, threads=2):
+    """The session API from several host threads, one QuerySession per scene,
+    each thread on its own CUDA stream (scenes t, t+T, ...): while one thread
+    waits for its comparison flags, another enqueues its next call.  Device
+    time from an event on the calling stream before the threads start to one
+    after every thread's stream is joined back."""
+    import threading
+
+    import torch
+
+    from gsa_b200 import QuerySession, distributed as gd, hierarchy as hz
+
+    S = host_x.shape[0]
+    ball_rows, hit_rows, nn_rows = rows_per_scene()
+    rows = ball_rows + hit_rows + nn_rows
+    streams = [torch.cuda.Stream(dev) for _ in range(threads)]
+    bufs = [hz.session_outputs(SIZES, dev) for _ in range(threads)]
+    errors = []
+
+    def worker(t, start):
+        try:
+            torch.cuda.set_device(dev)
+            st = streams[t]
+            st.wait_event(start)
+            flat, views = bufs[t]
+            with torch.cuda.stream(st):
+                for i in range(t, S, threads):
+                    x = host_x[i].to(dev, non_blocking=True)
+                    with QuerySession() as s:
+                        hz.run_session(s, x, SIZES, RADII, views)
+                    host_flat[i].copy_(flat, non_blocking=True)
+        except Exception as e:  # reported after the join
+            errors.append(e)
+
+    ms = 0.0
+    main = torch.cuda.current_stream()
+    for it in range(steps + 1):
+        torch.cuda.synchronize()
+        if world > 1:
+            gd.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        ths = [threading.Thread(target=worker, args=(t, t0)) for t in range(threads)]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        if errors:
+            raise errors[0]
+        for st in streams:
+            main.wait_stream(st)
+        t1.record()
+        torch.cuda.synchronize()
+        if it:
+            ms += t0.elapsed_time(t1)
+    return {
+        "value": world * S * rows * steps / (gd.max_over_ranks(ms, dev) / 1000.0),
+        "unit": UNIT,
+        "api": f"gsa_b200.QuerySession from {threads} host threads, one session per scene, each thread on its own CUDA stream",
+        "threads": threads,
+        "steps": steps,
+    }
 
 
 def cpu_baseline(P, out):

@@ -567,8 +567,9 @@ __device__ __forceinline__ LeafPts leaf_points(const float4* pts, int ref,
 template <int CAP, int FRONT>
 struct WarpBufs {
   int buf[32][CAP + 1];  // per-query hits (IDs) or candidates (positions)
-  float4 q[32];          // query coordinates and bound
-  int amap[32];          // pair step: active-query slot -> lane
+  float4 qa[32];         // pair steps: active query i's coordinates, and its
+                         // lane (radius) or its bound (3NN) in w
+  int amap[32];          // pair steps (3NN): active query i's lane
   int leafq[64];         // queued leaf entries (-1: the root)
   int front[FRONT];      // frontier stack of internal nodes
 };
@@ -607,8 +608,8 @@ __device__ __forceinline__ Top3 cut_candidates(const float4* pts, int* row,
 }
 
 // One batch of queued leaves lq[0..nleaf) (see the section comment).  `in`:
-// the lane's query takes part; `bound`: its current bound (r*r or B, also in
-// W.q[lane].w); `nc`: its buffer count.
+// the lane's query takes part; `bound`: its current bound (r*r, the same on
+// every lane, or B); `nc`: its buffer count.
 template <bool KNN, int CAP, int FRONT>
 __device__ void leaf_batches(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
                              const Entry* root, const float4* pts, int nleaf,
@@ -657,38 +658,40 @@ __device__ void leaf_batches(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
       if (KNN && __any_sync(kFull, need && nc + L.cnt > CAP)) {
         if (need && nc + L.cnt > CAP) {
           Top3 t = cut_candidates(pts, W.buf[lane], nc, px, py, pz);
-          if (nc == 3) {
-            bound = t.d2;
-            W.q[lane].w = bound;
-          }
+          if (nc == 3) bound = t.d2;
         }
       }
       const int nA = __popc(M);
       const int mine = __popc(M & lt);
-      if (need) W.amap[mine] = lane;
+      if (need) {
+        W.qa[mine] = make_float4(px, py, pz, KNN ? bound : __int_as_float(lane));
+        if (KNN) W.amap[mine] = lane;
+      }
       __syncwarp();
       const int logw = L.logw;
       const int w = 1 << logw, per = 32 >> logw;
-      const int k = lane >> logw, j = lane & (w - 1);
+      const int k = lane >> logw, j = lane & (w - 1), kw = k << logw;
       const unsigned seg0 = w == 32 ? kFull : (1u << w) - 1u;
       const int id = __float_as_int(L.pt.w);
       const bool pv = j < L.cnt && id < m;
       for (int base = 0; base < nA; base += per) {
-        int idx = base + k;
-        bool valid = pv && idx < nA;
-        int q = W.amap[idx < nA ? idx : 0];
-        float4 qc = W.q[q];
-        bool hit = valid && within<KNN>(exact_d2(qc.x, qc.y, qc.z, L.pt.x,
-                                                 L.pt.y, L.pt.z),
-                                        qc.w);
-        unsigned hm = __ballot_sync(kFull, hit);
+        const int idx = base + k;
+        const bool valid = pv && idx < nA;
+        // one 16-byte load per step: the query's coordinates with its lane
+        // (radius; the bound r*r is the same for every query) or its bound
+        const float4 qc = W.qa[idx < nA ? idx : 0];
+        const bool hit = valid && within<KNN>(exact_d2(qc.x, qc.y, qc.z, L.pt.x,
+                                                       L.pt.y, L.pt.z),
+                                              KNN ? qc.w : bound);
+        const unsigned hm = __ballot_sync(kFull, hit);
         if (!hm) continue;  // warp-uniform
-        int at = __shfl_sync(kFull, nc, q);
-        int slot = at + __popc(hm & (seg0 << (k << logw)) & lt);
+        const int q = KNN ? W.amap[idx < nA ? idx : 0] : __float_as_int(qc.w);
+        // hits of this query's segment below this lane, after its count
+        const int slot = __shfl_sync(kFull, nc, q) + __popc((hm & lt) >> kw);
         if (hit && (KNN || slot < CAP)) W.buf[q][slot] = KNN ? L.start + j : id;
-        int mk = mine - base;
-        if (need && mk >= 0 && mk < per)
-          nc += __popc(hm & (seg0 << (mk << logw)));
+        const int mk = mine - base;
+        if (need && (unsigned)mk < (unsigned)per)
+          nc += __popc((hm >> (mk << logw)) & seg0);
       }
       __syncwarp();
       if (nxt < 0) break;
@@ -841,7 +844,6 @@ __global__ void __launch_bounds__(kFWarps * 32)
   // distances are inf or NaN) and stay out of the packet box.
   const bool live = active && finite3(px, py, pz);
   float bound = c.r2;
-  W.q[lane] = make_float4(px, py, pz, bound);
   int hc = 0;  // this lane's hit count (may exceed kPacketCap)
   bool overflow = false;
   if (__any_sync(kFull, live)) {
@@ -948,7 +950,6 @@ __global__ void __launch_bounds__(kFWarps * 32)
     B = w2;  // inf unless three finite distances were seen
   }
   const bool inpk = live && B < inf;
-  W.q[lane] = make_float4(px, py, pz, B);
   int nc = 0;  // this lane's candidates
   bool overflow = false;
   if (__any_sync(kFull, inpk)) {

@@ -21,6 +21,7 @@ reference's short-circuit order over those flags, so
 
 import ctypes
 import math
+import threading
 
 import torch
 
@@ -41,6 +42,18 @@ er.lib.gather_rows.restype = _I
 er.lib.session_lookup.argtypes = [_I, _P, _P, _P, _I, _P, _I, _I, _I, _P, _P, _P, _P]
 er.lib.session_lookup.restype = _I
 _LOOKUP_MAX = 128  # pairs per session_lookup call (device flag buffer size)
+_TLS = threading.local()
+
+
+def _host_flags():
+    """This thread's pinned host buffer for the comparison flags (pinned, so
+    the flag read is a direct DMA instead of a staged copy), as a ctypes int
+    array over the tensor's memory."""
+    buf = getattr(_TLS, "flags", None)
+    if buf is None:
+        t = torch.empty(_LOOKUP_MAX, dtype=torch.int32, pin_memory=True)
+        buf = _TLS.flags = (t, (ctypes.c_int * _LOOKUP_MAX).from_address(t.data_ptr()))
+    return buf[1]
 
 
 class _CudaOps:
@@ -52,7 +65,7 @@ class _CudaOps:
 
     def __init__(self):
         self._dflags = None
-        self._hflags = (ctypes.c_int * _LOOKUP_MAX)()
+        self._hflags = _host_flags()
 
     def lookup(self, pairs, cached, rows, cols, out, device):
         """Compare every pair (a, b): a against the first a.numel() values
