@@ -167,53 +167,37 @@ def run_ref_cuda(args, total):
     X = scenes.room_batch(range(total))  # the same inputs as our arm
     flat, views = hz.session_outputs(SIZES, dev)
     steps = max(1, min(args.steps, 3))
-    # per call, device spans
-    per_call = {}
-    for step in range(steps + 1):
-        for i in range(total):
-            with gsa.QuerySession() as s:
-                calls = ref_session_calls(gsa, s, X[i], views)
-                while True:
-                    t0 = torch.cuda.Event(enable_timing=True)
-                    t1 = torch.cuda.Event(enable_timing=True)
-                    t0.record()
-                    name = next(calls, None)
-                    t1.record()
-                    if name is None:
-                        break
-                    if step:
-                        per_call.setdefault(name, []).append((t0, t1))
-    torch.cuda.synchronize()
-    call_ms = {k: sum(a.elapsed_time(b) for a, b in v) / steps for k, v in per_call.items()}
-    # standalone prefix-tree build (cuBQL build + prefix refit, host-synced levels)
-    spans = []
-    for step in range(steps + 1):
-        for i in range(total):
-            t0 = torch.cuda.Event(enable_timing=True)
-            t1 = torch.cuda.Event(enable_timing=True)
-            t0.record()
-            tree = gsa.Tree(X[i].clone(), prefix=True)
-            t1.record()
-            tree.close()
-            if step:
-                spans.append((t0, t1))
-    torch.cuda.synchronize()
-    build_ms = sum(a.elapsed_time(b) for a, b in spans) / steps
-    # end to end, as our e2e: pinned host points in, every row out
+    call_ms, build_ms = session_call_spans(gsa, X, views, steps)
+    # end to end, as our e2e: pinned host points in, every row out (a scene's
+    # rows on a copy stream while the next scene runs, two output buffers)
     host_x = X.cpu().pin_memory()
+    bufs = [(flat, views), hz.session_outputs(SIZES, dev)]
     host_flat = torch.empty((total, flat.numel()), dtype=torch.int32, pin_memory=True)
+    copy_stream = torch.cuda.Stream(dev)
+    main = torch.cuda.current_stream()
     ms = 0.0
     for step in range(steps + 1):
         torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+        for ev in free:
+            ev.record(main)
         for i in range(total):
+            k = i % 2
+            main.wait_event(free[k])
             x = host_x[i].to(dev, non_blocking=True)
             with gsa.QuerySession() as s:
-                for _ in ref_session_calls(gsa, s, x, views):
+                for _ in ref_session_calls(gsa, s, x, bufs[k][1]):
                     pass
-            host_flat[i].copy_(flat, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(main)
+            copy_stream.wait_event(done)
+            with torch.cuda.stream(copy_stream):
+                host_flat[i].copy_(bufs[k][0], non_blocking=True)
+                free[k].record(copy_stream)
+        main.wait_stream(copy_stream)
         t1.record()
         torch.cuda.synchronize()
         if step:
@@ -235,6 +219,48 @@ def run_ref_cuda(args, total):
         "unit": UNIT,
         "note": "call times are CUDA-event spans around each session call, host synchronisations inside the calls included",
     }
+
+
+def session_call_spans(mod, X, views, steps):
+    """Per session call, the CUDA-event span around the call summed over the
+    scenes (host synchronisations inside the call included), and a
+    standalone prefix-tree build per scene; ``mod`` is the reference's
+    ``gsa`` package or ``gsa_b200`` (the same QuerySession / Tree API), so
+    both arms are timed the same way.  Milliseconds per pass over X."""
+    import torch
+
+    total = X.shape[0]
+    per_call = {}
+    for step in range(steps + 1):
+        for i in range(total):
+            with mod.QuerySession() as s:
+                calls = ref_session_calls(mod, s, X[i], views)
+                while True:
+                    t0 = torch.cuda.Event(enable_timing=True)
+                    t1 = torch.cuda.Event(enable_timing=True)
+                    t0.record()
+                    name = next(calls, None)
+                    t1.record()
+                    if name is None:
+                        break
+                    if step:
+                        per_call.setdefault(name, []).append((t0, t1))
+    torch.cuda.synchronize()
+    call_ms = {k: sum(a.elapsed_time(b) for a, b in v) / steps for k, v in per_call.items()}
+    spans = []
+    for step in range(steps + 1):
+        for i in range(total):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            tree = mod.Tree(X[i].clone(), prefix=True)
+            t1.record()
+            tree.close()
+            if step:
+                spans.append((t0, t1))
+    torch.cuda.synchronize()
+    build_ms = sum(a.elapsed_time(b) for a, b in spans) / steps
+    return call_ms, build_ms
 
 
 def run_reference(args, rank, world):
@@ -707,6 +733,17 @@ def run_ours(args, rank, world, local):
     if not args.no_e2e:
         line["e2e"], line["e2e_fixed_graph"], line["e2e_batched"], line["e2e_concurrent_sessions"] = e2e(
             args, X, step, out, world, dev)
+        import gsa_b200
+
+        _, views = hz.session_outputs(SIZES, dev)
+        calls, build = session_call_spans(gsa_b200, X, views, max(1, min(args.steps, 3)))
+        line["session_calls"] = {
+            "calls_ms_per_step": {k: round(v, 4) for k, v in calls.items()},
+            "ms_per_step": sum(calls.values()),
+            "tree_build_ms_per_step": build,
+            "note": "CUDA-event span around each QuerySession call summed over the rank's scenes, "
+                    "as the reference arm's ref_cuda times the reference's session",
+        }
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out)
