@@ -8,8 +8,10 @@ answers every support size with the tree walk (the default library scans
 small prefixes), ``gsa_bvh_ordered.so`` does so with the per-query walks
 (ordered radius, nearest-first 3NN) instead of the packet-frontier kernels
 and builds every tree with the multi-launch sort instead of the cluster sort,
-and ``gsa_bvh_stack4.so`` has a 4-entry traversal stack (8-entry frontier)
-so that the per-query-walk and exact full-scan fallbacks are exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+``gsa_bvh_stack4.so`` has a 4-entry traversal stack (8-entry frontier)
+so that the per-query-walk and exact full-scan fallbacks are exercised, and
+``gsa_bvh_cap8.so`` caps every tree's stored nodes at 8 so that the
+node-capacity overflow path (exact scans) is exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
 intrinsics for every distance operation.
 """
@@ -50,6 +52,9 @@ LIBS = {
     "gsa_bvh_walk": (_BVH, _WALK_ONLY),
     "gsa_bvh_ordered": (_BVH, _WALK_ONLY + ["-DGSA_RADIUS_FRONTIER=0", "-DGSA_KNN_FRONTIER=0", "-DGSA_CLUSTER_SORT=0"]),
     "gsa_bvh_stack4": (_BVH, ["-DGSA_STACK=4"] + _WALK_ONLY),
+    # every tree of more than ~100 points overflows a node capacity of 8, so
+    # its queries take the exact scans
+    "gsa_bvh_cap8": (_BVH, ["-DGSA_NODE_CAP_LIMIT=8"] + _WALK_ONLY),
 }
 
 

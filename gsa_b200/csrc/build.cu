@@ -571,7 +571,7 @@ __device__ __forceinline__ int common_prefix(const uint64_t* k, int n, int i,
 }
 
 // Each internal node i > L points ("kept") emits a leaf record for every
-// child holding <= L points: (tree, first, last, i*2 + side); a tree of at most
+// child holding <= L points: (tree, first, last, compact(i)*2 + side); a tree of at most
 // L points emits one root record (tree, 0, n-1, -1).  Kept nodes whose two
 // children are leaves are listed as climb starts.  Lists are appended with
 // one atomic per warp.
@@ -598,18 +598,24 @@ __device__ __forceinline__ void emit(bool want, T rec, T* list, int* count) {
 // in shared memory; its warps then run the range, split and record work on
 // the list only, so the long binary searches of high nodes run on dense
 // warps instead of one lane in ten.
+//
+// Kept nodes get compact indices (one atomic per block on the tree's kept
+// count) that address the stored node entries; a kept node beyond the tree's
+// capacity sets the tree's overflow flag instead.  Parent links hold the
+// parent's radix-tree index (for the arrival counters) and compact index.
 __global__ void __launch_bounds__(256)
-    karras_kernel(const TreeDesc* desc, const uint64_t* keys, int* parent,
+    karras_kernel(const TreeDesc* desc, const uint64_t* keys, int2* parent,
                   int* counter, int leaf, int4* leaves, int* leaf_count,
-                  int* starts, int* start_count) {
+                  int2* starts, int* start_count, int* ovf) {
   __shared__ int kept[256];
-  __shared__ int nkept;
+  __shared__ int nkept, kbase;
   const int b = blockIdx.y;
   const TreeDesc d = desc[b];
   const int n = d.n;
   const uint64_t* k = keys + d.p0;
-  int* par = parent + (d.p0 - b);
+  int2* par = parent + (d.p0 - b);
   int* cnt = counter + (d.p0 - b);
+  int* kept_count = ovf + gridDim.y;
   if (threadIdx.x == 0) nkept = 0;
   __syncthreads();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -625,12 +631,16 @@ __global__ void __launch_bounds__(256)
       cnt[i] = 0;
   }
   __syncthreads();
+  if (threadIdx.x == 0) kbase = nkept ? atomicAdd(kept_count + b, nkept) : 0;
+  __syncthreads();
   const int total = nkept;
   const int lane = threadIdx.x & 31;
   // smallest power of two above `leaf`: every kept range reaches it
   const int lstart = 1 << (32 - __clz(leaf));
   for (int k0 = threadIdx.x & ~31; k0 < total; k0 += blockDim.x) {
-    const bool act = k0 + lane < total;
+    const int ci = kbase + k0 + lane;  // this kept node's compact index
+    const bool act = k0 + lane < total && ci < d.cap;
+    if (k0 + lane < total && ci >= d.cap) ovf[b] = 1;
     int node = 0;
     bool want0 = false, want1 = false;
     int4 rec0 = make_int4(0, 0, 0, 0), rec1 = rec0;
@@ -653,17 +663,19 @@ __global__ void __launch_bounds__(256)
         if (common_prefix(k, n, node, node + (s + t) * dir) > dnode) s += t;
       } while (t > 1);
       const int gamma = node + s * dir + min(dir, 0);
-      if (first != gamma) par[gamma] = (node << 1) | 0;
-      if (last != gamma + 1) par[gamma + 1] = (node << 1) | 1;
+      if (first != gamma) par[gamma] = make_int2((node << 1) | 0, ci);
+      if (last != gamma + 1) par[gamma + 1] = make_int2((node << 1) | 1, ci);
       want0 = gamma - first + 1 <= leaf;
       want1 = last - gamma <= leaf;
-      rec0 = make_int4(b, first, gamma, (node << 1) | 0);
-      rec1 = make_int4(b, gamma + 1, last, (node << 1) | 1);
+      // leaf records name the owner's slot by compact index
+      rec0 = make_int4(b, first, gamma, (ci << 1) | 0);
+      rec1 = make_int4(b, gamma + 1, last, (ci << 1) | 1);
       cnt[node] = (int)want0 + (int)want1;
     }
     emit(want0, rec0, leaves + d.p0, leaf_count + b);
     emit(want1, rec1, leaves + d.p0, leaf_count + b);
-    emit(act && want0 && want1, node, starts + (d.p0 - b), start_count + b);
+    emit(act && want0 && want1, make_int2(node, ci), starts + (d.p0 - b),
+         start_count + b);
   }
 }
 
@@ -672,13 +684,14 @@ struct RefitArgs {
   const TreeDesc* desc;
   const float* x;
   const int* perm;  // sorted local point indices
-  const int* parent;
+  const int2* parent;  // per radix-tree node: (parent*2 + side, parent's compact index)
   int* counter;
   const int* pref;  // [level-1][N]: level members before a leaf-order position
   const int4* leaves;
   const int* leaf_count;
-  const int* starts;  // per tree: nodes with two leaf children
+  const int2* starts;  // per tree: nodes with two leaf children (index, compact)
   const int* start_count;
+  const int* ovf;      // per tree: capacity overflow (tree not refitted)
   float4* pts;
   float4* lpts;
   int* qorder;
@@ -697,7 +710,7 @@ __device__ __forceinline__ int level_leaf_ref(int start, int count) {
 
 __device__ __forceinline__ Entry* node_entry(Entry* nodes, const TreeDesc& d,
                                              int level, int node, int slot) {
-  return nodes + d.node0 + ((size_t)level * (d.n - 1) + node) * 2 + slot;
+  return nodes + d.node0 + ((size_t)level * d.cap + node) * 2 + slot;
 }
 
 __device__ __forceinline__ Entry load_entry_cg(const Entry* e) {
@@ -729,36 +742,38 @@ __device__ __forceinline__ int arrive(int* p) {
 // children are level leaves holding at most `leaf` members together: the
 // members of a subtree are contiguous in the level's member array, the left
 // child's (slot 0 until this node swaps) first.
-__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
-  const int* par = a.parent + (d.p0 - b);
+__device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
+                      int ci) {
+  const int2* par = a.parent + (d.p0 - b);
   int* cnt = a.counter + (d.p0 - b);
-  // Karras depth is below 97 (64 key bits + 32 index bits); the bound only
-  // guards against a corrupted topology.
+  // i: the node's radix-tree index (parent links, arrival counters); ci: its
+  // compact index (stored entries).  Karras depth is below 97 (64 key bits +
+  // 32 index bits); the bound only guards against a corrupted topology.
   for (int step = 0; step < 128; ++step) {
     // issue every level's loads before any store (one L2 round trip)
     Entry u[kMaxLevels], v[kMaxLevels];
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
       if (l < a.levels) {
-        u[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 0));
-        v[l] = load_entry_cg(node_entry(a.nodes, d, l, i, 1));
+        u[l] = load_entry_cg(node_entry(a.nodes, d, l, ci, 0));
+        v[l] = load_entry_cg(node_entry(a.nodes, d, l, ci, 1));
       }
     }
-    int pc = i ? par[i] : 0;
+    const int2 pc = i ? par[i] : make_int2(0, 0);
     bool swap = v[0].minid < u[0].minid;
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
       if (l >= a.levels) break;
       if (swap) {
-        store_entry(node_entry(a.nodes, d, l, i, 0), v[l]);
-        store_entry(node_entry(a.nodes, d, l, i, 1), u[l]);
+        store_entry(node_entry(a.nodes, d, l, ci, 0), v[l]);
+        store_entry(node_entry(a.nodes, d, l, ci, 1), u[l]);
       }
       Entry e;
       e.lox = fminf(u[l].lox, v[l].lox); e.loy = fminf(u[l].loy, v[l].loy);
       e.loz = fminf(u[l].loz, v[l].loz); e.hix = fmaxf(u[l].hix, v[l].hix);
       e.hiy = fmaxf(u[l].hiy, v[l].hiy); e.hiz = fmaxf(u[l].hiz, v[l].hiz);
       e.minid = min(u[l].minid, v[l].minid);
-      e.ref = i;
+      e.ref = ci;
       if (l > 0 && u[l].ref < 0 && v[l].ref < 0) {
         int cu = level_leaf_count(u[l].ref), cv = level_leaf_count(v[l].ref);
         if (cu + cv <= a.leaf) {
@@ -771,10 +786,11 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i) {
       if (i == 0)
         a.root[b * a.levels + l] = e;
       else
-        store_entry(node_entry(a.nodes, d, l, pc >> 1, pc & 1), e);
+        store_entry(node_entry(a.nodes, d, l, pc.y, pc.x & 1), e);
     }
-    if (i == 0 || arrive(cnt + (pc >> 1)) == 0) return;
-    i = pc >> 1;
+    if (i == 0 || arrive(cnt + (pc.x >> 1)) == 0) return;
+    i = pc.x >> 1;
+    ci = pc.y;
   }
 }
 
@@ -798,6 +814,7 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
   int groups = (gridDim.x * blockDim.x) / G;
   const int b = blockIdx.y;
   const TreeDesc d = a.desc[b];
+  if (a.ovf[b]) return;  // kept nodes beyond capacity: the tree is not used
   int total = a.leaf_count[b];
   const float inf = __int_as_float(0x7f800000);
   for (int r = group; r < total; r += groups) {
@@ -860,7 +877,7 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
       t.ref = level_leaf_ref(start, members);
       if (gl == 0) {
         if (own)
-          store_entry(own + (size_t)l * (d.n - 1) * 2, t);
+          store_entry(own + (size_t)l * d.cap * 2, t);
         else
           a.root[b * a.levels + l] = t;
       }
@@ -876,11 +893,12 @@ __global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
 __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
   int b = blockIdx.y;
   TreeDesc d = a.desc[b];
-  const int* st = a.starts + (d.p0 - b);
+  if (a.ovf[b]) return;
+  const int2* st = a.starts + (d.p0 - b);
   int total = a.start_count[b];
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < total;
        r += gridDim.x * blockDim.x)
-    climb(a, d, b, st[r]);
+    climb(a, d, b, st[r].x, st[r].y);
 }
 
 // One warp per (level, tree): the top of the level's tree expanded breadth
@@ -891,12 +909,14 @@ __global__ void __launch_bounds__(256) climb_kernel(RefitArgs a) {
 __global__ void __launch_bounds__(32) cut_kernel(const TreeDesc* desc,
                                                  const Entry* nodes,
                                                  const Entry* root,
-                                                 int levels, int* cut) {
+                                                 int levels, int* cut,
+                                                 const int* ovf) {
   constexpr int CH = kCutMax / 32;  // list items per lane: c * 32 + lane
   __shared__ int next[kCutMax];
   const int l = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+  if (ovf[b]) return;  // the tree is not used
   const TreeDesc d = desc[b];
-  const Entry* nl = nodes + d.node0 + (size_t)l * (d.n - 1) * 2;
+  const Entry* nl = nodes + d.node0 + (size_t)l * d.cap * 2;
   const unsigned lt = (1u << lane) - 1u;
   const int rref = root[b * levels + l].ref;
   int cnt = 1;
@@ -1067,10 +1087,10 @@ struct BuildScratch {
   int* hist = nullptr;
   unsigned* bounds = nullptr;
   int4* leaves = nullptr;  // leaf records; at most one per point
-  int* parent = nullptr;
+  int2* parent = nullptr;  // per radix-tree node: (parent*2 + side, parent's compact index)
   int* counter = nullptr;  // arrival counters + leaf-record and climb-start counts
   int* pref = nullptr;
-  int* starts = nullptr;
+  int2* starts = nullptr;  // climb starts: (radix-tree index, compact index)
 };
 
 namespace {
@@ -1079,6 +1099,12 @@ int max_tiles_of(const Forest* f) { return blocks_for(f->max_n, kSortTile); }
 
 long long inner_nodes(const Forest* f) { return std::max<long long>(1, (long long)f->N - f->B); }
 
+// Every tree is keyed and sorted by one cluster launch (else the
+// multi-launch sort, which needs the double buffers and digit histograms).
+bool cluster_path(const Forest* f) {
+  return GSA_CLUSTER_SORT && f->max_n <= kClusterMaxPoints;
+}
+
 cudaError_t alloc_scratch(const Forest* f, BuildScratch* sc, cudaStream_t s) {
   const long long N = f->N, B = f->B, inner = inner_nodes(f);
   cudaError_t e = cudaSuccess;
@@ -1086,15 +1112,17 @@ cudaError_t alloc_scratch(const Forest* f, BuildScratch* sc, cudaStream_t s) {
     if (!e) e = pool_alloc(p, bytes, s);
   };
   alloc((void**)&sc->pref, sizeof(int) * std::max<long long>(1, (f->levels - 1) * N));
-  alloc((void**)&sc->starts, sizeof(int) * inner);
+  alloc((void**)&sc->starts, sizeof(int2) * inner);
   alloc((void**)&sc->vals, sizeof(int) * N);
   alloc((void**)&sc->keys, sizeof(uint64_t) * N);
-  alloc((void**)&sc->keys2, sizeof(uint64_t) * N);
-  alloc((void**)&sc->vals2, sizeof(int) * N);
-  alloc((void**)&sc->hist, sizeof(int) * 256ll * B * max_tiles_of(f));
+  if (!cluster_path(f)) {
+    alloc((void**)&sc->keys2, sizeof(uint64_t) * N);
+    alloc((void**)&sc->vals2, sizeof(int) * N);
+    alloc((void**)&sc->hist, sizeof(int) * 256ll * B * max_tiles_of(f));
+  }
   alloc((void**)&sc->bounds, sizeof(unsigned) * 6 * B);
   alloc((void**)&sc->leaves, sizeof(int4) * N);
-  alloc((void**)&sc->parent, sizeof(int) * inner);
+  alloc((void**)&sc->parent, sizeof(int2) * inner);
   alloc((void**)&sc->counter, sizeof(int) * (inner + 2 * B));
   return e;
 }
@@ -1155,6 +1183,7 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
   int *vals = sc.vals, *vals2 = sc.vals2, *hist = sc.hist;
   int* counter = sc.counter;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int) * (inner + 2 * B), s);
+  if (!e) e = cudaMemsetAsync(f->ovf, 0, sizeof(int) * 2 * B, s);
   if (e) return e;
   int* leaf_count = counter + inner;
   int* start_count = leaf_count + B;
@@ -1169,13 +1198,13 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
   int launches = (B + 255) / 256;
   dim3 gs(max_tiles, B);
   dim3 gk(blocks_for(std::max(1, max_n - 1), 256), B);
-  if (GSA_CLUSTER_SORT && max_n <= kClusterMaxPoints) {
+  if (cluster_path(f)) {
     // one cluster per tree: bounds, keys, sort and member offsets
     e = launch_cluster_sort(f, x, sc, s);
     if (e) return e;
     karras_kernel<<<gk, 256, 0, s>>>(f->desc, sc.keys, sc.parent, counter,
                                      f->leaf, sc.leaves, leaf_count, sc.starts,
-                                     start_count);
+                                     start_count, f->ovf);
     launches += 2;
   } else {
     dim3 g(std::min(blocks_for(max_n, 1024), 64), B);
@@ -1197,7 +1226,7 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
     }
     karras_kernel<<<gk, 256, 0, s>>>(f->desc, keys, sc.parent, counter,
                                      f->leaf, sc.leaves, leaf_count, sc.starts,
-                                     start_count);
+                                     start_count, f->ovf);
     launches += 2 + 3 * passes + 1;
     if (f->levels > 1) {
       // members of each prefix level before every sorted position
@@ -1221,6 +1250,7 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
   ra.leaf_count = leaf_count;
   ra.starts = sc.starts;
   ra.start_count = start_count;
+  ra.ovf = f->ovf;
   ra.pts = f->pts;
   ra.lpts = f->lpts;
   ra.qorder = f->qorder;
@@ -1239,7 +1269,7 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
     leaf_kernel<32><<<gl, 256, 0, s>>>(ra);
   climb_kernel<<<dim3(climb_grid(max_n), B), 256, 0, s>>>(ra);
   cut_kernel<<<dim3(f->levels, B), 32, 0, s>>>(f->desc, f->nodes, f->root,
-                                               f->levels, f->cut);
+                                               f->levels, f->cut, f->ovf);
   launches += 3;
   count_launches(launches);
   return cudaGetLastError();
@@ -1271,7 +1301,8 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
     d.n = n;
     d.node0 = (int)node_entries;
     d.q0 = (int)q_total;
-    node_entries += 2ll * f->levels * (n - 1);
+    d.cap = node_capacity(n, f->leaf);
+    node_entries += 2ll * f->levels * d.cap;
     for (int l = 0; l < f->levels; ++l) q_total += level_size(n, l);
     N += n;
     max_n = std::max(max_n, n);
@@ -1296,6 +1327,7 @@ cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
   alloc((void**)&f->lpts, sizeof(float4) * std::max<long long>(1, q_total - N));
   alloc((void**)&f->wrank, sizeof(int) * N * f->levels);
   alloc((void**)&f->cut, sizeof(int) * kCutStride * B * f->levels);
+  alloc((void**)&f->ovf, sizeof(int) * 2 * B);
   BuildScratch sc;
   if (!e) e = alloc_scratch(f, &sc, s);
   if (!e) e = enqueue_build(f, x, sc, s);
@@ -1330,7 +1362,7 @@ cudaError_t free_forest(Forest* f, cudaStream_t s) {
   if (!f) return cudaSuccess;
   cudaError_t e = cudaSuccess;
   void* bufs[] = {f->desc,  f->pts,    f->lpts,  f->nodes,
-                  f->root,  f->qorder, f->wrank, f->cut};
+                  f->root,  f->qorder, f->wrank, f->cut, f->ovf};
   for (void* p : bufs) {
     cudaError_t fe = pool_free(p, s);
     if (!e) e = fe;

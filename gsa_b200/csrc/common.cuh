@@ -43,9 +43,30 @@ static_assert(sizeof(Entry) == 32, "entry is 32 bytes");
 struct TreeDesc {
   int p0;     // first point of this tree in pts / x (and first row of seg)
   int n;      // number of support points
-  int node0;  // first Entry of this tree in `nodes` (levels*(n-1)*2 entries)
+  int node0;  // first Entry of this tree in `nodes` (levels*cap*2 entries)
   int q0;     // first slot of this tree in `qorder` (sum of level sizes)
+  int cap;    // stored internal nodes: the kept radix-tree nodes (those over
+              // more than `leaf` points) get compact indices below cap
 };
+
+// Compact-node capacity of a tree of n points with leaves of at most `leaf`
+// points.  A kept node has two children and the leaf records partition the
+// points, so kept = records - 1 < 3n/leaf whenever the records average more
+// than leaf/3 points (and always for leaf <= 3); measured on rooms, clustered
+// scenes with duplicates and uniform clouds the kept count is 0.66-0.80 of
+// 2n/leaf + 64.  A tree whose kept nodes exceed cap is flagged at build time
+// and its queries take the exact scan.  GSA_NODE_CAP_LIMIT (a test build)
+// caps it further so that the overflow path runs.
+#ifndef GSA_NODE_CAP_LIMIT
+#define GSA_NODE_CAP_LIMIT 0x7fffffff
+#endif
+__host__ __device__ inline int node_capacity(int n, int leaf) {
+  long long c = 3ll * ((n + (long long)leaf - 1) / leaf) + 64;
+  const long long m = n > 1 ? n - 1 : 1;
+  if (c > m) c = m;
+  if (c > GSA_NODE_CAP_LIMIT) c = GSA_NODE_CAP_LIMIT;
+  return (int)(c < 1 ? 1 : c);
+}
 
 struct ForestView {
   const TreeDesc* desc;
@@ -58,6 +79,8 @@ struct ForestView {
                         // point's leaf-order position
   const int* cut;       // [tree][level][kCutStride]: count, then up to kCutMax
                         // entry indices (-1: the root) that cover the tree
+  const int* ovf;       // [tree]: 1 when the kept nodes exceeded the tree's
+                        // capacity (the tree is unusable: exact scans)
   const float* x;       // borrowed original coordinates (AoS, 3 floats)
   int levels;           // 4 for prefix trees, 1 otherwise
 };

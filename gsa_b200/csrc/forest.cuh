@@ -25,6 +25,7 @@ struct Forest {
   int* qorder = nullptr;
   int* wrank = nullptr;
   int* cut = nullptr;
+  int* ovf = nullptr;  // [0, B): capacity overflow flags; [B, 2B): kept counts
   const float* x = nullptr;  // borrowed
   BuildScratch* scratch = nullptr;  // kept build temporaries (rebuild_forest)
 
@@ -38,6 +39,7 @@ struct Forest {
     v.qorder = qorder;
     v.wrank = wrank;
     v.cut = cut;
+    v.ovf = ovf;
     v.x = x;
     v.levels = levels;
     return v;

@@ -98,7 +98,8 @@ __device__ __forceinline__ int level_offset(int n, int l) {
 
 struct Slot {
   int qbase, qin, Q, m, slots, lev;
-  const int* order;
+  const int* order;  // slot -> query (null: identity)
+  bool ovf;          // the tree overflowed its node capacity: exact scans
 };
 
 __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
@@ -112,13 +113,15 @@ __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
   int ql = s.Q <= d.n ? query_level(d.n, a.f.levels, s.Q) : 0;
   s.slots = s.Q <= d.n ? level_size(d.n, ql) : s.Q;
   s.order = a.f.qorder + d.q0 + level_offset(d.n, ql);
+  s.ovf = a.f.ovf[b] != 0;
+  if (s.ovf) s.order = nullptr;  // the build wrote no query order
   return s;
 }
 
 __device__ __forceinline__ int slot_query(const Slot& s, const TreeDesc& d,
                                           int t) {
   if (t >= s.slots) return -1;
-  int qi = t < d.n ? __ldg(s.order + t) : t;
+  int qi = t < d.n && s.order ? __ldg(s.order + t) : t;
   return qi < s.Q ? qi : -1;
 }
 
@@ -278,7 +281,7 @@ __device__ __forceinline__ RadiusCtx radius_ctx(const QArgs& a,
                                                 const TreeDesc& d, int b,
                                                 const Slot& s) {
   RadiusCtx c;
-  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * d.cap * 2;
   c.root = a.f.root + b * a.f.levels + s.lev;
   c.pts = level_pts(a.f, d, s.lev);
   c.xs = a.f.x + 3ll * d.p0;
@@ -312,6 +315,15 @@ __global__ void __launch_bounds__(kQThreads)
   }
   RadiusCtx c = radius_ctx(a, d, b, s);
   int* L = lists[warp][lane];
+  if (s.ovf) {  // tree-uniform: no usable tree, every query scans
+    int count = 0;
+    if (active) {
+      atomicAdd(a.fallback, 1);
+      count = scan_ordered(c, px, py, pz, L);
+    }
+    write_rows4(a.out, &lists[warp][0][0], 33, qi, count, s.qbase, c.K, lane);
+    return;
+  }
   bool overflow = false;
   int count = walk_ordered<STACK>(c, active, px, py, pz, L, stack[warp], overflow);
   if (overflow && active) {
@@ -368,7 +380,7 @@ struct KnnCtx {
 __device__ __forceinline__ KnnCtx knn_ctx(const QArgs& a, const TreeDesc& d,
                                           int b, const Slot& s) {
   KnnCtx c;
-  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * (d.n - 1) * 2;
+  c.nodes = a.f.nodes + d.node0 + (size_t)s.lev * d.cap * 2;
   c.root = a.f.root + b * a.f.levels + s.lev;
   c.pts = level_pts(a.f, d, s.lev);
   c.xs = a.f.x + 3ll * d.p0;
@@ -484,6 +496,13 @@ __global__ void __launch_bounds__(kQThreads)
     pz = qp[2];
   }
   KnnCtx c = knn_ctx(a, d, b, s);
+  if (s.ovf) {  // tree-uniform: no usable tree, every query scans
+    if (active) {
+      atomicAdd(a.fallback, 1);
+      write_top3(a, s, qi, scan_knn3(c, px, py, pz));
+    }
+    return;
+  }
   Top3 t = empty_top3();
   bool overflow = walk_knn3<STACK>(c, active, px, py, pz, t, stack[warp]);
   if (overflow && active) {
@@ -840,6 +859,16 @@ __global__ void __launch_bounds__(kFWarps * 32)
   }
   RadiusCtx c = radius_ctx(a, d, b, s);
   int* H = W.buf[lane];
+  if (s.ovf) {  // tree-uniform: no usable tree, every query scans
+    int count = 0;
+    if (active) {
+      atomicAdd(a.fallback, 1);
+      count = scan_ordered(c, px, py, pz, H);
+    }
+    write_rows4(a.out, &W.buf[0][0], kPacketCap + 1, qi, count, s.qbase, c.K,
+                lane);
+    return;
+  }
   // Queries with a non-finite coordinate have no hits (their squared
   // distances are inf or NaN) and stay out of the packet box.
   const bool live = active && finite3(px, py, pz);
@@ -916,6 +945,13 @@ __global__ void __launch_bounds__(kFWarps * 32)
     pz = qp[2];
   }
   KnnCtx c = knn_ctx(a, d, b, s);
+  if (s.ovf) {  // tree-uniform: no usable tree, every query scans
+    if (active) {
+      atomicAdd(a.fallback, 1);
+      write_top3(a, s, qi, scan_knn3(c, px, py, pz));
+    }
+    return;
+  }
   const int m = c.m;
   const float inf = __int_as_float(0x7f800000);
   // Non-finite queries have no finite distance: their rows stay (inf, 0).

@@ -51,7 +51,7 @@ def test_only_declared_symbols_are_exported():
 
 
 def test_test_variant_library_exports_same_abi():
-    for name in ("gsa_bvh_walk", "gsa_bvh_ordered", "gsa_bvh_stack4"):
+    for name in ("gsa_bvh_walk", "gsa_bvh_ordered", "gsa_bvh_stack4", "gsa_bvh_cap8"):
         p = _library.path(name)
         assert p.is_file(), name
         assert exported(p) == declared(HEADERS["gsa_bvh"]), name

@@ -261,10 +261,11 @@ def test_pool_memory_next_to_reference(gsa, workload):
     """Native-pool high-water marks of one scene's hierarchy through each
     session (``pool_memory`` after ``pool_reset_peak``, both libraries'
     own pools, ``gsa/runtime.py:33-40``): the figures the reference's
-    memory-overhead comparison reads.  The forest stores two 32-byte child
-    entries per level for every one of the n-1 radix-tree nodes (about a
-    tenth are used), so it holds more than the reference's cuBQL tree; the
-    test pins that ratio so it cannot grow unnoticed."""
+    memory-overhead comparison reads.  The forest stores child entries for
+    its kept radix-tree nodes only (a capacity of 3n/leaf + 64 per tree) and
+    per-level member arrays; measured 1.30x / 1.41x the reference's peak on
+    the room / 1M-point room.  The test pins the ratio below 2 so it cannot
+    grow unnoticed."""
     from gsa_b200 import QuerySession, hierarchy as hz, runtime, scenes
 
     if workload == "room":
@@ -283,6 +284,6 @@ def test_pool_memory_next_to_reference(gsa, workload):
     print(f"\npool peaks {workload} ({sizes[0]} points): {json.dumps(peaks)}")
     ours = peaks["ours"]["native_pool_used_peak_bytes"]
     ref = peaks["reference"]["native_pool_used_peak_bytes"]
-    assert 0 < ref and 0 < ours <= 16 * ref
+    assert 0 < ref and 0 < ours <= 2 * ref
     for p in peaks.values():
         assert p["native_pool_reserved_peak_bytes"] >= p["native_pool_used_peak_bytes"]

@@ -209,7 +209,28 @@ def test_small_stack_fallback_is_exact_and_counted():
     h.free()
 
 
-@pytest.mark.parametrize("lib_name", LIBS)
+@pytest.mark.parametrize("n,leaf", [(5000, 4), (5000, 16), (700, 32), (60, 4)])
+def test_node_capacity_overflow_is_exact_and_counted(n, leaf):
+    """A tree whose kept nodes exceed its stored-node capacity (8 in this
+    build) is flagged by the build; its queries take the exact scans, are
+    counted as fallbacks and equal the oracle on every level."""
+    rng = np.random.default_rng(16 + n + leaf)
+    x = rng.random((n, 3)).astype(np.float32)
+    lib = abi.bvh_lib("gsa_bvh_cap8")
+    h = abi.Handle(lib, cuda(x), prefix=1, leaf=leaf)
+    assert h.code == 0
+    for level in range(4):
+        m = n >> (2 * level)
+        if m < 3:
+            break
+        fb = check_ball(h, x, x[:m], m, level, 0.2, 32)
+        assert fb.item() > 0
+        fb = check_knn(h, x, x[:m], m, level)
+        assert fb.item() > 0
+    h.free()
+
+
+@pytest.mark.parametrize("lib_name", LIBS + ["gsa_bvh_cap8"])
 def test_forest_batch_equals_oracle_per_scene(lib_name):
     rng = np.random.default_rng(15)
     sizes = [1, 3, 17, 700, 4096, 2500, 12000]
