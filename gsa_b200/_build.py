@@ -11,7 +11,9 @@ and builds every tree with the multi-launch sort instead of the cluster sort,
 ``gsa_bvh_stack4.so`` has a 4-entry traversal stack (8-entry frontier)
 so that the per-query-walk and exact full-scan fallbacks are exercised, and
 ``gsa_bvh_cap8.so`` caps every tree's stored nodes at 8 so that the
-node-capacity overflow path (exact scans) is exercised.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
+node-capacity overflow path (exact scans) is exercised; ``gsa_fps_drop.so``
+(FPS only) has one grid block that never arrives at the FPS grid barrier,
+so the barrier's bounded wait runs out and reports its error flag.  Flags keep GSA's arithmetic contract (``scripts/build.py:25-34``:
 ``--fmad=false --ftz=false``); the kernels also use explicit round-to-nearest
 intrinsics for every distance operation.
 """
@@ -55,6 +57,10 @@ LIBS = {
     # every tree of more than ~100 points overflows a node capacity of 8, so
     # its queries take the exact scans
     "gsa_bvh_cap8": (_BVH, ["-DGSA_NODE_CAP_LIMIT=8"] + _WALK_ONLY),
+    # FPS only: one block of the cooperative grid never arrives at the
+    # barrier and the others' waits are short, so the timeout path runs
+    "gsa_fps_drop": (["launches.cu", "fps.cu"],
+                     ["-DGSA_FPS_DROP_BLOCK=1", "-DGSA_FPS_BARRIER_SPINS=65536"]),
 }
 
 

@@ -89,7 +89,16 @@ __global__ void __launch_bounds__(kFpsThreads)
 // selects the global best, and a grid barrier separates steps.  The winner
 // slot is triple-buffered so it can be cleared two steps ahead without a
 // second barrier.
-constexpr long long kBarrierSpins = 1ll << 24;
+#ifndef GSA_FPS_BARRIER_SPINS
+#define GSA_FPS_BARRIER_SPINS (1ll << 24)
+#endif
+constexpr long long kBarrierSpins = GSA_FPS_BARRIER_SPINS;
+// Test builds only: the block with this index leaves the kernel at its first
+// barrier without arriving, so every other block's bounded wait runs out and
+// the call reports the error flag (-1: none).
+#ifndef GSA_FPS_DROP_BLOCK
+#define GSA_FPS_DROP_BLOCK -1
+#endif
 
 __device__ __forceinline__ unsigned order_key(float f) {
   unsigned u = __float_as_uint(f);
@@ -172,6 +181,7 @@ __global__ void __launch_bounds__(kFpsThreads)
       }
       if (lane == 0) atomicMax(best + it % 3, mine);
     }
+    if (GSA_FPS_DROP_BLOCK >= 0 && (int)blockIdx.x == GSA_FPS_DROP_BLOCK) return;
     grid_barrier(bar, bar + 1, err);
     if (*reinterpret_cast<volatile int*>(err)) return;
     unsigned long long win = *reinterpret_cast<volatile unsigned long long*>(best + it % 3);

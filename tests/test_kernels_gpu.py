@@ -365,6 +365,33 @@ def test_fps_cooperative_grid_matches_single_block():
     assert torch.equal(small, large)
 
 
+def test_fps_grid_barrier_timeout_sets_error_and_returns():
+    """In a test build where one block of the cooperative FPS grid leaves
+    before its first barrier, every other block's bounded wait runs out: the
+    kernel ends, the error flag reads 1, and the context stays usable (the
+    regular library then computes the same order correctly)."""
+    from gsa_b200 import _library, scenes
+
+    p, st = scenes.room(9, n=6000)
+    x = torch.from_numpy(p).cuda()
+    P_, I_ = ctypes.c_void_p, ctypes.c_int
+    drop = _library.load("gsa_fps_drop")
+    drop.fps_order_large.argtypes = [I_, P_, I_, P_, P_, P_, P_]
+    drop.fps_order_large.restype = I_
+    order = torch.full((len(p),), -1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(16, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    code = drop.fps_order_large(len(p), x.data_ptr(), int(st), order.data_ptr(), scratch.data_ptr(),
+                                err.data_ptr(), abi.stream())
+    assert code == 0
+    torch.cuda.synchronize()
+    assert err.item() == 1
+    assert (order[1:] == -1).all()  # no step completed after the first barrier
+    small = scenes.fps_order(x, st, large=False)
+    large = scenes.fps_order(x, st, large=True)
+    assert torch.equal(small, large)
+
+
 def test_furthest_point_sample_op_matches_sequential_rule():
     """The PointNet++-style FPS op: first m indices from index 0, exact FP32
     distances, ties to the lowest index (a lattice makes many exact ties),
