@@ -322,8 +322,10 @@ __global__ void __launch_bounds__(kSortThreads)
 // distributed shared memory and scatter keys straight into the destination
 // CTA's buffer, with cluster barriers between the steps.  Inside a tile each
 // warp owns kCItems * 32 consecutive positions, so a warp ranks its items
-// against its own running digit counts (match_any, no block barrier per
-// item row) and one scan over the warps per digit places them.  The
+// against its own running digit counts (peers found by eight ballots over
+// the digit bits, no block barrier per item row) and one scan over the warps
+// per digit places them; reads of the other CTAs' bounds, histograms and
+// member counts are issued together, one remote round trip each.  The
 // multi-launch path (bounds_kernel ... member_prefix, 14 launches) does the
 // same work for larger trees.  Keys are at most 30 bits here (morton_bits of
 // n <= 32768 is 10), so they live in shared memory as 32-bit words; the output
@@ -342,6 +344,7 @@ struct ClusterSmem {
   int hist[256];           // this tile's digit counts (read by the cluster)
   int goff[256];
   unsigned bnd[6];         // this tile's bounds keys (read by the cluster)
+  unsigned gbnd[6];        // the tree's bounds keys
   int lcnt[kMaxLevels];    // this tile's member counts (read by the cluster)
   int wsum[kCWarps];
   int wmem[kCWarps][kMaxLevels];  // members per warp, then their exclusive scan
@@ -402,14 +405,22 @@ __global__ void __launch_bounds__(kCThreads)
     }
   }
   cluster.sync();
-  unsigned bk[6] = {~0u, ~0u, ~0u, 0u, 0u, 0u};
-  for (int c = 0; c < cs; ++c) {
-    const unsigned* rb = cluster.map_shared_rank(S.bnd, c);
-    for (int k = 0; k < 3; ++k) {
-      bk[k] = min(bk[k], rb[k]);
-      bk[3 + k] = max(bk[3 + k], rb[3 + k]);
-    }
+  // thread k < 6 reads bound k of every CTA of the cluster (all loads in
+  // flight at once) and leaves the cluster-wide value in gbnd
+  if (tid < 6) {
+    unsigned v[kClusterMax];
+#pragma unroll
+    for (int c = 0; c < kClusterMax; ++c)
+      v[c] = c < cs ? cluster.map_shared_rank(S.bnd, c)[tid] : S.bnd[tid];
+    unsigned r = v[0];
+#pragma unroll
+    for (int c = 1; c < kClusterMax; ++c) r = tid < 3 ? min(r, v[c]) : max(r, v[c]);
+    S.gbnd[tid] = r;
   }
+  __syncthreads();
+  unsigned bk[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) bk[k] = S.gbnd[k];
 
   // 2. Morton keys (as morton_kernel) and local indices, in registers
   unsigned key[kCItems];
@@ -446,7 +457,14 @@ __global__ void __launch_bounds__(kCThreads)
     for (int j = 0; j < kCItems; ++j) {
       const bool valid = base + cpos(warp, j, lane) < n;
       const int digit = valid ? (int)((key[j] >> shift) & 255) : 256 + lane;
-      const unsigned peers = __match_any_sync(kFull, digit);
+      // lanes with this lane's digit: eight ballots over the digit bits
+      unsigned peers = __ballot_sync(kFull, valid);
+#pragma unroll
+      for (int bit = 0; bit < 8; ++bit) {
+        const unsigned bb = __ballot_sync(kFull, (digit >> bit) & 1);
+        peers &= ((digit >> bit) & 1) ? bb : ~bb;
+      }
+      if (!valid) peers = 1u << lane;
       const int lower = __popc(peers & lt);
       rk[j] = valid ? wc[digit] + lower : 0;
       __syncwarp();
@@ -466,11 +484,14 @@ __global__ void __launch_bounds__(kCThreads)
     cluster.sync();  // every tile's histogram complete, every buffer read
     if (tid < 256) {
       // digits below tid over the whole tree, plus digit tid in lower tiles
-      int below = 0, total = 0;
-      for (int c = 0; c < cs; ++c) {
-        const int v = cluster.map_shared_rank(S.hist, c)[tid];
-        total += v;
-        if (c < rank) below += v;
+      int below = 0, total = 0, v[kClusterMax];
+#pragma unroll
+      for (int c = 0; c < kClusterMax; ++c)  // every remote load in flight
+        v[c] = c < cs ? cluster.map_shared_rank(S.hist, c)[tid] : 0;
+#pragma unroll
+      for (int c = 0; c < kClusterMax; ++c) {
+        total += v[c];
+        below += c < rank ? v[c] : 0;
       }
       int incl = total;  // inclusive scan of totals over digits (8 warps)
       for (int o = 1; o < 32; o <<= 1) {
@@ -544,7 +565,9 @@ __global__ void __launch_bounds__(kCThreads)
     for (int l = 1; l < kMaxLevels; ++l) {
       if (l >= levels) break;
       int run = S.wmem[warp][l];
-      for (int c = 0; c < rank; ++c) run += cluster.map_shared_rank(S.lcnt, c)[l];
+#pragma unroll
+      for (int c = 0; c < kClusterMax; ++c)  // every remote load in flight
+        run += c < rank ? cluster.map_shared_rank(S.lcnt, c)[l] : 0;
 #pragma unroll
       for (int j = 0; j < kCItems; ++j) {
         const int i = base + cpos(warp, j, lane);
