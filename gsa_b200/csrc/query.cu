@@ -533,7 +533,14 @@ __global__ void __launch_bounds__(kQThreads)
 // a buffer that could overflow is first cut to its best three (lowering B).
 // Every point of the final answer satisfies the hit test at every moment, so
 // both answers are exact.
-constexpr int kFWarps = 4;
+// Warps (packets) per frontier block.  Two rather than four: a block's
+// slot is freed when its slowest packet ends, so smaller blocks waste less
+// of an SM on finished warps (64 scenes: 3NN stage 0 436 -> 422 us, radius
+// 592 -> 587 us; one warp per block hits the 32-block limit first).
+#ifndef GSA_FRONTIER_WARPS
+#define GSA_FRONTIER_WARPS 2
+#endif
+constexpr int kFWarps = GSA_FRONTIER_WARPS;
 constexpr int kPacketCap = 32;  // radius hits per query; holds a K-list (K<=32)
 constexpr int kCandCap = 35;    // 3NN candidates: three kept + a leaf of 32
 constexpr int kWindow = 16;     // 3NN bound: 2*kWindow members (3NN stages
@@ -1172,18 +1179,21 @@ int sm_count() {
 
 // Queries per warp of a frontier launch.  A packet of 32 queries shares one
 // walk of the tree, which is the cheapest per query; a launch whose grid
-// would hold fewer than four blocks per SM (a single scene) takes narrower
+// would hold fewer than 16 warps per SM (a single scene) takes narrower
 // packets (16, then 8 queries) so that more warps walk at once: each walk is
 // shorter and the launch's latency falls, at some cost in instructions per
 // query (one scene of 24,000 points: radius stage 0 108 -> 90 us, 3NN stage
 // 0 57 -> 51 us; 8 or more such scenes keep 32).
 constexpr int kPacketMin = 8;
-constexpr int kPacketFill = 4;  // blocks per SM below which packets narrow
+constexpr int kPacketFillWarps = 16;  // warps per SM below which packets narrow
+// Packets (warps) of a tree launch at `pw` queries per warp.
+long long launch_warps(const Forest& f, long long slots, int pw) {
+  return (slots + kFWarps * pw - 1) / (kFWarps * pw) * kFWarps * f.B;
+}
 int packet_width(const Forest& f, long long slots) {
   int pw = 32;
   while (pw > kPacketMin &&
-         (slots + kFWarps * pw - 1) / (kFWarps * pw) * f.B <
-             (long long)kPacketFill * sm_count())
+         launch_warps(f, slots, pw) < (long long)kPacketFillWarps * sm_count())
     pw >>= 1;
   return pw;
 }
@@ -1204,8 +1214,7 @@ bool prefer_scan(const Forest& f, const QuerySet& qs, int scan_max,
   if (scan_max <= 0) return false;
   long long slots = max_slots(f, qs.qseg_host, qs.nq);
   const int pw = narrow ? packet_width(f, slots) : 32;
-  long long blocks = (slots + kFWarps * pw - 1) / (kFWarps * pw) * f.B;
-  if (blocks >= sm_count()) return false;
+  if (launch_warps(f, slots, pw) >= 4ll * sm_count()) return false;
   long long q = qs.qseg_host ? qs.qseg_host[f.B] : qs.nq;
   return q * (long long)m <= (1ll << 26);
 }
