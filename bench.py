@@ -1010,8 +1010,8 @@ def main():
 
     torch.cuda.set_device(local)
     if world > 1:
-        # keep stdout to the one JSON line (NCCL may print its version)
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        # stdout carries the one JSON line: NCCL_DEBUG is left unset here
+        # (at WARN, NCCL prints its version line on stdout)
         dist.init_process_group(
             "nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local)
         )
