@@ -95,6 +95,8 @@ def parse():
     p.add_argument("--scenes", type=int, default=SCENES, help="scenes of the whole job")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-configs", action="store_true",
+                   help="skip the 1M-point room and the clustered stress scene (N=1 runs)")
     p.add_argument("--write-traffic-profile", metavar="NCU_CSV",
                    help="write the DRAM traffic profile from an ncu --csv capture of the frontier "
                         "kernels' first hierarchy run (see TRAFFIC_SOURCES) and exit")
@@ -747,6 +749,8 @@ def run_ours(args, rank, world, local):
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(X[0].cpu().numpy(), out)
+    if world == 1 and not args.no_configs:
+        line["configs"] = other_configs(dev, flush)
     step.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -968,6 +972,85 @@ def concurrent_sessions(host_x, host_flat, steps, world, dev, threads=2):
         "threads": threads,
         "steps": steps,
     }
+
+
+def other_configs(dev, flush, steps=5):
+    """The other device workloads, each timed on its own (CUDA events per
+    step, L2 flushed between steps, inputs resident): the 1,000,000-point
+    room (20 x 20 x 3 m, FPS-ordered, prefixes 1M/250k/62.5k/15.6k/3.9k,
+    r = 0.05/0.1/0.2/0.4, K = 32) through the batched engine with one scene,
+    and the 200,000-point clustered stress scene (50,000 radius queries at
+    r = 0.25, K = 32, against all points; 3NN of all 200,000 points against
+    the first 50,000) through the forest API.  Stage times from a
+    serialized pass; `radius_gbs` = 140 algorithmic bytes per radius row
+    over the radius stages' time."""
+    import torch
+
+    from gsa_b200 import hierarchy as hz, scenes
+    from gsa_b200.forest import Forest
+
+    res = {}
+    # 1M-point room: scene generation (FPS order) outside any timing
+    p, start = scenes.room(11, n=1_000_000, box=(20.0, 20.0, 3.0))
+    x = torch.from_numpy(p).to(dev)
+    order = scenes.fps_order(x, start)
+    X = x[order.to(dev)].contiguous()[None]
+    eng = hz.Batch(hz.LARGE_SIZES, hz.LARGE_RADII)
+    out = eng.allocate(1, dev)
+    for _ in range(2):
+        eng.run(X, out)
+    ms = statistics.median(timed_steps(lambda: eng.run(X, out), steps, flush, torch))
+    timer = hz.StageTimer()
+    for _ in range(steps):
+        flush.zero_()
+        eng.run(X, out, timer, concurrent=False)
+    torch.cuda.synchronize()
+    stage = {k: v / steps for k, v in timer.totals().items()}
+    ball, hit, nn = hz.unit_counts(hz.LARGE_SIZES)
+    radius_ms = sum(stage.get(f"ball{s}", 0.0) for s in range(4))
+    res["large_room"] = {
+        "workload": "1,000,000-point room (20 x 20 x 3 m), one scene, prefixes "
+                    + "/".join(str(v) for v in hz.LARGE_SIZES) + ", r = "
+                    + "/".join(str(v) for v in hz.LARGE_RADII) + ", K = 32, reuse rows, 3NN per stage",
+        "rows_per_step": ball + hit + nn,
+        "ms_per_step": ms,
+        "rows_per_s": (ball + hit + nn) / (ms / 1000.0),
+        "stages_ms": {k: round(v, 4) for k, v in stage.items()},
+        "radius_gbs": 140 * ball / (radius_ms / 1000.0) / 1e9 if radius_ms else None,
+    }
+    del X, out, x
+    # clustered stress scene
+    pts, info = scenes.clustered(seed=0)
+    xc = torch.from_numpy(pts).to(dev)
+    n, nq = len(pts), info["queries"]
+    f = Forest(xc, [0, n], prefix=True)
+    rows = torch.empty((nq, 32), dtype=torch.int32, device=dev)
+    d = torch.empty((n, 3), device=dev)
+    ids = torch.empty((n, 3), dtype=torch.int32, device=dev)
+    level = next(l for l in range(4) if n >> (2 * l) == nq)
+    calls = {
+        "build": lambda: f.rebuild(xc),
+        "radius": lambda: f.ball_prefix(nq, 0, 0.25, 32, rows, m=n),
+        "nn3": lambda: f.query_prefix(n, level, d, ids),
+    }
+    for _ in range(2):
+        for c in calls.values():
+            c()
+    stage = {k: statistics.median(timed_steps(c, steps, flush, torch)) for k, c in calls.items()}
+    total = sum(stage.values())
+    res["clustered_stress"] = {
+        "workload": f"{n} clustered points (50 clusters, sigma 1e-3, 20 % duplicates, 5 % at exactly r), "
+                    f"{nq} radius queries r = 0.25 K = 32 against all points, 3NN of all points against the first {nq}",
+        "rows_per_step": nq + n,
+        "ms_per_step": total,
+        "rows_per_s": (nq + n) / (total / 1000.0),
+        "stages_ms": {k: round(v, 4) for k, v in stage.items()},
+        "radius_gbs": 140 * nq / (stage["radius"] / 1000.0) / 1e9,
+        "fallback_queries": int(f.fallback.item()),
+    }
+    f.close()
+    torch.cuda.synchronize()
+    return res
 
 
 def cpu_baseline(P, out):

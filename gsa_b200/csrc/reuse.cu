@@ -13,6 +13,7 @@
 // torch.equal: NaN never equals, -0 equals +0.
 #include <cooperative_groups.h>
 #include <algorithm>
+#include <atomic>
 #include "common.cuh"
 
 namespace gsa {
@@ -235,6 +236,54 @@ __global__ void __launch_bounds__(kStageThreads)
   }
 }
 
+// Grid-wide form of the same check for batches whose clusters would not
+// cover the SMs (a few large scenes): every block compares its share of
+// scene p's support and ORs the two flags (zeroed first) atomically; the
+// rows follow in reuse_rows_batch_kernel.
+__global__ void __launch_bounds__(kStageThreads)
+    prefix_mismatch_kernel(const float* a, long long a_stride, const float* b,
+                           long long b_stride, long long ns, long long nq,
+                           int* flags) {
+  const long long p = blockIdx.y;
+  const float* u = a + p * a_stride;
+  const float* v = b + p * b_stride;
+  const long long t = (long long)blockIdx.x * kStageThreads + threadIdx.x;
+  const long long stride = (long long)gridDim.x * kStageThreads;
+  bool ds = false, dq = false;
+  long long tail = 0;
+  if (((((uintptr_t)u) | ((uintptr_t)v)) & 15) == 0) {
+    const float4* u4 = reinterpret_cast<const float4*>(u);
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    const long long n4 = ns >> 2;
+    for (long long i = t; i < n4; i += stride)
+      diff4(__ldcs(u4 + i), __ldcs(v4 + i), 4 * i, nq, ds, dq);
+    tail = n4 << 2;
+  }
+  for (long long k = tail + t; k < ns; k += stride) {
+    const bool e = u[k] != v[k];
+    ds |= e;
+    dq |= e && k < nq;
+  }
+  const int any_s = __syncthreads_or(ds), any_q = __syncthreads_or(dq);
+  if (threadIdx.x == 0) {
+    if (any_s) atomicOr(flags + 2 * p, 1);
+    if (any_q) atomicOr(flags + 2 * p + 1, 1);
+  }
+}
+
+int sms_of_current_device() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (!n) {
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 }  // namespace
 }  // namespace gsa
 
@@ -374,11 +423,29 @@ GSA_API int reuse_prefix_batch(int count, const float* a, long long a_stride,
   const long long bytes = 8 * ns + 8ll * rows * cols;
   const int cs = (int)std::max<long long>(
       1, std::min<long long>(kStageClusterMax, (bytes + (64 << 10) - 1) >> 16));
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cs == kStageClusterMax && (long long)count * cs < sms_of_current_device()) {
+    // a few large scenes: grid-wide check, then the batched row copy
+    cudaError_t e = cudaMemsetAsync(flags, 0, sizeof(int) * 2 * count, s);
+    if (e) return e;
+    count_launches(2);
+    prefix_mismatch_kernel<<<dim3(copy_blocks((ns + 3) / 4), count),
+                             kStageThreads, 0, s>>>(a, a_stride, b, b_stride,
+                                                    ns, nq, flags);
+    if (rows)
+      reuse_rows_batch_kernel<<<dim3(copy_blocks(((long long)rows * cols + 3) / 4), count),
+                                256, 0, s>>>(src, src_stride, src_ld, flags, rows,
+                                             cols, dst, dst_stride, hits);
+    else if (hits)
+      reuse_rows_batch_kernel<<<dim3(1, count), 256, 0, s>>>(
+          src, src_stride, src_ld, flags, 0, cols, dst, dst_stride, hits);
+    return cudaGetLastError();
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, count);
   cfg.blockDim = dim3(kStageThreads);
   cfg.dynamicSmemBytes = 0;
-  cfg.stream = (cudaStream_t)stream;
+  cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cs;

@@ -157,15 +157,19 @@ def test_batched_reuse_admission_rejects_changed_scene():
             assert (got == -1).all()
 
 
-@pytest.mark.parametrize("N,n_q,shift", [(1000, 250, 0), (24000, 6000, 0), (1001, 333, 1), (94, 23, 0), (7, 7, 1)])
-def test_fused_stage_reuse_equals_two_step_path(N, n_q, shift):
-    """reuse_prefix_batch (one cluster launch) against coords_mismatch_strided
-    twice + reuse_rows_batch: same flags, hits and rows; rows of a miss stay
-    untouched.  shift=1 offsets every buffer by one element (scalar path)."""
+@pytest.mark.parametrize("N,n_q,shift,B", [(1000, 250, 0, 6), (24000, 6000, 0, 6), (24000, 6000, 0, 24),
+                                           (1001, 333, 1, 6), (94, 23, 0, 6), (7, 7, 1, 6)])
+def test_fused_stage_reuse_equals_two_step_path(N, n_q, shift, B):
+    """reuse_prefix_batch against coords_mismatch_strided twice +
+    reuse_rows_batch: same flags, hits and rows; rows of a miss stay
+    untouched.  Six 24,000-point scenes take its grid-wide form (their
+    clusters would not cover the SMs), 24 take one 8-CTA cluster per scene,
+    small scenes smaller clusters.  shift=1 offsets every buffer by one
+    element (scalar path)."""
     from tests import abi
 
     lib = abi.bvh_lib()
-    B, K = 6, 32
+    K = 32
     g = torch.Generator(device="cpu").manual_seed(N + n_q)
     X = torch.randn(B * N * 3 + shift, generator=g).cuda()[shift:].view(B, N, 3)
     snap = torch.empty(B * N * 3 + shift, device="cuda")[shift:].view(B, N, 3)
@@ -197,7 +201,7 @@ def test_fused_stage_reuse_equals_two_step_path(N, n_q, shift):
         assert flags.tolist() == want_flags.tolist()
         assert hits.tolist() == want_hits.tolist()
         assert torch.equal(got, want)
-    expect_hits = [1, 0 if N > n_q else 1, 0, 0, 1, 0]
+    expect_hits = [1, 0 if N > n_q else 1, 0, 0, 1, 0] + [1] * (B - 6)
     assert hits.tolist() == expect_hits
     assert lib.reuse_prefix_batch(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, N * 3,
                                   rows.data_ptr(), N * K, K, n_q, K, got.data_ptr(), n_q * K,
