@@ -464,7 +464,7 @@ TRAFFIC_COMMAND = (
 )
 
 
-def write_traffic_profile(csv_path):
+def write_traffic_profile(csv_path, out_path=None):
     """Per-query DRAM bytes of the frontier kernels from an ncu --csv capture
     of TRAFFIC_COMMAND (the first hierarchy run: each kernel's launches are
     stages 0, 1, 2 in order, over 64 scenes of SIZES[0..2] queries), written
@@ -505,8 +505,9 @@ def write_traffic_profile(csv_path):
                 for i, (q, d, st) in enumerate(zip(queries, dram, stages))
             ],
         }
-    TRAFFIC_PROFILE.write_text(json.dumps(out, indent=1) + "\n")
+    Path(out_path or TRAFFIC_PROFILE).write_text(json.dumps(out, indent=1) + "\n")
     print(json.dumps(out, indent=1))
+    return out
 
 
 def kernel_sources_sha(names):

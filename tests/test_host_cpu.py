@@ -63,3 +63,34 @@ def test_session_outputs_reuse_a_given_buffer():
     same, out = hz.session_outputs(hz.ROOM_SIZES, "cpu", flat)
     assert same.data_ptr() == flat.data_ptr()
     assert out["ball0"].data_ptr() == flat.data_ptr()
+
+
+def test_traffic_profile_parses_ncu_csv_and_pins_the_sources(tmp_path):
+    """``bench.py --write-traffic-profile``: per kernel, launches in ID order
+    are stages 0..2, DRAM bytes per query are read + write over the stage's
+    queries, and the profile records the SHA-256 of the sources it was taken
+    of, which ``measured_traffic`` then requires."""
+    import bench
+
+    head = ('"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream",'
+            '"Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"\n')
+    rows = []
+    for i, (kern, stage) in enumerate([("radius_frontier_kernel", 0), ("knn3_frontier_kernel", 0),
+                                       ("radius_frontier_kernel", 1), ("knn3_frontier_kernel", 1),
+                                       ("radius_frontier_kernel", 2), ("knn3_frontier_kernel", 2)]):
+        name = f"void <unnamed>::{kern}<128>(<unnamed>::QArgs)"
+        q = bench.SCENES * bench.SIZES[stage]
+        for metric, unit, val in [("dram__bytes_read.sum", "byte", 100 * q), ("dram__bytes_write.sum", "byte", 40 * q),
+                                  ("gpu__time_duration.sum", "nsecond", 1000 + i), ("smsp__inst_executed.sum", "inst", 250 * q)]:
+            rows.append(f'"{i}","1","python","h","{name}","1","7","(64, 1, 1)","(375, 64, 1)","0","10.0",'
+                        f'"Command line profiler metrics","{metric}","{unit}","{val:,}"\n')
+    csv_path = tmp_path / "dram.csv"
+    csv_path.write_text("==PROF== Connected\n" + head + "".join(rows))
+    out = tmp_path / "profile.json"
+    prof = bench.write_traffic_profile(str(csv_path), out)
+    assert sorted(prof["kernels"]) == ["knn3_frontier_kernel", "radius_frontier_kernel"]
+    for entry in prof["kernels"].values():
+        assert abs(entry["dram_bytes_per_query"] - 140.0) < 1e-9
+        assert [s["stage"] for s in entry["per_stage"]] == [0, 1, 2]
+        assert all(abs(s["warp_inst_per_32_queries"] - 8000.0) < 1e-9 for s in entry["per_stage"])
+    assert prof["sources_sha256"] == bench.kernel_sources_sha(bench.TRAFFIC_SOURCES)
