@@ -718,6 +718,14 @@ def run_ours(args, rank, world, local):
         "step_calibration_ms": getattr(step, "calibration_ms", None),
         "roofline": roofline,
         "phases_ms_per_step": {k: v / args.steps for k, v in phase.items()},
+        # per row type, from the serialized pass: computed radius rows over the
+        # radius stages, reuse-hit rows over the reuse checks and copies, 3NN
+        # rows over the 3NN stages
+        "rates_per_s": {
+            "radius_computed": S * ball_rows * args.steps / (phase["ball"] / 1000.0),
+            "reuse_hit": S * hit_rows * args.steps / (phase["reuse"] / 1000.0),
+            "nn3": S * nn_rows * args.steps / (phase["nn"] / 1000.0),
+        },
         "stages_ms_per_step": {k: round(v / args.steps, 4) for k, v in stage.items()},
         "serialized_ms_per_step": serial_ms,
         "stage_note": (
