@@ -1180,12 +1180,20 @@ int sm_count() {
 // Queries per warp of a frontier launch.  A packet of 32 queries shares one
 // walk of the tree, which is the cheapest per query; a launch whose grid
 // would hold fewer than 16 warps per SM (a single scene) takes narrower
-// packets (16, then 8 queries) so that more warps walk at once: each walk is
-// shorter and the launch's latency falls, at some cost in instructions per
-// query (one scene of 24,000 points: radius stage 0 108 -> 90 us, 3NN stage
-// 0 57 -> 51 us; 8 or more such scenes keep 32).
-constexpr int kPacketMin = 8;
-constexpr int kPacketFillWarps = 16;  // warps per SM below which packets narrow
+// packets (16, 8, 4, then 2 queries) so that more warps walk at once: each
+// walk is shorter and the launch's latency falls, at some cost in
+// instructions per query (one scene of 24,000 points: radius stage 0 108 ->
+// 90 us, 3NN stage 0 57 -> 51 us; radius stage 1 at 6,000 queries 32.6 ->
+// 24.6 us and stage 2 22.5 -> 18.5 us with packets down to 2; 8 or more such
+// scenes keep 32).
+#ifndef GSA_PACKET_MIN
+#define GSA_PACKET_MIN 2
+#endif
+constexpr int kPacketMin = GSA_PACKET_MIN;
+#ifndef GSA_PACKET_FILL_WARPS
+#define GSA_PACKET_FILL_WARPS 16
+#endif
+constexpr int kPacketFillWarps = GSA_PACKET_FILL_WARPS;  // warps per SM below which packets narrow
 // Packets (warps) of a tree launch at `pw` queries per warp.
 long long launch_warps(const Forest& f, long long slots, int pw) {
   return (slots + kFWarps * pw - 1) / (kFWarps * pw) * kFWarps * f.B;
