@@ -41,6 +41,12 @@ namespace cg = cooperative_groups;
 #define GSA_CLUSTER_SORT 1
 #endif
 
+// 1: launches with few trees sort with 2,048-position tiles (clusters of up
+// to 16 CTAs); 0: always 4,096.
+#ifndef GSA_SMALL_SORT_TILES
+#define GSA_SMALL_SORT_TILES 1
+#endif
+
 namespace gsa {
 namespace {
 
@@ -331,13 +337,15 @@ __global__ void __launch_bounds__(kSortThreads)
 // n <= 32768 is 10), so they live in shared memory as 32-bit words; the output
 // (64-bit keys, local indices, member offsets) equals the multi-launch path's.
 constexpr int kCThreads = 512;
-constexpr int kCItems = 8;
-constexpr int kCTile = kCThreads * kCItems;  // 4096 positions per CTA
-constexpr int kClusterMax = 8;               // portable cluster size
-constexpr int kClusterMaxPoints = kClusterMax * kCTile;
+constexpr int kClusterMaxPoints = 32768;     // 8 tiles of 4096 or 16 of 2048
 constexpr int kCWarps = kCThreads / 32;
 
+// ITEMS positions per thread: tiles of 512 * ITEMS positions, at most
+// kClusterMaxPoints / tile CTAs per cluster (8, the portable size, at
+// ITEMS = 8; 16 at ITEMS = 4, for launches with few trees).
+template <int ITEMS>
 struct ClusterSmem {
+  static constexpr int kCTile = kCThreads * ITEMS;
   unsigned keys[kCTile];   // the tile's keys in position order (scatter target)
   int vals[kCTile];
   int wcnt[kCWarps][256];  // per-warp digit counts, then their exclusive scan
@@ -351,16 +359,22 @@ struct ClusterSmem {
 };
 
 // Position of item j of a lane inside its CTA's tile (warp-major).
+template <int ITEMS>
 __device__ __forceinline__ int cpos(int warp, int j, int lane) {
-  return warp * (kCItems * 32) + j * 32 + lane;
+  return warp * (ITEMS * 32) + j * 32 + lane;
 }
 
+template <int ITEMS>
 __global__ void __launch_bounds__(kCThreads)
     cluster_sort_kernel(const TreeDesc* desc, const float* x, int bits,
                         int levels, uint64_t* keys_out, int* vals_out,
                         int* pref, int N) {
+  constexpr int kCItems = ITEMS;
+  constexpr int kCTile = kCThreads * ITEMS;
+  constexpr int kClusterMax = kClusterMaxPoints / kCTile;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  ClusterSmem& S = *reinterpret_cast<ClusterSmem*>(smem_raw);
+  using Smem = ClusterSmem<ITEMS>;
+  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int cs = (int)cluster.num_blocks();
@@ -375,7 +389,7 @@ __global__ void __launch_bounds__(kCThreads)
   unsigned lo[3] = {~0u, ~0u, ~0u}, hi[3] = {0u, 0u, 0u};
 #pragma unroll
   for (int j = 0; j < kCItems; ++j) {
-    const int i = base + cpos(warp, j, lane);
+    const int i = base + cpos<ITEMS>(warp, j, lane);
     px[j] = py[j] = pz[j] = NAN;
     if (i < n) {
       const float* q = x + 3ll * (d.p0 + i);
@@ -440,12 +454,12 @@ __global__ void __launch_bounds__(kCThreads)
       key[j] = (unsigned)((spread3(quantize(px[j], l3[0], scale, top)) << 2) |
                           (spread3(quantize(py[j], l3[1], scale, top)) << 1) |
                           spread3(quantize(pz[j], l3[2], scale, top)));
-      val[j] = base + cpos(warp, j, lane);
+      val[j] = base + cpos<ITEMS>(warp, j, lane);
     }
   }
 
   // 3. stable LSD radix passes over 8-bit digits.  Item j of a lane sits at
-  // tile position cpos(warp, j, lane) at the start of every pass.
+  // tile position cpos<ITEMS>(warp, j, lane) at the start of every pass.
   const int passes = (3 * bits + 7) / 8;
   for (int pass = 0; pass < passes; ++pass) {
     const int shift = 8 * pass;
@@ -455,7 +469,7 @@ __global__ void __launch_bounds__(kCThreads)
     int rk[kCItems];
 #pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      const bool valid = base + cpos(warp, j, lane) < n;
+      const bool valid = base + cpos<ITEMS>(warp, j, lane) < n;
       const int digit = valid ? (int)((key[j] >> shift) & 255) : 256 + lane;
       // lanes with this lane's digit: eight ballots over the digit bits
       unsigned peers = __ballot_sync(kFull, valid);
@@ -510,14 +524,14 @@ __global__ void __launch_bounds__(kCThreads)
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      const bool valid = base + cpos(warp, j, lane) < n;
+      const bool valid = base + cpos<ITEMS>(warp, j, lane) < n;
       if (!valid) continue;
       const int digit = (int)((key[j] >> shift) & 255);
       const int r = S.goff[digit] + wc[digit] + rk[j];
       // r < n by construction; the check keeps a corrupted count from
       // addressing a CTA outside the cluster
       if (r >= 0 && r < n) {
-        ClusterSmem* dst = cluster.map_shared_rank(&S, r / kCTile);
+        Smem* dst = cluster.map_shared_rank(&S, r / kCTile);
         dst->keys[r % kCTile] = key[j];
         dst->vals[r % kCTile] = val[j];
       }
@@ -525,8 +539,8 @@ __global__ void __launch_bounds__(kCThreads)
     cluster.sync();  // every scatter landed
 #pragma unroll
     for (int j = 0; j < kCItems; ++j) {
-      key[j] = S.keys[cpos(warp, j, lane)];
-      val[j] = S.vals[cpos(warp, j, lane)];
+      key[j] = S.keys[cpos<ITEMS>(warp, j, lane)];
+      val[j] = S.vals[cpos<ITEMS>(warp, j, lane)];
     }
   }
 
@@ -534,7 +548,7 @@ __global__ void __launch_bounds__(kCThreads)
   // position (member_count + member_prefix of the multi-launch path)
 #pragma unroll
   for (int j = 0; j < kCItems; ++j) {
-    const int i = base + cpos(warp, j, lane);
+    const int i = base + cpos<ITEMS>(warp, j, lane);
     if (i < n) {
       keys_out[d.p0 + i] = key[j];
       vals_out[d.p0 + i] = val[j];
@@ -545,7 +559,7 @@ __global__ void __launch_bounds__(kCThreads)
       int run = 0;
 #pragma unroll
       for (int j = 0; j < kCItems; ++j) {
-        const bool m = l < levels && base + cpos(warp, j, lane) < n &&
+        const bool m = l < levels && base + cpos<ITEMS>(warp, j, lane) < n &&
                        val[j] < level_size(n, l);
         run += __popc(__ballot_sync(kFull, m));
       }
@@ -570,7 +584,7 @@ __global__ void __launch_bounds__(kCThreads)
         run += c < rank ? cluster.map_shared_rank(S.lcnt, c)[l] : 0;
 #pragma unroll
       for (int j = 0; j < kCItems; ++j) {
-        const int i = base + cpos(warp, j, lane);
+        const int i = base + cpos<ITEMS>(warp, j, lane);
         const bool m = i < n && val[j] < level_size(n, l);
         const unsigned bal = __ballot_sync(kFull, m);
         if (i < n) pref[(size_t)(l - 1) * N + d.p0 + i] = run + __popc(bal & lt);
@@ -1163,25 +1177,30 @@ cudaError_t free_scratch(BuildScratch* sc, cudaStream_t s) {
   return e;
 }
 
-cudaError_t launch_cluster_sort(const Forest* f, const float* x,
-                                const BuildScratch& sc, cudaStream_t s) {
+template <int ITEMS>
+cudaError_t launch_cluster_sort_items(const Forest* f, const float* x,
+                                      const BuildScratch& sc, cudaStream_t s) {
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e) return e;
   const unsigned long long bit = 1ull << (device & 63);
   if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
-    e = cudaFuncSetAttribute(cluster_sort_kernel,
+    e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(ClusterSmem));
+                             (int)sizeof(ClusterSmem<ITEMS>));
+    // clusters above the portable size of 8
+    if (!e)
+      e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS>,
+                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e) return e;
     attr_set.fetch_or(bit, std::memory_order_relaxed);
   }
-  const int cs = blocks_for(f->max_n, kCTile);
+  const int cs = blocks_for(f->max_n, kCThreads * ITEMS);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, f->B);
   cfg.blockDim = dim3(kCThreads);
-  cfg.dynamicSmemBytes = sizeof(ClusterSmem);
+  cfg.dynamicSmemBytes = sizeof(ClusterSmem<ITEMS>);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1190,9 +1209,26 @@ cudaError_t launch_cluster_sort(const Forest* f, const float* x,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, cluster_sort_kernel, f->desc, x,
+  return cudaLaunchKernelEx(&cfg, cluster_sort_kernel<ITEMS>, f->desc, x,
                             morton_bits(f->max_n), f->levels, sc.keys,
                             sc.vals, sc.pref, f->N);
+}
+
+// Very few trees (their 4,096-position tiles would fill at most an eighth of
+// the SMs, e.g. the session's one tree per build): tiles of 2,048 in
+// clusters of up to 16, so each CTA ranks half as many items per pass (one
+// 24,000-point tree: build 125 -> 111 us); otherwise tiles of 4,096 in
+// portable clusters of up to 8 (8 trees: 144 us, against 158 us with the
+// 16-CTA clusters, which the GPCs place less freely).
+cudaError_t launch_cluster_sort(const Forest* f, const float* x,
+                                const BuildScratch& sc, cudaStream_t s) {
+  int device = 0, sms = 148;
+  if (cudaGetDevice(&device) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const long long ctas = (long long)f->B * blocks_for(f->max_n, kCThreads * 8);
+  if (GSA_SMALL_SORT_TILES && 8 * ctas <= sms)
+    return launch_cluster_sort_items<4>(f, x, sc, s);
+  return launch_cluster_sort_items<8>(f, x, sc, s);
 }
 
 // Enqueues every build kernel of `f` over points `x` (the layout in f->hdesc)
