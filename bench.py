@@ -272,7 +272,10 @@ def run_reference(args, rank, world):
         return
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     workers = max(1, min(cores, args.scenes))
-    fraction = 0.25
+    # each step answers the first 10 % of every hierarchy call's queries on
+    # each worker's scene (~2.5 s of CPU work per step), so a 20-step run
+    # ends in about a minute while the GPUs of the job are held
+    fraction = 0.10
     ctx = mp.get_context("spawn")
     with ctx.Pool(workers, initializer=_ref_worker_init) as pool:
         seeds = list(range(workers))
