@@ -121,18 +121,12 @@ def _ref_scene(seed):
 
 
 def _ref_step(args):
-    seed, fraction = args
+    P, fraction = args
     from oracle import numpy_oracle as orc
 
-    P = _ref_scene_cache.get(seed)
-    if P is None:
-        P = _ref_scene_cache[seed] = _ref_scene(seed)
     t0 = time.perf_counter()
     _, rows = orc.hierarchy_oracle(P, SIZES, RADII, K, fraction)
     return rows, time.perf_counter() - t0
-
-
-_ref_scene_cache = {}
 
 
 def ref_session_calls(gsa, s, P, out):
@@ -278,14 +272,16 @@ def run_reference(args, rank, world):
     fraction = 0.10
     ctx = mp.get_context("spawn")
     with ctx.Pool(workers, initializer=_ref_worker_init) as pool:
-        seeds = list(range(workers))
-        pool.map(_ref_step, [(s, 0.001) for s in seeds])  # build each worker's scene (untimed)
+        # the scenes (CPU FPS order) once, untimed; every step then sends each
+        # worker a scene's points, so no timed step generates a scene
+        scenes_P = pool.map(_ref_scene, list(range(workers)), chunksize=1)
+        tasks = [(P, fraction) for P in scenes_P]
         for _ in range(args.warmup):
-            pool.map(_ref_step, [(s, fraction) for s in seeds])
+            pool.map(_ref_step, tasks, chunksize=1)
         total_rows, total_t = 0, 0.0
         for _ in range(args.steps):
             t0 = time.perf_counter()
-            res = pool.map(_ref_step, [(s, fraction) for s in seeds])
+            res = pool.map(_ref_step, tasks, chunksize=1)
             total_t += time.perf_counter() - t0
             total_rows += sum(r for r, _ in res)
     value = total_rows / total_t
