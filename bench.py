@@ -459,7 +459,7 @@ TRAFFIC_SOURCES = ["query.cu", "common.cuh", "forest.cuh", "build.cu"]
 TRAFFIC_COMMAND = (
     "ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum,smsp__inst_executed.sum "
     "--clock-control none -k regex:frontier_kernel -c 6 --csv --log-file dram.csv "
-    "python bench.py --steps 1 --warmup 3 --no-e2e --no-cpu-baseline"
+    "python bench.py --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-configs"
 )
 
 
