@@ -816,31 +816,44 @@ __device__ bool frontier_walk(WarpBufs<CAP, FRONT>& W, const Entry* nodes,
   return false;
 }
 
-// Sorts h[0..count) ascending (count <= W) with a bitonic network over W
-// registers, the slots past count padded with INT_MAX.
-template <int W>
+// Sorts h[0..count) ascending (count <= N <= W, W a power of two) with a
+// bitonic network over registers in its all-ascending form (each merge
+// starts with a flip step i <-> i ^ (k-1), then half-cleaners; every
+// comparator puts the minimum at the lower index).  Slots from count on hold
+// INT_MAX, so slots N..W-1 would stay INT_MAX throughout and every
+// comparator touching them is dropped at compile time: W = 32 costs 240
+// comparators at N = 32, 168 at 24, 134 at 20; W = 16, N = 16 costs 80.
+template <int W, int N>
 __device__ __forceinline__ void sort_hits(int* h, int count) {
   int v[W];
 #pragma unroll
-  for (int i = 0; i < W; ++i) v[i] = i < count ? h[i] : INT_MAX;
+  for (int i = 0; i < W; ++i) v[i] = i < N && i < count ? h[i] : INT_MAX;
 #pragma unroll
   for (int k = 2; k <= W; k <<= 1) {
 #pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
+    for (int i = 0; i < W; ++i) {
+      const int l = i ^ (k - 1);
+      if (l > i && l < N) {
+        const int lo = min(v[i], v[l]), hi = max(v[i], v[l]);
+        v[i] = lo;
+        v[l] = hi;
+      }
+    }
+#pragma unroll
+    for (int j = k >> 2; j > 0; j >>= 1) {
 #pragma unroll
       for (int i = 0; i < W; ++i) {
         const int l = i ^ j;
-        if (l > i) {
+        if (l > i && l < N) {
           const int lo = min(v[i], v[l]), hi = max(v[i], v[l]);
-          const bool up = (i & k) == 0;
-          v[i] = up ? lo : hi;
-          v[l] = up ? hi : lo;
+          v[i] = lo;
+          v[l] = hi;
         }
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < W; ++i)
+  for (int i = 0; i < N; ++i)
     if (i < count) h[i] = v[i];
 }
 
@@ -894,12 +907,18 @@ __global__ void __launch_bounds__(kFWarps * 32)
   if (!overflow) {
     bool spill = active && hc > kPacketCap;
     // ascending IDs: a sorting network in registers (no data-dependent
-    // branches), 16 wide when no lane of the warp holds more hits
+    // branches), sized by the warp's largest hit count
     const bool sorted_here = active && !spill;
-    if (__any_sync(kFull, sorted_here && hc > 16)) {
-      if (sorted_here) sort_hits<32>(H, hc);
-    } else if (sorted_here) {
-      sort_hits<16>(H, hc);
+    const int most = (int)__reduce_max_sync(kFull, sorted_here ? hc : 0);
+    if (sorted_here) {
+      if (most > 24)
+        sort_hits<32, 32>(H, hc);
+      else if (most > 20)
+        sort_hits<32, 24>(H, hc);
+      else if (most > 16)
+        sort_hits<32, 20>(H, hc);
+      else
+        sort_hits<16, 16>(H, hc);
     }
     if (sorted_here) count = min(hc, c.K);
     if (__any_sync(kFull, spill)) {

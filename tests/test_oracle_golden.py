@@ -86,3 +86,15 @@ def test_oracle_edge_rules():
     assert i.tolist() == [[0, 1, 3]] and d.tolist() == [[1.0, 1.0, 1.0]]
     d, i = orc.nn_oracle(q, x[2:3])
     assert i.tolist() == [[0, 0, 0]] and np.isinf(d).all()
+
+
+def test_index_candidate_misses_host_logic():
+    """Index lookups whose first candidate's root differs: the answer comes
+    from the matching or newly built index, the statistics count as GSA's."""
+    from tests.index_miss import INDEX_MISS_STATS, index_candidate_misses
+
+    got, want, stats = index_candidate_misses(make_oracle_session, "cpu")
+    for g, w in zip(got, want):
+        assert np.array_equal(g, w)
+    for key, value in INDEX_MISS_STATS.items():
+        assert stats[key] == value, (key, stats)

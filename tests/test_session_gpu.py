@@ -152,3 +152,17 @@ def test_session_rejects_wrong_stream_and_closed_use():
     s.close()
     with pytest.raises(ValueError):
         s.ball_into(x[:4], x, 0.5, 4, torch.empty(4, 4, dtype=torch.int32, device="cuda"))
+
+
+def test_index_candidate_misses():
+    """Through the real session: index lookups whose first candidate's root
+    differs by one ulp answer from the matching or newly built index, and
+    the statistics count as GSA's."""
+    from gsa_b200 import QuerySession
+    from tests.index_miss import INDEX_MISS_STATS, index_candidate_misses
+
+    got, want, stats = index_candidate_misses(lambda t: QuerySession(threshold=t), "cuda")
+    for g, w in zip(got, want):
+        assert np.array_equal(g, w)
+    for key, value in INDEX_MISS_STATS.items():
+        assert stats[key] == value, (key, stats)
