@@ -26,6 +26,7 @@ struct Forest {
   int* wrank = nullptr;
   int* cut = nullptr;
   int* ovf = nullptr;  // [0, B): capacity overflow flags; [B, 2B): kept counts
+  void* block = nullptr;  // the one pool allocation holding the arrays above
   const float* x = nullptr;  // borrowed
   BuildScratch* scratch = nullptr;  // kept build temporaries (rebuild_forest)
 

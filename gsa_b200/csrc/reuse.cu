@@ -271,6 +271,117 @@ __global__ void __launch_bounds__(kStageThreads)
   }
 }
 
+// One session admission step (the body of session_lookup) in one launch for
+// lookups of a few MB: a single thread-block cluster compares every pair
+// (each pair's difference bit ORed over the cluster through distributed
+// shared memory), picks the first memo candidate whose support and query
+// pairs both match, copies its rows, and writes the flags to the device
+// buffer and, when the host buffer is device-accessible pinned memory, to
+// the host directly.  This replaces a flag memset, the comparison kernel,
+// the row-copy kernel and the flag copy: four dependent operations, each
+// paying its own launch latency, on a call the host waits for.
+constexpr int kLookupThreads = 512;
+constexpr int kLookupClusterMax = 8;  // portable cluster size
+constexpr int kLookupPairs = 64;      // two 32-bit masks
+
+struct LookupArgs {
+  const float* a[kLookupPairs];
+  const float* b[kLookupPairs];
+  long long n[kLookupPairs];
+  const int* src[kLookupPairs / 2];
+  int count, nmemo, src_ld, rows, cols;
+  int* dst;
+  int* flags;
+  int* hflags;  // device address of the pinned host flags, or null
+};
+
+// Does any element i = t, t+stride, ... of a[0..n) differ from b (IEEE !=)?
+__device__ __forceinline__ bool span_differs(const float* a, const float* b,
+                                             long long n, long long t,
+                                             long long stride) {
+  bool diff = false;
+  long long tail = 0;
+  if (((((uintptr_t)a) | ((uintptr_t)b)) & 15) == 0) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    const long long n4 = n >> 2;
+    for (long long i = t; i < n4; i += stride) {
+      const float4 u = __ldcs(a4 + i), v = __ldcs(b4 + i);
+      diff |= (u.x != v.x) | (u.y != v.y) | (u.z != v.z) | (u.w != v.w);
+    }
+    tail = n4 << 2;
+  }
+  for (long long i = tail + t; i < n; i += stride) diff |= a[i] != b[i];
+  return diff;
+}
+
+__global__ void __launch_bounds__(kLookupThreads)
+    session_lookup_kernel(const __grid_constant__ LookupArgs L) {
+  namespace cg = cooperative_groups;
+  __shared__ unsigned bits[2];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+  if (threadIdx.x < 2) bits[threadIdx.x] = 0u;
+  __syncthreads();
+  const long long t = (long long)rank * kLookupThreads + threadIdx.x;
+  const long long stride = (long long)cs * kLookupThreads;
+  unsigned m0 = 0u, m1 = 0u;
+  for (int p = 0; p < L.count; ++p) {
+    if (span_differs(L.a[p], L.b[p], L.n[p], t, stride)) {
+      if (p < 32)
+        m0 |= 1u << p;
+      else
+        m1 |= 1u << (p - 32);
+    }
+  }
+  m0 = __reduce_or_sync(kFull, m0);
+  m1 = __reduce_or_sync(kFull, m1);
+  if ((threadIdx.x & 31) == 0) {
+    if (m0) atomicOr(&bits[0], m0);
+    if (m1) atomicOr(&bits[1], m1);
+  }
+  cluster.sync();  // every CTA's bits complete
+  unsigned all0 = 0u, all1 = 0u;
+  for (int c = 0; c < cs; ++c) {
+    const unsigned* rb = cluster.map_shared_rank(bits, c);
+    all0 |= rb[0];
+    all1 |= rb[1];
+  }
+  cluster.sync();  // no CTA leaves while another may still read its bits
+  auto differs = [&](int p) {
+    return (int)(((p < 32 ? all0 >> p : all1 >> (p - 32))) & 1u);
+  };
+  if (rank == 0) {
+    for (int p = threadIdx.x; p < L.count; p += kLookupThreads) {
+      const int f = differs(p);
+      L.flags[p] = f;
+      if (L.hflags) L.hflags[p] = f;
+    }
+    if (L.hflags) __threadfence_system();
+  }
+  int c = 0;
+  while (c < L.nmemo && (differs(2 * c) | differs(2 * c + 1))) ++c;
+  if (c >= L.nmemo || L.rows == 0) return;
+  const int* src = L.src[c];
+  int* dst = L.dst;
+  const long long total = (long long)L.rows * L.cols;
+  if (L.cols == L.src_ld && ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0 &&
+      (total & 3) == 0) {
+    const int4* s4 = reinterpret_cast<const int4*>(src);
+    int4* d4 = reinterpret_cast<int4*>(dst);
+    for (long long i = t; i < (total >> 2); i += stride) d4[i] = __ldcs(s4 + i);
+    return;
+  }
+  for (long long i = t; i < total; i += stride) {
+    const long long row = i / L.cols, col = i - row * L.cols;
+    dst[i] = src[row * L.src_ld + col];
+  }
+}
+
+// Bytes up to which one cluster serves a lookup (above, the grid-wide
+// kernels are faster despite their extra launches).
+constexpr long long kLookupFusedBytes = 8ll << 20;
+
 int sms_of_current_device() {
   static std::atomic<int> cached[64];
   int dev = 0;
@@ -392,6 +503,62 @@ GSA_API int session_lookup(int count, const float* const* a,
   if (count < 1 || nmemo < 0 || 2 * nmemo > count || nmemo > kMaxPairs ||
       !flags || !flags_host)
     return -2;
+  cudaStream_t s = (cudaStream_t)stream;
+  long long bytes = 8ll * rows * cols;
+  bool fused = count <= kLookupPairs && a && b && nfloat &&
+               rows >= 0 && cols >= 1 && src_ld >= cols &&
+               (!nmemo || (cached && (!rows || dst)));
+  for (int p = 0; fused && p < count; ++p) {
+    if (nfloat[p] < 0) return -2;
+    bytes += 8 * nfloat[p];
+  }
+  if (fused && bytes <= kLookupFusedBytes) {
+    LookupArgs L;
+    for (int p = 0; p < kLookupPairs; ++p) {
+      const bool on = p < count;
+      L.a[p] = on ? a[p] : nullptr;
+      L.b[p] = on ? b[p] : nullptr;
+      L.n[p] = on ? nfloat[p] : 0;
+    }
+    for (int c = 0; c < kLookupPairs / 2; ++c) L.src[c] = c < nmemo ? cached[c] : nullptr;
+    L.count = count;
+    L.nmemo = nmemo;
+    L.src_ld = src_ld;
+    L.rows = rows;
+    L.cols = cols;
+    L.dst = dst;
+    L.flags = flags;
+    // pinned host memory is device-accessible at its own address under
+    // unified addressing; anything else gets a copy after the kernel
+    L.hflags = nullptr;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, flags_host) == cudaSuccess) {
+      if (pa.type == cudaMemoryTypeHost && pa.devicePointer)
+        L.hflags = static_cast<int*>(pa.devicePointer);
+    } else {
+      cudaGetLastError();
+    }
+    const int cs = (int)std::max<long long>(
+        1, std::min<long long>(kLookupClusterMax, (bytes + (64 << 10) - 1) >> 16));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs);
+    cfg.blockDim = dim3(kLookupThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launches();
+    cudaError_t e = cudaLaunchKernelEx(&cfg, session_lookup_kernel, L);
+    if (!e && !L.hflags)
+      e = cudaMemcpyAsync(flags_host, flags, sizeof(int) * count,
+                          cudaMemcpyDeviceToHost, s);
+    if (!e) e = cudaStreamSynchronize(s);
+    return (int)e;
+  }
   int code = coords_mismatch(count, a, b, nfloat, flags, stream);
   if (code) return code;
   if (nmemo) {
@@ -399,7 +566,6 @@ GSA_API int session_lookup(int count, const float* const* a,
                       stream);
     if (code) return code;
   }
-  cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaMemcpyAsync(flags_host, flags, sizeof(int) * count,
                                   cudaMemcpyDeviceToHost, s);
   if (!e) e = cudaStreamSynchronize(s);

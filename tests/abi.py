@@ -27,6 +27,7 @@ def bvh_lib(name="gsa_bvh"):
     lib.coords_mismatch.argtypes = [I, P, P, P, P, P]
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]
+    lib.session_lookup.argtypes = [I, P, P, P, I, P, I, I, I, P, P, P, P]
     lib.fps_order.argtypes = [I, I, P, P, P, P]
     lib.furthest_point_sample.argtypes = [I, I, I, P, P, P, P]
     lib.bvh_info.argtypes = [P] + [ctypes.POINTER(I)] * 4

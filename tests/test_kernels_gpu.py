@@ -336,6 +336,58 @@ def test_reuse_kernels():
     assert torch.equal(out, cached[1][:, :7])
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+@pytest.mark.parametrize("case", ["small", "large", "many_pairs"])
+def test_session_lookup_paths(case, pinned):
+    """session_lookup: one cluster launch for lookups of a few MB and at
+    most 64 pairs (flags written straight into pinned host memory, or copied
+    when the host buffer is pageable), the four-operation path otherwise;
+    flags as torch.equal, rows of the first fully matching memo candidate."""
+    lib = abi.bvh_lib()
+    n = {"small": 6000, "large": 1 << 20, "many_pairs": 500}[case]
+    x = torch.randn(n, 3, device="cuda")
+    x[7, 2] = float("nan")  # NaN never equals itself: x never equals a copy
+    y = torch.randn(n, 3, device="cuda")
+    z = y.clone()
+    z[n - 1, 0] = -0.0 if z[n - 1, 0] == 0 else z[n - 1, 0]
+    w = y.clone()
+    w[n // 2, 1] = torch.nextafter(w[n // 2, 1], torch.tensor(float("inf"), device="cuda"))
+    # memo pairs: candidate 0 (NaN in x, one ulp in w) differs, candidate 1
+    # (y, z) / (y[:n//4], z) matches
+    pairs = [(x, x.clone()), (y, w), (y, z), (y[: n // 4], z)]
+    memo = 2
+    if case == "many_pairs":
+        pairs += [(y, z) if i % 3 else (y, w) for i in range(70)]
+    rows, cols = n // 4, 32
+    cached = [torch.randint(0, 1 << 20, (n, 32), dtype=torch.int32, device="cuda") for _ in range(memo)]
+    count = len(pairs)
+    A = (ctypes.c_void_p * count)(*[p[0].data_ptr() for p in pairs])
+    B = (ctypes.c_void_p * count)(*[p[1].data_ptr() for p in pairs])
+    C = (ctypes.c_longlong * count)(*[p[0].numel() for p in pairs])
+    src = (ctypes.c_void_p * memo)(*[c.data_ptr() for c in cached])
+    flags = torch.full((count,), 9, dtype=torch.int32, device="cuda")
+    want = [0 if torch.equal(u, v[: u.shape[0]]) else 1 for u, v in pairs]
+    assert want[:4] == [1, 1, 0, 0]
+    for rep in range(2):  # twice in a row: nothing of the first call leaks
+        out = torch.full((rows, cols), -1, dtype=torch.int32, device="cuda")
+        if pinned:
+            host_t = torch.full((count,), 7, dtype=torch.int32, pin_memory=True)
+            host = (ctypes.c_int * count).from_address(host_t.data_ptr())
+        else:
+            host = (ctypes.c_int * count)(*([7] * count))
+        code = lib.session_lookup(count, A, B, C, memo, src, 32, rows, cols, out.data_ptr(),
+                                  flags.data_ptr(), host, abi.stream())
+        assert code == 0
+        assert list(host) == want and flags.tolist() == want
+        assert torch.equal(out, cached[1][:rows, :cols])
+    # no matching candidate: out untouched
+    out = torch.full((rows, cols), -1, dtype=torch.int32, device="cuda")
+    host = (ctypes.c_int * count)()
+    assert lib.session_lookup(2, A, B, C, 1, src, 32, rows, cols, out.data_ptr(), flags.data_ptr(), host,
+                              abi.stream()) == 0
+    assert list(host)[:2] == [1, 1] and (out == -1).all()
+
+
 def test_fps_order_matches_sequential_rule():
     from gsa_b200 import scenes
     from oracle import fps as fps_cpu
