@@ -364,8 +364,11 @@ __device__ __forceinline__ int cpos(int warp, int j, int lane) {
   return warp * (ITEMS * 32) + j * 32 + lane;
 }
 
-template <int ITEMS>
-__global__ void __launch_bounds__(kCThreads)
+// MINB: resident CTAs per SM the register budget is cut for (2: 64
+// registers; 3: 40, with spills, so that the 384 tiles of 64 rooms run as
+// one wave of three CTAs per SM instead of two waves of two).
+template <int ITEMS, int MINB>
+__global__ void __launch_bounds__(kCThreads, MINB)
     cluster_sort_kernel(const TreeDesc* desc, const float* x, int bits,
                         int levels, uint64_t* keys_out, int* vals_out,
                         int* pref, int N) {
@@ -842,8 +845,10 @@ __device__ void climb(const RefitArgs& a, const TreeDesc& d, int b, int i,
 // level-l leaf reference.  Two groups per warp keep twice as many leaves in
 // flight; no arrivals here -- the counters were initialised with the
 // leaf-child counts.
+// Eight resident CTAs per SM (32 registers, a few spilled): the kernel is
+// issue bound at low occupancy, 64 rooms 96 -> 85 us under ncu.
 template <int G>
-__global__ void __launch_bounds__(256) leaf_kernel(RefitArgs a) {
+__global__ void __launch_bounds__(256, 8) leaf_kernel(RefitArgs a) {
   int lane = threadIdx.x & 31;
   int gl = lane & (G - 1);
   unsigned gmask = G == 32 ? kFull : (0xffffu << (lane & 16));
@@ -1196,7 +1201,7 @@ cudaError_t free_scratch(BuildScratch* sc, cudaStream_t s) {
   return e;
 }
 
-template <int ITEMS>
+template <int ITEMS, int MINB>
 cudaError_t launch_cluster_sort_items(const Forest* f, const float* x,
                                       const BuildScratch& sc, cudaStream_t s) {
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
@@ -1205,12 +1210,12 @@ cudaError_t launch_cluster_sort_items(const Forest* f, const float* x,
   if (e) return e;
   const unsigned long long bit = 1ull << (device & 63);
   if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
-    e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS>,
+    e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS, MINB>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)sizeof(ClusterSmem<ITEMS>));
     // clusters above the portable size of 8
     if (!e)
-      e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS>,
+      e = cudaFuncSetAttribute(cluster_sort_kernel<ITEMS, MINB>,
                                cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e) return e;
     attr_set.fetch_or(bit, std::memory_order_relaxed);
@@ -1228,7 +1233,7 @@ cudaError_t launch_cluster_sort_items(const Forest* f, const float* x,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, cluster_sort_kernel<ITEMS>, f->desc, x,
+  return cudaLaunchKernelEx(&cfg, cluster_sort_kernel<ITEMS, MINB>, f->desc, x,
                             morton_bits(f->max_n), f->levels, sc.keys,
                             sc.vals, sc.pref, f->N);
 }
@@ -1238,7 +1243,10 @@ cudaError_t launch_cluster_sort_items(const Forest* f, const float* x,
 // clusters of up to 16, so each CTA ranks half as many items per pass (one
 // 24,000-point tree: build 125 -> 111 us); otherwise tiles of 4,096 in
 // portable clusters of up to 8 (8 trees: 144 us, against 158 us with the
-// 16-CTA clusters, which the GPCs place less freely).
+// 16-CTA clusters, which the GPCs place less freely), with the register
+// budget of three CTAs per SM once two per SM would take a second wave (64
+// rooms: 152 -> 130 us under ncu; fewer tiles keep 64 registers, since the
+// spills only add latency when the tiles fit anyway).
 cudaError_t launch_cluster_sort(const Forest* f, const float* x,
                                 const BuildScratch& sc, cudaStream_t s) {
   int device = 0, sms = 148;
@@ -1246,8 +1254,9 @@ cudaError_t launch_cluster_sort(const Forest* f, const float* x,
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   const long long ctas = (long long)f->B * blocks_for(f->max_n, kCThreads * 8);
   if (GSA_SMALL_SORT_TILES && 8 * ctas <= sms)
-    return launch_cluster_sort_items<4>(f, x, sc, s);
-  return launch_cluster_sort_items<8>(f, x, sc, s);
+    return launch_cluster_sort_items<4, 1>(f, x, sc, s);
+  if (ctas > 2ll * sms) return launch_cluster_sort_items<8, 3>(f, x, sc, s);
+  return launch_cluster_sort_items<8, 2>(f, x, sc, s);
 }
 
 // Enqueues every build kernel of `f` over points `x` (the layout in f->hdesc)
