@@ -210,7 +210,10 @@ int reuse_lookup_static(int count, const float* x, long long nx,
  * when nmemo > 0, copies the rows of the first memo candidate c whose pairs
  * 2c and 2c+1 both match, as reuse_rows does (nmemo <= 64, pairs 0..2*nmemo-1
  * are the memo pairs), then copies the flags to flags_host (count host
- * ints) and waits for the stream.  Returns 0, a cudaError_t, or -2. */
+ * ints) and waits for the stream.  Up to 64 pairs and 8 MB of compared and
+ * copied data run as one thread-block cluster launch, which writes the flags
+ * straight into flags_host when that is pinned host memory.  Returns 0, a
+ * cudaError_t, or -2. */
 int session_lookup(int count, const float* const* a, const float* const* b,
                    const long long* nfloat, int nmemo,
                    const int* const* cached, int src_ld, int rows, int cols,
