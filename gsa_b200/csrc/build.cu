@@ -1364,6 +1364,78 @@ cudaError_t enqueue_build(Forest* f, const float* x, const BuildScratch& sc,
 
 }  // namespace
 
+cudaError_t sort_query_rows(const float* q, int n, const int** perm,
+                            void** block, cudaStream_t s) {
+  *perm = nullptr;
+  *block = nullptr;
+  if (!q || n < 1 || n > kMaxPoints) return cudaErrorInvalidValue;
+  // the queries laid out as one tree whose build stops after the key sort
+  Forest f;
+  f.B = 1;
+  f.levels = 1;
+  f.N = n;
+  f.max_n = n;
+  f.hdesc.resize(1);
+  f.hdesc[0].p0 = 0;
+  f.hdesc[0].n = n;
+  f.hdesc[0].node0 = 0;
+  f.hdesc[0].q0 = 0;
+  f.hdesc[0].cap = 0;
+  BuildScratch sc;
+  const bool cluster = cluster_path(&f);
+  Carve c;
+  c.add(&f.desc, 1);
+  c.add(&sc.keys, n);
+  c.add(&sc.vals, n);
+  c.add(&sc.bounds, 6);
+  if (!cluster) {
+    c.add(&sc.keys2, n);
+    c.add(&sc.vals2, n);
+    c.add(&sc.hist, 256ll * max_tiles_of(&f));
+  }
+  cudaError_t e = c.alloc(block, s);
+  if (e) return e;
+  DescChunk dc;
+  dc.first = 0;
+  dc.count = 1;
+  dc.d[0] = f.hdesc[0];
+  upload_desc<<<1, 256, 0, s>>>(f.desc, dc, sc.bounds);
+  int launches = 1;
+  const int* order = sc.vals;
+  if (cluster) {
+    e = launch_cluster_sort(&f, q, sc, s);  // one level: no member offsets
+    launches += 1;
+  } else {
+    uint64_t *keys = sc.keys, *keys2 = sc.keys2;
+    int *vals = sc.vals, *vals2 = sc.vals2;
+    const int max_tiles = max_tiles_of(&f);
+    dim3 gs(max_tiles, 1);
+    bounds_kernel<<<dim3(std::min(blocks_for(n, 1024), 64), 1), 256, 0, s>>>(
+        f.desc, q, sc.bounds);
+    const int bits = morton_bits(n);
+    const int passes = (3 * bits + 7) / 8;
+    morton_kernel<<<dim3(std::min(blocks_for(n, 256 * kUnroll), 1024), 1), 256,
+                    0, s>>>(f.desc, q, sc.bounds, bits, keys, vals);
+    for (int pass = 0; pass < passes; ++pass) {
+      sort_upsweep<<<gs, kSortThreads, 0, s>>>(f.desc, keys, 8 * pass,
+                                               sc.hist, max_tiles);
+      seg_scan<<<1, kScanThreads, 0, s>>>(f.desc, sc.hist, 256, max_tiles,
+                                          kSortTile);
+      sort_scatter<<<gs, kSortThreads, 0, s>>>(f.desc, keys, vals, keys2,
+                                               vals2, sc.hist, 8 * pass,
+                                               max_tiles);
+      std::swap(keys, keys2);
+      std::swap(vals, vals2);
+    }
+    order = vals;
+    launches += 2 + 3 * passes;
+  }
+  count_launches(launches);
+  if (!e) e = cudaGetLastError();
+  if (!e) *perm = order;
+  return e;
+}
+
 cudaError_t build_forest(const float* x, const int* seg, int B, int prefix,
                          int leaf, cudaStream_t s, Forest** out) {
   *out = nullptr;

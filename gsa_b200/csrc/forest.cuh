@@ -71,7 +71,17 @@ struct QuerySet {
   int nq = 0;
   int m = 0;      // support prefix of every tree; 0 = that tree's level size
   int level = -1; // bounds level; -1 = all points
+  bool morton = false;  // single tree: walk the queries in their own Morton
+                        // order (they are not the support's points)
 };
+
+// Morton order of n query points q[0..n) (over their own finite bounds, as
+// a tree's points are ordered before its build): enqueues the key sort and
+// sets *perm to a device array of the n row indices in that order, which
+// lives in *block (a pool allocation the caller frees, stream-ordered, once
+// the queries that read it are enqueued).  build.cu.
+cudaError_t sort_query_rows(const float* q, int n, const int** perm,
+                            void** block, cudaStream_t s);
 
 // Query launchers (query.cu).
 cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,

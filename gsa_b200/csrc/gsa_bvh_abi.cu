@@ -69,6 +69,44 @@ GSA_API int query_ball_bvh(void* handle, const float* q, int nq, int m,
       launch_radius(*f, qs, radius, ns, out, fallback, (cudaStream_t)stream));
 }
 
+// As query_bvh / query_ball_bvh, walking the queries in their own Morton
+// order (see include/gsa_bvh.h).
+GSA_API int query_bvh_unordered(void* handle, const float* q, int nq, int m,
+                                int level, float* d, int* ix, int* fallback,
+                                void* stream) {
+  Forest* f = (Forest*)handle;
+  if (!f || nq < 0 || m < 3 || m > f->hdesc[0].n || !level_ok(f, m, level))
+    return -2;
+  if (!nq) return 0;
+  if (!q || !d || !ix || !fallback) return -2;
+  QuerySet qs;
+  qs.q = q;
+  qs.nq = nq;
+  qs.m = m;
+  qs.level = level;
+  qs.morton = true;
+  return as_code(launch_knn3(*f, qs, d, ix, fallback, (cudaStream_t)stream));
+}
+
+GSA_API int query_ball_bvh_unordered(void* handle, const float* q, int nq,
+                                     int m, int level, float radius, int ns,
+                                     int* out, int* fallback, void* stream) {
+  Forest* f = (Forest*)handle;
+  if (!f || nq < 0 || m < 1 || m > f->hdesc[0].n || ns < 1 || ns > 32 ||
+      !level_ok(f, m, level))
+    return -2;
+  if (!nq) return 0;
+  if (!q || !out || !fallback) return -2;
+  QuerySet qs;
+  qs.q = q;
+  qs.nq = nq;
+  qs.m = m;
+  qs.level = level;
+  qs.morton = true;
+  return as_code(
+      launch_radius(*f, qs, radius, ns, out, fallback, (cudaStream_t)stream));
+}
+
 GSA_API int free_bvh(void* handle, int async_free, void* stream) {
   Forest* f = (Forest*)handle;
   if (!f) return -3;

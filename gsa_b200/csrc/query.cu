@@ -30,6 +30,7 @@
 #include <atomic>
 #include <algorithm>
 #include "forest.cuh"
+#include "pool.cuh"
 
 #ifndef GSA_STACK
 #define GSA_STACK 128
@@ -77,6 +78,9 @@ struct QArgs {
   float* dout;
   int* fallback;
   int pw;             // frontier kernels: queries per warp (8, 16 or 32)
+  const int* qperm;   // single tree: query rows in a spatial (Morton) order,
+                      // walked instead of the support's leaf order; null:
+                      // the queries are taken to be the support's points
 };
 
 __device__ __forceinline__ bool nonempty(const Entry& e) {
@@ -100,6 +104,7 @@ struct Slot {
   int qbase, qin, Q, m, slots, lev;
   const int* order;  // slot -> query (null: identity)
   bool ovf;          // the tree overflowed its node capacity: exact scans
+  bool perm;         // order is a permutation of the Q query rows
 };
 
 __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
@@ -110,10 +115,16 @@ __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
   s.Q = a.qseg ? a.qseg[b + 1] - s.qbase : a.nq;
   s.m = a.m > 0 ? a.m : level_size(d.n, a.level);
   s.lev = a.level < 0 ? 0 : a.level;
+  s.ovf = a.f.ovf[b] != 0;
+  s.perm = a.qperm != nullptr;
+  if (s.perm) {  // single tree: every query row once, in the given order
+    s.slots = s.Q;
+    s.order = a.qperm;
+    return s;
+  }
   int ql = s.Q <= d.n ? query_level(d.n, a.f.levels, s.Q) : 0;
   s.slots = s.Q <= d.n ? level_size(d.n, ql) : s.Q;
   s.order = a.f.qorder + d.q0 + level_offset(d.n, ql);
-  s.ovf = a.f.ovf[b] != 0;
   if (s.ovf) s.order = nullptr;  // the build wrote no query order
   return s;
 }
@@ -121,7 +132,7 @@ __device__ __forceinline__ Slot slot_setup(const QArgs& a, const TreeDesc& d,
 __device__ __forceinline__ int slot_query(const Slot& s, const TreeDesc& d,
                                           int t) {
   if (t >= s.slots) return -1;
-  int qi = t < d.n && s.order ? __ldg(s.order + t) : t;
+  int qi = s.order && (s.perm || t < d.n) ? __ldg(s.order + t) : t;
   return qi < s.Q ? qi : -1;
 }
 
@@ -983,7 +994,9 @@ __global__ void __launch_bounds__(kFWarps * 32)
   // Non-finite queries have no finite distance: their rows stay (inf, 0).
   const bool live = active && finite3(px, py, pz);
   float B = inf;
-  if (live) {
+  // Queries in a given order are not the support's points: no window; they
+  // take the per-query walk below, in packets made coherent by that order.
+  if (live && !s.perm) {
     // window of the level's members around the query's member rank (a query
     // that is not a support point of this tree uses the first members)
     const int nl = level_size(d.n, s.lev);
@@ -1149,7 +1162,10 @@ long long tree_slots(int n, int levels, int nq) {
 }
 
 // Largest slot count over the trees, from host-side query offsets.
-long long max_slots(const Forest& f, const int* qseg_host, int nq) {
+long long max_slots(const Forest& f, const QuerySet& qs) {
+  const int* qseg_host = qs.qseg_host;
+  const int nq = qs.nq;
+  if (qs.morton) return nq;  // single tree, every query row once
   if (!qseg_host) return nq > 0 ? tree_slots(f.hdesc[0].n, f.levels, nq) : 0;
   long long best = 0;
   for (int b = 0; b < f.B; ++b) {
@@ -1174,6 +1190,7 @@ QArgs make_args(const Forest& f, const QuerySet& qs) {
   a.dout = nullptr;
   a.fallback = nullptr;
   a.pw = 32;
+  a.qperm = nullptr;
   return a;
 }
 
@@ -1239,7 +1256,7 @@ bool prefer_scan(const Forest& f, const QuerySet& qs, int scan_max,
   const int m = max_prefix(f, qs);
   if (m <= scan_max) return true;
   if (scan_max <= 0) return false;
-  long long slots = max_slots(f, qs.qseg_host, qs.nq);
+  long long slots = max_slots(f, qs);
   const int pw = narrow ? packet_width(f, slots) : 32;
   if (launch_warps(f, slots, pw) >= 4ll * sm_count()) return false;
   long long q = qs.qseg_host ? qs.qseg_host[f.B] : qs.nq;
@@ -1263,8 +1280,16 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
     radius_scan_kernel<<<grid, kScanWarps * 32, 0, s>>>(a);
     return cudaGetLastError();
   }
-  long long slots = max_slots(f, qs.qseg_host, qs.nq);
+  long long slots = max_slots(f, qs);
   if (slots <= 0) return cudaSuccess;
+  void* block = nullptr;
+  if (qs.morton) {
+    cudaError_t e = sort_query_rows(qs.q, qs.nq, &a.qperm, &block, s);
+    if (e) {
+      pool_free(block, s);
+      return e;
+    }
+  }
   count_launches();
   if (GSA_RADIUS_FRONTIER) {
     a.pw = packet_width(f, slots);
@@ -1274,7 +1299,9 @@ cudaError_t launch_radius(const Forest& f, const QuerySet& qs, float radius,
     dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
     radius_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
   }
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  cudaError_t fe = pool_free(block, s);
+  return e ? e : fe;
 }
 
 cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
@@ -1291,8 +1318,16 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
     knn3_scan_kernel<<<grid, kScanWarps * 32, 0, s>>>(a);
     return cudaGetLastError();
   }
-  long long slots = max_slots(f, qs.qseg_host, qs.nq);
+  long long slots = max_slots(f, qs);
   if (slots <= 0) return cudaSuccess;
+  void* block = nullptr;
+  if (qs.morton) {
+    cudaError_t e = sort_query_rows(qs.q, qs.nq, &a.qperm, &block, s);
+    if (e) {
+      pool_free(block, s);
+      return e;
+    }
+  }
   count_launches();
   if (GSA_KNN_FRONTIER) {
     a.pw = packet_width(f, slots);
@@ -1302,7 +1337,9 @@ cudaError_t launch_knn3(const Forest& f, const QuerySet& qs, float* d, int* ix,
     dim3 grid((unsigned)((slots + kQThreads - 1) / kQThreads), f.B);
     knn3_kernel<GSA_STACK><<<grid, kQThreads, 0, s>>>(a);
   }
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  cudaError_t fe = pool_free(block, s);
+  return e ? e : fe;
 }
 
 }  // namespace gsa

@@ -25,6 +25,8 @@ for _name, _args in {
     "build_bvh": [_ptr, _int, _int, _int, ctypes.POINTER(_ptr), _ptr],
     "query_bvh": [_ptr, _ptr, _int, _int, _int, _ptr, _ptr, _ptr, _ptr],
     "query_ball_bvh": [_ptr, _ptr, _int, _int, _int, ctypes.c_float, _int, _ptr, _ptr, _ptr],
+    "query_bvh_unordered": [_ptr, _ptr, _int, _int, _int, _ptr, _ptr, _ptr, _ptr],
+    "query_ball_bvh_unordered": [_ptr, _ptr, _int, _int, _int, ctypes.c_float, _int, _ptr, _ptr, _ptr],
     "free_bvh": [_ptr, _int, _ptr],
     "pool_memory": [_u64p, _u64p],
     "pool_reset_peak": [],
@@ -64,6 +66,15 @@ def prefix_sizes(n):
     """Supports a prefix index over ``n`` points serves: ``n, n//4, n//16,
     n//64`` (``docs/api.md`` "Index reuse")."""
     return [n >> (2 * level) for level in range(4)]
+
+
+def support_rows(q, x):
+    """Whether the query tensor starts at the support tensor's first row
+    (its rows are then the support's points, which the query kernels walk
+    in the tree's leaf order); other query sets take the ``_unordered``
+    entries, which walk them in their own Morton order.  Either way the
+    results are the same; only the speed differs."""
+    return q.data_ptr() == x.data_ptr()
 
 
 def _is_points(x):
@@ -137,8 +148,9 @@ class Tree:
         if m < 3 or not _is_rows(d, q, nq, 3, torch.float32):
             raise ValueError("3NN requires at least 3 supports and FP32 (Q,3) distances")
         if nq:
+            fn = lib.query_bvh if support_rows(q, self.x) else lib.query_bvh_unordered
             check(
-                lib.query_bvh(
+                fn(
                     self.ptr, q.data_ptr(), nq, m, self.level(m), d.data_ptr(),
                     idx.data_ptr(), self.fallback.data_ptr(), self.stream,
                 )
@@ -152,8 +164,9 @@ class Tree:
             raise ValueError("Radius query requires K in [1,32] and finite nonnegative FP32 radius")
         nq = q.shape[0]
         if nq:
+            fn = lib.query_ball_bvh if support_rows(q, self.x) else lib.query_ball_bvh_unordered
             check(
-                lib.query_ball_bvh(
+                fn(
                     self.ptr, q.data_ptr(), nq, m, self.level(m), r, ns,
                     idx.data_ptr(), self.fallback.data_ptr(), self.stream,
                 )

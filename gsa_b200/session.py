@@ -160,17 +160,23 @@ class _CudaOps:
         if code:
             raise RuntimeError(f"nn3: CUDA error {code}")
 
-    def tree_ball(self, tree, q, m, r, cap, out):
+    # The tree holds a snapshot of the support, so whether the queries are
+    # the support's own rows is judged against the caller's support tensor x
+    # (er.support_rows): those walk in the tree's leaf order, other query
+    # sets in their own Morton order (same results).
+    def tree_ball(self, tree, q, x, m, r, cap, out):
+        fn = self.lib.query_ball_bvh if er.support_rows(q, x) else self.lib.query_ball_bvh_unordered
         er.check(
-            self.lib.query_ball_bvh(
+            fn(
                 tree.ptr, q.data_ptr(), q.shape[0], m, tree.level(m), r, cap,
                 out.data_ptr(), tree.fallback.data_ptr(), _stream(),
             )
         )
 
-    def tree_query(self, tree, q, m, d, ids):
+    def tree_query(self, tree, q, x, m, d, ids):
+        fn = self.lib.query_bvh if er.support_rows(q, x) else self.lib.query_bvh_unordered
         er.check(
-            self.lib.query_bvh(
+            fn(
                 tree.ptr, q.data_ptr(), q.shape[0], m, tree.level(m), d.data_ptr(),
                 ids.data_ptr(), tree.fallback.data_ptr(), _stream(),
             )
@@ -336,7 +342,7 @@ class QuerySession:
             result = self._ops.rows(nq, q.device)
             tree = self._pick_tree(x, trees, flags[2 * len(memo):])
             owned_x = tree.x[:n]
-            self._ops.tree_ball(tree, q, n, r, cap, result)
+            self._ops.tree_ball(tree, q, x, n, r, cap, result)
         if q.data_ptr() == x.data_ptr() and nq == n:
             # a self-query: the query snapshot would be a second copy of the
             # support snapshot's values, so the entry shares it (snapshots
@@ -374,7 +380,7 @@ class QuerySession:
             else:
                 self.nn_reference(1, nq, n, q[None], x[None], d[None], ids[None])
         else:
-            self._ops.tree_query(self._tree(x), q, n, d, ids)
+            self._ops.tree_query(self._tree(x), q, x, n, d, ids)
 
     def close(self, collect=False):
         if self.closed:

@@ -72,6 +72,22 @@ int pool_reset_peak(void);
 
 /* ---- Extensions without a counterpart in the reference ---------------- */
 
+/* query_bvh / query_ball_bvh for query sets that are not the support's own
+ * points (same arguments, same results).  The query kernels walk queries in
+ * packets of neighbouring points, and query_bvh / query_ball_bvh take the
+ * support's leaf order for them, which fits GSA's prefix queries (a query
+ * array that is the support's first rows) exactly.  These take the queries'
+ * own Morton order instead (one key sort of the nq points, scratch from the
+ * library pool, freed stream-ordered), so shuffled or unrelated query sets
+ * keep coherent packets; their 3NN rows take the per-query walk, the window
+ * bound needing support points.  Same extension of GSA csrc/gsa_bvh.cu:249
+ * and :344. */
+int query_bvh_unordered(void* h, const float* q, int nq, int m, int level,
+                        float* d, int* ix, int* fallback, void* stream);
+int query_ball_bvh_unordered(void* h, const float* q, int nq, int m,
+                             int level, float radius, int ns, int* out,
+                             int* fallback, void* stream);
+
 /* Forest of b independent trees (one per scene) over one concatenated point
  * array: tree i owns x[seg[i]..seg[i+1]) (seg is a HOST array of b+1
  * ascending offsets starting at 0, every tree non-empty).  All trees are

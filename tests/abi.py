@@ -28,6 +28,8 @@ def bvh_lib(name="gsa_bvh"):
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]
     lib.session_lookup.argtypes = [I, P, P, P, I, P, I, I, I, P, P, P, P]
+    lib.query_bvh_unordered.argtypes = [P, P, I, I, I, P, P, P, P]
+    lib.query_ball_bvh_unordered.argtypes = [P, P, I, I, I, F, I, P, P, P]
     lib.fps_order.argtypes = [I, I, P, P, P, P]
     lib.furthest_point_sample.argtypes = [I, I, I, P, P, P, P]
     lib.bvh_info.argtypes = [P] + [ctypes.POINTER(I)] * 4
@@ -56,17 +58,19 @@ class Handle:
         self.h = P()
         self.code = lib.build_bvh(ptr(x), len(x), prefix, leaf, ctypes.byref(self.h), stream())
 
-    def ball(self, q, m, level, r, ns, out=None, fallback=None):
+    def ball(self, q, m, level, r, ns, out=None, fallback=None, unordered=False):
         out = torch.full((len(q), ns), -7, dtype=torch.int32, device="cuda") if out is None else out
         fb = torch.zeros(1, dtype=torch.int32, device="cuda") if fallback is None else fallback
-        code = self.lib.query_ball_bvh(self.h, ptr(q), len(q), m, level, r, ns, ptr(out), ptr(fb), stream())
+        fn = self.lib.query_ball_bvh_unordered if unordered else self.lib.query_ball_bvh
+        code = fn(self.h, ptr(q), len(q), m, level, r, ns, ptr(out), ptr(fb), stream())
         return code, out, fb
 
-    def knn(self, q, m, level, fallback=None):
+    def knn(self, q, m, level, fallback=None, unordered=False):
         d = torch.full((len(q), 3), -1.0, device="cuda")
         ix = torch.full((len(q), 3), -7, dtype=torch.int32, device="cuda")
         fb = torch.zeros(1, dtype=torch.int32, device="cuda") if fallback is None else fallback
-        code = self.lib.query_bvh(self.h, ptr(q), len(q), m, level, ptr(d), ptr(ix), ptr(fb), stream())
+        fn = self.lib.query_bvh_unordered if unordered else self.lib.query_bvh
+        code = fn(self.h, ptr(q), len(q), m, level, ptr(d), ptr(ix), ptr(fb), stream())
         return code, d, ix, fb
 
     def free(self, async_free=1):

@@ -90,11 +90,11 @@ class OracleOps:
         _nn_scan(1, nq, n, q[None], x[None], d[None], ids[None])
 
     @staticmethod
-    def tree_ball(tree, q, m, r, cap, out):
+    def tree_ball(tree, q, x, m, r, cap, out):
         tree.ball(q, m, r, cap, out)
 
     @staticmethod
-    def tree_query(tree, q, m, d, ids):
+    def tree_query(tree, q, x, m, d, ids):
         tree.query(q, m, d, ids)
 
     @staticmethod

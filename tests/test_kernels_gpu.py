@@ -29,8 +29,8 @@ def levels_of(n):
     return [n >> (2 * l) for l in range(4)]
 
 
-def check_ball(h, x, q, m, level, r, ns):
-    code, out, fb = h.ball(cuda(q), m, level, r, ns)
+def check_ball(h, x, q, m, level, r, ns, unordered=False):
+    code, out, fb = h.ball(cuda(q), m, level, r, ns, unordered=unordered)
     assert code == 0
     want = orc.ball_oracle_fast(q, x[:m], r, ns)
     got = out.cpu().numpy()
@@ -38,8 +38,8 @@ def check_ball(h, x, q, m, level, r, ns):
     return fb
 
 
-def check_knn(h, x, q, m, level):
-    code, d, ix, fb = h.knn(cuda(q), m, level)
+def check_knn(h, x, q, m, level, unordered=False):
+    code, d, ix, fb = h.knn(cuda(q), m, level, unordered=unordered)
     assert code == 0
     ed, ei = orc.nn_oracle_fast(q, x[:m])
     assert np.array_equal(d.cpu().numpy(), ed), (len(x), m, level)
@@ -170,6 +170,79 @@ def test_queries_outnumber_support_and_unrelated_queries(lib_name):
     check_ball(h, x, unrelated, 125, 2, 0.2, 16)
     check_knn(h, x, unrelated, 31, 3)
     h.free()
+
+
+@pytest.mark.parametrize("lib_name", LIBS)
+def test_unordered_entries_for_other_query_sets(lib_name):
+    """query_ball_bvh_unordered / query_bvh_unordered (queries walked in
+    their own Morton order): the support's points shuffled, unrelated points,
+    more queries than support points, non-finite queries; rows equal the
+    oracle and the ordered entries.  The default library takes the tree (not
+    the scan) only for large query sets, so it runs a 24,000-point room (and
+    40,000 queries: the multi-launch key sort above 32,768); the tree-only
+    variants run a 6,000-point room."""
+    rng = np.random.default_rng(31)
+    from gsa_b200 import scenes
+
+    big = lib_name == "gsa_bvh"
+    n = 24000 if big else 6000
+    x = scenes.room(2, n=n)[0].astype(np.float32)
+    lib = abi.bvh_lib(lib_name)
+    h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
+    shuffled = x[rng.permutation(n)]
+    unrelated = scenes.room(3, n=n)[0].astype(np.float32)
+    odd = unrelated[: n // 2].copy()
+    odd[::97, 1] = np.nan
+    odd[5::101, 0] = np.inf
+    sets = [shuffled, odd]
+    if big:
+        sets.append(np.concatenate([unrelated, rng.random((16000, 3)).astype(np.float32) * 3.0]))
+    else:
+        sets += [unrelated, np.concatenate([unrelated, shuffled[:2000]])]
+    for q in sets:
+        check_ball(h, x, q, n, 0, 0.1, 32, unordered=True)
+        check_knn(h, x, q, n // 4, 1, unordered=True)
+    if not big:
+        check_ball(h, x, unrelated, n // 4, 1, 0.2, 16, unordered=True)
+        check_knn(h, x, unrelated, n // 16, 2, unordered=True)
+    # the ordered entries give the same rows
+    rows = []
+    for unordered in (False, True):
+        code, out, _ = h.ball(cuda(shuffled), n, 0, 0.1, 32, unordered=unordered)
+        code2, d, ix, _ = h.knn(cuda(shuffled), n // 4, 1, unordered=unordered)
+        assert code == code2 == 0
+        rows.append((out, d, ix))
+    assert all(torch.equal(u, v) for u, v in zip(*rows))
+    h.free()
+
+
+def test_tree_and_session_pick_the_query_order():
+    """Tree.ball / Tree.query and the session walk query arrays that start at
+    the support's first row in the tree's leaf order and other query sets in
+    their own Morton order; both equal the oracle."""
+    from gsa_b200 import QuerySession, Tree, scenes
+
+    x = scenes.room(4, n=24000)[0].astype(np.float32)
+    X = cuda(x)
+    rng = np.random.default_rng(5)
+    q = x[rng.permutation(24000)]
+    Q = cuda(q)
+    t = Tree(X, prefix=True)
+    out = torch.empty(24000, 32, dtype=torch.int32, device="cuda")
+    t.ball(Q, 24000, 0.1, 32, out)
+    assert np.array_equal(out.cpu().numpy(), orc.ball_oracle_fast(q, x, 0.1, 32))
+    d = torch.empty(24000, 3, device="cuda")
+    ix = torch.empty(24000, 3, dtype=torch.int32, device="cuda")
+    t.query(Q, 6000, d, ix)
+    ed, ei = orc.nn_oracle_fast(q, x[:6000])
+    assert np.array_equal(d.cpu().numpy(), ed) and np.array_equal(ix.cpu().numpy(), ei)
+    t.close()
+    with QuerySession(threshold=32) as s:
+        s.ball_into(Q, X, 0.1, 32, out)
+        s.nn_into(Q, X[:6000], d, ix)
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), orc.ball_oracle_fast(q, x, 0.1, 32))
+        assert np.array_equal(d.cpu().numpy(), ed) and np.array_equal(ix.cpu().numpy(), ei)
 
 
 @pytest.mark.parametrize("lib_name", LIBS)
