@@ -21,8 +21,10 @@
 //     loaded once per warp as 16-byte broadcast loads; the radius walk visits
 //     children in ascending minimum-ID order so the reference's "K found and
 //     minid >= K-th ID" early exit applies.  They answer what the frontier
-//     kernels hand back (more than 32 radius hits, no finite 3NN bound,
-//     frontier overflow) and run alone in a test variant;
+//     kernels hand back (more than 32 radius hits when a lane holds
+//     thousands, no finite 3NN bound, frontier overflow) and run alone in a
+//     test variant; radius lanes with 33-256 hits take dense_walk, a
+//     frontier over their box whose leaves are entered in minimum-ID order;
 //   * warp scans of the support in original order, for small prefixes.
 // A walk's stack overflow (impossible for STACK >= 97 on a Karras tree of
 // 64-bit keys) falls back to the exact original-order scan and is counted,
@@ -868,6 +870,194 @@ __device__ __forceinline__ void sort_hits(int* h, int count) {
     if (i < count) h[i] = v[i];
 }
 
+#ifndef GSA_DENSE_WALK
+#define GSA_DENSE_WALK 1
+#endif
+// Largest hit count of a spilled lane up to which dense_walk answers the
+// packet's spilled lanes; above it they take the ordered walk, whose
+// depth-first descent in minimum-ID order finds the first K of thousands of
+// hits (a packet inside a cluster that r covers whole) with less work.
+#ifndef GSA_DENSE_MAX_HITS
+#define GSA_DENSE_MAX_HITS 256
+#endif
+
+// Ascending sort of one key per lane across the warp (bitonic network over
+// lanes); `src` travels with its key.
+__device__ __forceinline__ void warp_sort_keys(int& key, int& src) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int ok = __shfl_xor_sync(kFull, key, j);
+      const int os = __shfl_xor_sync(kFull, src, j);
+      const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+      // the lower lane of an ascending pair keeps the smaller key
+      const bool take = (ok < key || (ok == key && os < src)) == (lower == up);
+      if (take) {
+        key = ok;
+        src = os;
+      }
+    }
+  }
+}
+
+// Dense neighbourhoods: lanes with more than kPacketCap hits inside r (the
+// spilled lanes of a packet) need the first K IDs among all of them.  They
+// walk the tree together as a frontier over the box of their queries (as
+// frontier_walk), pruning every node whose minimum ID reaches the warp's
+// bound, the largest of the lanes' bounds (a lane's bound: its K-th ID once
+// it holds K, else b0, an ID above its first K known from the frontier
+// pass).  Each batch of queued leaves is sorted by minimum ID and entered in
+// that order, every lane inserting the leaf's points inside r with ID below
+// its bound into its ascending first-K list (as walk_ordered), until a
+// leaf's minimum ID reaches the warp's bound.  The ordered walk enters the
+// same subtrees one dependent step at a time; here a step tests up to 32
+// child entries and the bounds fall as soon as the smallest-ID leaves are
+// in.  Returns the lane's count; sets `overflow` (warp-uniform) when the
+// frontier outgrows its stack or the step cap, for walk_ordered to answer.
+template <int FRONT>
+__device__ __forceinline__ int dense_walk(WarpBufs<kPacketCap, FRONT>& W,
+                                       RadiusCtx c, const int* cut, bool act,
+                                       float px, float py, float pz, int b0,
+                                       bool& overflow) {
+  constexpr int CH = kCutMax / 32;
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  const int K = c.K, m = c.m;
+  const float r2 = c.r2;
+  int* L = W.buf[lane];
+  int count = 0, bound = act ? b0 : 0;
+  int wb = (int)__reduce_max_sync(kFull, (unsigned)bound);
+  const Packet pk = make_packet(act, px, py, pz, r2);
+  overflow = false;
+  int top = 0, nleaf = 0;
+  {
+    const int ncut = cut[0];
+    Entry e[CH];
+    int ei[CH];
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      ei[k] = -1;
+      if (k * 32 + lane < ncut) {
+        ei[k] = cut[1 + k * 32 + lane];
+        e[k] = load_entry(ei[k] >= 0 ? c.nodes + ei[k] : c.root);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      bool pass = false, inner = false;
+      if (k * 32 + lane < ncut) {
+        pass = e[k].minid < m && e[k].minid < wb &&
+               box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy, pk.hz, e[k]) <
+                   r2;
+        inner = e[k].ref >= 0;
+      }
+      const unsigned bi = __ballot_sync(kFull, pass && inner);
+      const unsigned bl = __ballot_sync(kFull, pass && !inner);
+      if (top + __popc(bi) > FRONT) {
+        overflow = true;
+        return 0;
+      }
+      if (pass && inner) W.front[top + __popc(bi & lt)] = e[k].ref;
+      if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei[k];
+      top += __popc(bi);
+      nleaf += __popc(bl);
+    }
+  }
+  __syncwarp();
+  long long steps = 0;
+  while (top > 0 || nleaf > 0) {
+    if (++steps > c.max_steps) {
+      overflow = true;
+      return 0;
+    }
+    if (nleaf >= 32 || top == 0) {
+      for (int q0 = 0; q0 < nleaf; q0 += 32) {
+        const int nb = min(32, nleaf - q0);
+        Entry le;
+        le.lox = le.loy = le.loz = 1.f;
+        le.hix = le.hiy = le.hiz = 0.f;  // empty
+        le.minid = INT_MAX;
+        le.ref = -1;
+        int key = INT_MAX, src = lane;
+        if (lane < nb) {
+          const int ei = W.leafq[q0 + lane];
+          le = load_entry(ei >= 0 ? c.nodes + ei : c.root);
+          key = le.minid;
+        }
+        warp_sort_keys(key, src);
+        for (int k = 0; k < nb; ++k) {
+          const int mk = __shfl_sync(kFull, key, k);
+          if (mk >= wb) break;  // warp-uniform; later leaves' IDs are larger
+          const int from = __shfl_sync(kFull, src, k);
+          Entry e;
+          e.lox = __shfl_sync(kFull, le.lox, from);
+          e.loy = __shfl_sync(kFull, le.loy, from);
+          e.loz = __shfl_sync(kFull, le.loz, from);
+          e.hix = __shfl_sync(kFull, le.hix, from);
+          e.hiy = __shfl_sync(kFull, le.hiy, from);
+          e.hiz = __shfl_sync(kFull, le.hiz, from);
+          const int ref = __shfl_sync(kFull, le.ref, from);
+          const bool need = act && mk < bound && nonempty(e) &&
+                            lower_d2(px, py, pz, e) < r2;
+          if (!__any_sync(kFull, need)) continue;
+          int start, cnt;
+          leaf_decode(ref, start, cnt);
+          for (int j = 0; j < cnt; ++j) {
+            const float4 pt = __ldg(c.pts + start + j);
+            const int id = __float_as_int(pt.w);
+            const bool cand = need && id < m && id < bound;
+            // in an ascending leaf no later point can qualify
+            if (c.sorted && !__any_sync(kFull, cand)) break;
+            if (cand && exact_d2(px, py, pz, pt.x, pt.y, pt.z) < r2) {
+              int pos = count < K ? count : K - 1;
+              while (pos > 0 && L[pos - 1] > id) {
+                L[pos] = L[pos - 1];
+                --pos;
+              }
+              L[pos] = id;
+              if (count < K) ++count;
+              if (count == K) bound = L[K - 1];
+            }
+          }
+          wb = (int)__reduce_max_sync(kFull, act ? (unsigned)bound : 0u);
+        }
+      }
+      nleaf = 0;
+      __syncwarp();
+      continue;
+    }
+    // Pop up to 16 internal nodes; lane 2i+j tests child j of node i.
+    const int P = min(top, 16);
+    bool pass = false, inner = false;
+    int ei = 0, ref = 0;
+    if (lane < 2 * P) {
+      ei = 2 * W.front[top - P + (lane >> 1)] + (lane & 1);
+      const Entry e = load_entry(c.nodes + ei);
+      pass = e.minid < m && e.minid < wb &&
+             box_lower_d2(pk.lx, pk.ly, pk.lz, pk.hx, pk.hy, pk.hz, e) < r2;
+      inner = e.ref >= 0;
+      ref = e.ref;
+    }
+    __syncwarp();
+    top -= P;
+    const unsigned bi = __ballot_sync(kFull, pass && inner);
+    const unsigned bl = __ballot_sync(kFull, pass && !inner);
+    const int ni = __popc(bi);
+    if (top + ni > FRONT) {
+      overflow = true;
+      return 0;
+    }
+    if (pass && inner) W.front[top + __popc(bi & lt)] = ref;
+    if (pass && !inner) W.leafq[nleaf + __popc(bl & lt)] = ei;
+    top += ni;
+    nleaf += __popc(bl);
+    __syncwarp();
+  }
+  return count;
+}
+
 template <int STACK>
 __global__ void __launch_bounds__(kFWarps * 32)
     radius_frontier_kernel(QArgs a) {
@@ -906,9 +1096,9 @@ __global__ void __launch_bounds__(kFWarps * 32)
   float bound = c.r2;
   int hc = 0;  // this lane's hit count (may exceed kPacketCap)
   bool overflow = false;
+  const int* cut = a.f.cut + ((size_t)b * a.f.levels + s.lev) * kCutStride;
   if (__any_sync(kFull, live)) {
     Packet pk = make_packet(live, px, py, pz, bound);
-    const int* cut = a.f.cut + ((size_t)b * a.f.levels + s.lev) * kCutStride;
     overflow = frontier_walk<false>(W, c.nodes, c.root, cut, c.pts,
                                     c.max_steps, c.m, pk, live, px, py, pz,
                                     bound, hc);
@@ -942,7 +1132,17 @@ __global__ void __launch_bounds__(kFWarps * 32)
         b0 += 1;
       }
       bool again = false;
-      int c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, W.front, again, b0);
+      int c2 = 0;
+      const bool dense =
+          GSA_DENSE_WALK &&
+          (int)__reduce_max_sync(kFull, spill ? (unsigned)hc : 0u) <=
+              GSA_DENSE_MAX_HITS;
+      if (dense)
+        c2 = dense_walk<2 * STACK>(W, c, cut, spill, px, py, pz, b0, again);
+      if (again || !dense) {
+        again = false;
+        c2 = walk_ordered<STACK>(c, spill, px, py, pz, H, W.front, again, b0);
+      }
       if (spill) count = c2;
       if (again && spill) {
         atomicAdd(a.fallback, 1);
