@@ -158,6 +158,27 @@ def test_duplicates_and_ties(lib_name):
 
 
 @pytest.mark.parametrize("lib_name", LIBS)
+def test_dense_neighbourhoods_first_k(lib_name):
+    """Queries with 33-256 hits (the dense-neighbourhood frontier), with more
+    (the ordered walk) and with fewer in the same packets, K from 1 to 32:
+    a lattice of 40 points repeated ~60 times plus scattered points, radii
+    taking one lattice point's copies, or its axis neighbours too."""
+    rng = np.random.default_rng(17)
+    base = rng.integers(0, 5, size=(40, 3)).astype(np.float32)
+    x = np.concatenate([base[rng.integers(0, 40, size=2400)],
+                        rng.random((600, 3)).astype(np.float32) * 5.0])
+    x = x[rng.permutation(len(x))]
+    lib = abi.bvh_lib(lib_name)
+    h = abi.Handle(lib, cuda(x), prefix=1, leaf=16)
+    q = np.concatenate([x[:1500], base + np.float32(0.25)])
+    for r in (0.5, 1.01):
+        for ns in (1, 5, 16, 32):
+            check_ball(h, x, q, 3000, 0, r, ns)
+        check_ball(h, x, q[:750], 750, 1, r, 32)
+    h.free()
+
+
+@pytest.mark.parametrize("lib_name", LIBS)
 def test_queries_outnumber_support_and_unrelated_queries(lib_name):
     rng = np.random.default_rng(13)
     x = rng.random((2000, 3)).astype(np.float32)
