@@ -1058,6 +1058,64 @@ def other_configs(dev, flush, steps=5):
     }
     f.close()
     torch.cuda.synchronize()
+    res["query_order"] = query_order(dev, flush, steps)
+    return res
+
+
+def query_order(dev, flush, steps=5):
+    """Query sets that are not the support's own rows, through the C ABI on
+    one FPS-ordered 24,000-point room: the room's points shuffled and 24,000
+    unrelated room points (another seed), radius r = 0.1 (K = 32) over all
+    points and 3NN against the 6,000-point prefix, walked in the support's
+    leaf order (`query_ball_bvh` / `query_bvh`) and in the queries' own
+    Morton order (the `_unordered` entries, which sort them first; the sort
+    is inside the timed call); the support's own points for reference.
+    Microseconds per call, median of `steps`, L2 flushed between calls."""
+    import ctypes
+
+    import torch
+
+    from gsa_b200 import runtime as er, scenes
+
+    X = scenes.room_batch([5, 6], n=24000)
+    x, other = X[0].contiguous(), X[1].contiguous()
+    tree = er.Tree(x, prefix=True)
+    lib, fb = er.lib, torch.zeros(1, dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    cases = {
+        "support_points": x,
+        "support_points_shuffled": x[torch.randperm(24000, device=dev, generator=g)].contiguous(),
+        "unrelated_points": other,
+    }
+    out = torch.empty((24000, 32), dtype=torch.int32, device=dev)
+    d = torch.empty((24000, 3), device=dev)
+    ids = torch.empty((24000, 3), dtype=torch.int32, device=dev)
+    st = er._stream()
+
+    def us(fn):
+        return round(1000.0 * statistics.median(timed_steps(fn, steps, flush, torch)), 1)
+
+    res = {"workload": "one 24,000-point room, 24,000 queries: radius r = 0.1 K = 32 over all "
+                       "points, 3NN against the 6,000-point prefix (microseconds per call)"}
+    for name, q in cases.items():
+        qp = q.data_ptr()
+        row = {}
+        for order, (ball, knn) in {
+            "support_order": (lib.query_ball_bvh, lib.query_bvh),
+            "morton_order": (lib.query_ball_bvh_unordered, lib.query_bvh_unordered),
+        }.items():
+            calls = {
+                "radius": lambda: er.check(ball(tree.ptr, qp, 24000, 24000, 0, 0.1, 32, out.data_ptr(),
+                                                fb.data_ptr(), st)),
+                "nn3": lambda: er.check(knn(tree.ptr, qp, 24000, 6000, 1, d.data_ptr(), ids.data_ptr(),
+                                            fb.data_ptr(), st)),
+            }
+            for c in calls.values():
+                c()
+            row[order] = {k: us(c) for k, c in calls.items()}
+        res[name] = row
+    tree.close()
+    torch.cuda.synchronize()
     return res
 
 
