@@ -159,16 +159,16 @@ __device__ __forceinline__ void diff4(const float4 x, const float4 y,
         (ew & (j + 3 < nq));
 }
 
-__global__ void __launch_bounds__(kStageThreads)
-    reuse_stage_kernel(const float* a, long long a_stride, const float* b,
-                       long long b_stride, long long ns, long long nq,
-                       const int* src, long long src_stride, int src_ld,
-                       int rows, int cols, int* dst, long long dst_stride,
-                       int* flags, int* hits) {
+// Scene p of one stage, by a thread-block cluster (the body of both stage
+// kernels below).
+__device__ __forceinline__ void reuse_stage(
+    const float* a, long long a_stride, const float* b, long long b_stride,
+    long long ns, long long nq, const int* src, long long src_stride,
+    int src_ld, int rows, int cols, int* dst, long long dst_stride,
+    int* flags, int* hits, long long p) {
   namespace cg = cooperative_groups;
   __shared__ int bits;  // bit 0: support differs, bit 1: query prefix differs
   cg::cluster_group cluster = cg::this_cluster();
-  const long long p = blockIdx.y;
   const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
   const float* u = a + p * a_stride;
   const float* v = b + p * b_stride;
@@ -234,6 +234,41 @@ __global__ void __launch_bounds__(kStageThreads)
     const long long row = i / cols, col = i - row * cols;
     d[i] = s[row * src_ld + col];
   }
+}
+
+__global__ void __launch_bounds__(kStageThreads)
+    reuse_stage_kernel(const float* a, long long a_stride, const float* b,
+                       long long b_stride, long long ns, long long nq,
+                       const int* src, long long src_stride, int src_ld,
+                       int rows, int cols, int* dst, long long dst_stride,
+                       int* flags, int* hits) {
+  reuse_stage(a, a_stride, b, b_stride, ns, nq, src, src_stride, src_ld, rows,
+              cols, dst, dst_stride, flags, hits, blockIdx.y);
+}
+
+// Every stage of a hierarchy step in one launch: grid.y = stage * count +
+// scene, a cluster per (stage, scene) sized for the largest stage.
+constexpr int kMaxReuseStages = 8;
+struct StageSet {
+  long long ns[kMaxReuseStages], nq[kMaxReuseStages];
+  const int* src[kMaxReuseStages];
+  long long src_stride[kMaxReuseStages], dst_stride[kMaxReuseStages];
+  int rows[kMaxReuseStages];
+  int* dst[kMaxReuseStages];
+  int* flags[kMaxReuseStages];
+  int* hits[kMaxReuseStages];
+  int count;
+};
+
+__global__ void __launch_bounds__(kStageThreads)
+    reuse_stages_kernel(const float* a, long long a_stride, const float* b,
+                        long long b_stride, int src_ld, int cols,
+                        const __grid_constant__ StageSet S) {
+  const int st = blockIdx.y / S.count;
+  const long long p = blockIdx.y - (long long)st * S.count;
+  reuse_stage(a, a_stride, b, b_stride, S.ns[st], S.nq[st], S.src[st],
+              S.src_stride[st], src_ld, S.rows[st], cols, S.dst[st],
+              S.dst_stride[st], S.flags[st], S.hits[st], p);
 }
 
 // Grid-wide form of the same check for batches whose clusters would not
@@ -570,6 +605,81 @@ GSA_API int session_lookup(int count, const float* const* a,
                                   cudaMemcpyDeviceToHost, s);
   if (!e) e = cudaStreamSynchronize(s);
   return (int)e;
+}
+
+GSA_API int reuse_prefix_batch(int count, const float* a, long long a_stride,
+                               const float* b, long long b_stride,
+                               long long ns, long long nq, const int* src,
+                               long long src_stride, int src_ld, int rows,
+                               int cols, int* dst, long long dst_stride,
+                               int* flags, int* hits, void* stream);
+
+// See include/gsa_bvh.h.
+GSA_API int reuse_prefix_stages(int stages, int count, const float* a,
+                                long long a_stride, const float* b,
+                                long long b_stride, const long long* ns,
+                                const long long* nq, const int* const* src,
+                                const long long* src_stride, int src_ld,
+                                const int* rows, int cols, int* const* dst,
+                                const long long* dst_stride,
+                                int* const* flags, int* const* hits,
+                                void* stream) {
+  if (stages < 0 || stages > kMaxReuseStages || count < 0 || cols < 1 ||
+      src_ld < cols || (stages && (!ns || !nq || !src || !src_stride ||
+                                   !rows || !dst || !dst_stride || !flags ||
+                                   !hits)))
+    return -2;
+  if (!stages || !count) return 0;
+  if ((long long)count * stages > 65535 || !a || !b) return -2;
+  long long bytes = 0;
+  for (int i = 0; i < stages; ++i) {
+    if (ns[i] < 0 || nq[i] < 0 || nq[i] > ns[i] || rows[i] < 0 || !flags[i] ||
+        (rows[i] && (!src[i] || !dst[i])))
+      return -2;
+    bytes = std::max<long long>(bytes, 8 * ns[i] + 8ll * rows[i] * cols);
+  }
+  const int cs = (int)std::max<long long>(
+      1, std::min<long long>(kStageClusterMax, (bytes + (64 << 10) - 1) >> 16));
+  if (cs == kStageClusterMax && (long long)count * cs < sms_of_current_device()) {
+    // a few large scenes: each stage takes the grid-wide form
+    for (int i = 0; i < stages; ++i) {
+      const int code = reuse_prefix_batch(
+          count, a, a_stride, b, b_stride, ns[i], nq[i], src[i], src_stride[i],
+          src_ld, rows[i], cols, dst[i], dst_stride[i], flags[i], hits[i],
+          stream);
+      if (code) return code;
+    }
+    return 0;
+  }
+  StageSet S;
+  for (int i = 0; i < kMaxReuseStages; ++i) {
+    const bool on = i < stages;
+    S.ns[i] = on ? ns[i] : 0;
+    S.nq[i] = on ? nq[i] : 0;
+    S.src[i] = on ? src[i] : nullptr;
+    S.src_stride[i] = on ? src_stride[i] : 0;
+    S.rows[i] = on ? rows[i] : 0;
+    S.dst[i] = on ? dst[i] : nullptr;
+    S.dst_stride[i] = on ? dst_stride[i] : 0;
+    S.flags[i] = on ? flags[i] : nullptr;
+    S.hits[i] = on ? hits[i] : nullptr;
+  }
+  S.count = count;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs, count * stages);
+  cfg.blockDim = dim3(kStageThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launches();
+  return cudaLaunchKernelEx(&cfg, reuse_stages_kernel, a, a_stride, b,
+                            b_stride, src_ld, cols, S);
 }
 
 // See include/gsa_bvh.h.

@@ -39,6 +39,8 @@ er.lib.reuse_rows_batch.argtypes = [_I, _P, _LL, _I, _P, _I, _I, _P, _LL, _P, _P
 er.lib.reuse_rows_batch.restype = _I
 er.lib.reuse_prefix_batch.argtypes = [_I, _P, _LL, _P, _LL, _LL, _LL, _P, _LL, _I, _I, _I, _P, _LL, _P, _P, _P]
 er.lib.reuse_prefix_batch.restype = _I
+er.lib.reuse_prefix_stages.argtypes = [_I, _I, _P, _LL, _P, _LL, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P]
+er.lib.reuse_prefix_stages.restype = _I
 
 
 def unit_counts(sizes):
@@ -162,12 +164,13 @@ class Batch:
     def run(self, X, out=None, timer=None, concurrent=True):
         """X: CUDA float32 (B, N, 3), N == sizes[0], each scene FPS-ordered.
 
-        After the forest build, the eight query stages (radius + reuse for
-        s = 0..3, 3NN for s = 0..3) depend only on the build, so with
-        ``concurrent`` they run on eight streams and the small, latency-bound
-        stages overlap the large ones; the caller's stream waits for all of
-        them.  ``timer.span(name)``, if given, brackets each stage on the
-        stream it runs on (build, ball<s>, reuse<s>, nn<s>)."""
+        After the forest build, the eight query stages (radius and 3NN for
+        s = 0..3) depend only on the build, so with ``concurrent`` they run
+        on eight streams and the small, latency-bound stages overlap the
+        large ones; the four stages' reuse checks follow the radius stages
+        in one launch; the caller's stream waits for all of them.
+        ``timer.span(name)``, if given, brackets each stage on the stream it
+        runs on (build, ball<s>, reuse, nn<s>)."""
         self._check_input(X)
         B, N = X.shape[0], X.shape[1]
         out = out if out is not None else self.allocate(B, X.device)
@@ -190,27 +193,37 @@ class Batch:
         return CapturedStep(self, X, out)
 
     def _stages(self, X, out, forest, timer=None, concurrent=True):
-        """Enqueue the eight query stages on ``forest`` (built over X)."""
+        """Enqueue the eight query stages on ``forest`` (built over X) and
+        the reuse checks of the four radius stages (one launch after them)."""
         B, N = X.shape[0], X.shape[1]
         timer = timer or _NoTimer()
         main = torch.cuda.current_stream()
         snap = out["snapshot"]
 
         def radius_stage(s):
-            n_s, n_q = self.sizes[s], self.sizes[s + 1]
-            rows = out[f"ball{s}"]
-            flags, hitflags = out["flags"][s], out["hits"][s]
             with timer.span(f"ball{s}"):
-                forest.ball_prefix(n_s, s, self.radii[s], K, rows)
-            # reuse admission: support P_s and query prefix P_{s+1} equal the
-            # retained snapshot, then gather the first n_q rows of each scene
-            # (one launch: a thread-block cluster per scene)
-            with timer.span(f"reuse{s}"):
+                forest.ball_prefix(self.sizes[s], s, self.radii[s], K, out[f"ball{s}"])
+
+        def reuse_stages():
+            # reuse admission of every stage in one launch (a thread-block
+            # cluster per stage and scene): support P_s and query prefix
+            # P_{s+1} equal the retained snapshot, then the first n_{s+1}
+            # rows of each scene's radius rows are copied
+            st = range(4)
+            ns = (ctypes.c_longlong * 4)(*[self.sizes[s] * 3 for s in st])
+            nq = (ctypes.c_longlong * 4)(*[self.sizes[s + 1] * 3 for s in st])
+            src = (ctypes.c_void_p * 4)(*[out[f"ball{s}"].data_ptr() for s in st])
+            src_stride = (ctypes.c_longlong * 4)(*[self.sizes[s] * K for s in st])
+            rows = (ctypes.c_int * 4)(*[self.sizes[s + 1] for s in st])
+            dst = (ctypes.c_void_p * 4)(*[out[f"hit{s}"].data_ptr() for s in st])
+            dst_stride = (ctypes.c_longlong * 4)(*[self.sizes[s + 1] * K for s in st])
+            flags = (ctypes.c_void_p * 4)(*[out["flags"][s].data_ptr() for s in st])
+            hits = (ctypes.c_void_p * 4)(*[out["hits"][s].data_ptr() for s in st])
+            with timer.span("reuse"):
                 er.check(
-                    er.lib.reuse_prefix_batch(
-                        B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, n_q * 3,
-                        rows.data_ptr(), n_s * K, K, n_q, K, out[f"hit{s}"].data_ptr(), n_q * K,
-                        flags.data_ptr(), hitflags.data_ptr(), er._stream(),
+                    er.lib.reuse_prefix_stages(
+                        4, B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, ns, nq, src,
+                        src_stride, K, rows, K, dst, dst_stride, flags, hits, er._stream(),
                     )
                 )
 
@@ -227,18 +240,29 @@ class Batch:
             built = torch.cuda.Event()
             built.record(main)
             done = []
-            for job, stream in zip(stages, self._side_streams(X.device)):
+            streams = self._side_streams(X.device)
+            for job, stream in zip(stages, streams):
                 stream.wait_event(built)
                 with torch.cuda.stream(stream):
                     job()
                     ev = torch.cuda.Event()
                     ev.record(stream)
                 done.append(ev)
+            # the reuse checks read the four radius stages' rows (jobs 0, 2,
+            # 4, 6); they run on radius stage 0's stream, the longest
+            for ev in done[2::2]:
+                streams[0].wait_event(ev)
+            with torch.cuda.stream(streams[0]):
+                reuse_stages()
+                ev = torch.cuda.Event()
+                ev.record(streams[0])
+            done[0] = ev
             for ev in done:
                 main.wait_event(ev)
         else:
             for job in stages:
                 job()
+            reuse_stages()
 
 
 class CapturedStep:

@@ -190,6 +190,26 @@ int reuse_prefix_batch(int count, const float* a, long long a_stride,
                        long long dst_stride, int* flags, int* hits,
                        void* stream);
 
+/* reuse_prefix_batch for `stages` hierarchy stages of the same scenes in
+ * one launch (a cluster per stage and scene): stage i compares ns[i] floats
+ * of every scene's support (query prefix nq[i]) and copies rows[i] rows of
+ * src[i] (scene stride src_stride[i]) to dst[i] (stride dst_stride[i]),
+ * writing flags[i] (2*count ints) and hits[i] (count ints or null).  The
+ * per-stage arguments are HOST arrays of `stages` (<= 8) entries; a and b
+ * (and their strides), src_ld and cols are shared.  A hierarchy step's four
+ * reuse checks run in one launch after its radius stages instead of four
+ * launches of mostly latency.  No counterpart in the reference (whose
+ * session makes these checks per call, gsa/session.py:104-114).  Returns 0,
+ * -2 (bad argument), or a cudaError_t. */
+int reuse_prefix_stages(int stages, int count, const float* a,
+                        long long a_stride, const float* b,
+                        long long b_stride, const long long* ns,
+                        const long long* nq, const int* const* src,
+                        const long long* src_stride, int src_ld,
+                        const int* rows, int cols, int* const* dst,
+                        const long long* dst_stride, int* const* flags,
+                        int* const* hits, void* stream);
+
 /* Total kernel launches this library has issued since it was loaded. */
 int launch_counter(unsigned long long* total);
 

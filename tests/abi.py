@@ -24,6 +24,7 @@ def bvh_lib(name="gsa_bvh"):
     lib.reuse_rows_batch.argtypes = [I, P, ctypes.c_longlong, I, P, I, I, P, ctypes.c_longlong, P, P]
     LL = ctypes.c_longlong
     lib.reuse_prefix_batch.argtypes = [I, P, LL, P, LL, LL, LL, P, LL, I, I, I, P, LL, P, P, P]
+    lib.reuse_prefix_stages.argtypes = [I, I, P, LL, P, LL, P, P, P, P, I, P, I, P, P, P, P, P]
     lib.coords_mismatch.argtypes = [I, P, P, P, P, P]
     lib.reuse_rows.argtypes = [I, P, P, I, I, I, P, P, P]
     lib.gather_rows.argtypes = [P, I, I, I, P, P]

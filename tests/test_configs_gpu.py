@@ -14,6 +14,8 @@
   recompute correctly.
 """
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -206,6 +208,55 @@ def test_fused_stage_reuse_equals_two_step_path(N, n_q, shift, B):
     assert lib.reuse_prefix_batch(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_q * 3, N * 3,
                                   rows.data_ptr(), N * K, K, n_q, K, got.data_ptr(), n_q * K,
                                   flags.data_ptr(), hits.data_ptr(), st) == (-2 if N > n_q else 0)
+
+
+@pytest.mark.parametrize("N,B", [(24000, 64), (24000, 4), (1001, 5)])
+def test_all_stage_reuse_equals_per_stage_calls(N, B):
+    """reuse_prefix_stages (the four hierarchy stages in one launch) against
+    reuse_prefix_batch per stage: same flags, hits and rows, with scenes whose
+    support differs at some stages only.  Four 24,000-point
+    scenes take the per-stage grid-wide form."""
+    from tests import abi
+
+    lib = abi.bvh_lib()
+    K = 32
+    sizes = [N, N // 4, N // 16, N // 64, max(1, N // 256)]
+    g = torch.Generator(device="cpu").manual_seed(N + B)
+    X = torch.randn(B, N, 3, generator=g).cuda()
+    snap = X.clone()
+    snap[1, sizes[1] + 3, 0] += 1.0    # stage 0 support differs only
+    snap[2, sizes[3], 2] = float("nan")  # supports of stages 0-2 only
+    snap[B - 1, 0, 1] = -snap[B - 1, 0, 1] if snap[B - 1, 0, 1] != 0 else 1.0  # every stage
+    rows = [torch.randint(0, 1 << 20, (B * sizes[s], K), dtype=torch.int32, device="cuda") for s in range(4)]
+    st = abi.stream()
+    want, got = [], []
+    for s in range(4):
+        n_s, n_q = sizes[s], sizes[s + 1]
+        w = {"rows": torch.full((B * n_q, K), -1, dtype=torch.int32, device="cuda"),
+             "flags": torch.full((2 * B,), 7, dtype=torch.int32, device="cuda"),
+             "hits": torch.full((B,), 9, dtype=torch.int32, device="cuda")}
+        assert lib.reuse_prefix_batch(B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3, n_s * 3, n_q * 3,
+                                      rows[s].data_ptr(), n_s * K, K, n_q, K, w["rows"].data_ptr(), n_q * K,
+                                      w["flags"].data_ptr(), w["hits"].data_ptr(), st) == 0
+        want.append(w)
+        got.append({k: torch.full_like(v, -1 if k == "rows" else 5) for k, v in w.items()})
+    LLa, Pa, Ia = ctypes.c_longlong * 4, ctypes.c_void_p * 4, ctypes.c_int * 4
+    for _ in range(2):  # flags and hits are written whole on every call
+        code = lib.reuse_prefix_stages(
+            4, B, X.data_ptr(), N * 3, snap.data_ptr(), N * 3,
+            LLa(*[sizes[s] * 3 for s in range(4)]), LLa(*[sizes[s + 1] * 3 for s in range(4)]),
+            Pa(*[rows[s].data_ptr() for s in range(4)]), LLa(*[sizes[s] * K for s in range(4)]), K,
+            Ia(*[sizes[s + 1] for s in range(4)]), K, Pa(*[got[s]["rows"].data_ptr() for s in range(4)]),
+            LLa(*[sizes[s + 1] * K for s in range(4)]), Pa(*[got[s]["flags"].data_ptr() for s in range(4)]),
+            Pa(*[got[s]["hits"].data_ptr() for s in range(4)]), st)
+        assert code == 0
+        torch.cuda.synchronize()
+        for s in range(4):
+            for k in ("flags", "hits", "rows"):
+                assert torch.equal(got[s][k], want[s][k]), (s, k)
+    assert [h.item() for h in want[0]["hits"][:3]] == [1, 0, 0]
+    assert want[3]["hits"][2].item() == 1 and want[2]["hits"][2].item() == 0
+    assert all(w["hits"][B - 1].item() == 0 for w in want)
 
 
 def test_clustered_exactness_stress():
