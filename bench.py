@@ -663,15 +663,16 @@ def run_ours(args, rank, world, local):
         "knn3_scan_kernel": kernel_line(["nn3"], [3], 36),
     }
     # Reuse check + row copy (reuse_stages_kernel, one launch for the four
-    # stages): per scene and stage the support prefix is read twice (input
-    # and snapshot, 12 B per point each; the query prefix is its first rows,
-    # so one pass answers both checks) and the hit rows are read and written
-    # once (4K B each).
-    reuse_ms = stage.get("reuse", 0.0)
+    # stages of a large batch, else reuse_stage_kernel per stage): per scene
+    # and stage the support prefix is read twice (input and snapshot, 12 B
+    # per point each; the query prefix is its first rows, so one pass
+    # answers both checks) and the hit rows are read and written once (4K B
+    # each).
+    reuse_ms = stage.get("reuse", 0.0) + sum(stage.get(f"reuse{s}", 0.0) for s in range(4))
     reuse_bytes = args.steps * S * sum(24 * SIZES[s] + 8 * K * SIZES[s + 1] for s in range(4))
     reuse_line = {
         "ms_per_step": reuse_ms / args.steps,
-        "launches_per_step": 1,
+        "launches_per_step": 1 if "reuse" in stage else 4,
         "bytes_per_step": reuse_bytes // args.steps,
         "achieved_gbs": reuse_bytes / (reuse_ms / 1000.0) / 1e9 if reuse_ms else 0.0,
     }
